@@ -1,0 +1,866 @@
+// bev_pool forward / backward for sm_100a.
+//
+// Reference semantics: ops/bev_pool/src/bev_pool_triton.py:219-227.
+//   out[b, c, z, x, y] = sum over points n with coords[n] = (x, y, z, b) of feats[n, c]
+// with the cell rank r = ((b * D + z) * H + x) * W + y (`_flatten_ranks`,
+// bev_pool_triton.py:34-39) and out laid out [B, C, D, H, W].
+//
+// Design (one plan, reused by forward and backward):
+//   1. bev_keys_kernel       coords -> 32-bit cell rank per point (+ first radix histogram)
+//   2. stable LSD radix sort  (rank, point index) pairs, so a cell's points stay in
+//                             ascending index order (the order torch.index_add_ sums in)
+//   3. bev_bounds_kernel      [start, end) of every non-empty cell in the sorted order
+//   4. bev_tile_plan_kernel   the grid is cut into tiles of 32 consecutive cells (one
+//                             row segment of the output plane); a tile whose points
+//                             exceed kPiecePoints is cut at cell boundaries into pieces
+//   5. scan + bev_emit_kernel one work descriptor per piece
+//   6. bev_fwd_kernel         one CTA per piece; each non-empty cell is summed by ONE
+//                             warp in ascending point order with fp32 adds (16-byte
+//                             row loads), largest cells first, into a shared
+//                             [cell][channel] tile; then every channel-plane segment
+//                             of the piece is written coalesced, zeros included (no
+//                             memset, no permute).  fp32 results equal index_add_'s
+//                             bit for bit.
+//   7. bev_bwd_kernel         one CTA per piece: stage grad_out[b, :, cells] in shared
+//                             memory (only 32-byte sectors that hold a non-empty
+//                             cell), then a warp per cell keeps the cell's gradient
+//                             row in registers and stores it to each of the cell's
+//                             points with 16-byte stores; dropped points get 0 rows.
+#include "radix.cuh"
+#include "scan.cuh"
+
+namespace bfb {
+namespace {
+
+constexpr int kTileCells = 32;
+constexpr int kPiecePoints = 2048;
+constexpr int kPoolWarps = 4;
+constexpr int kPoolThreads = kPoolWarps * 32;
+constexpr int kUnroll = 8;
+
+struct PlanHeader {
+  uint32_t n_valid;
+  uint32_t total_pieces;
+  uint32_t n_invalid;
+  uint32_t pad[61];
+};
+static_assert(sizeof(PlanHeader) == 256, "header is one aligned block");
+
+struct Geometry {
+  int64_t n, B, D, H, W;
+  int64_t dhw, cells, tpb, tiles, max_pieces;
+};
+
+int make_geometry(int64_t n, int64_t B, int64_t D, int64_t H, int64_t W, Geometry* g) {
+  if (n < 0 || B <= 0 || D <= 0 || H <= 0 || W <= 0) return BFB_ERR_INVALID_ARG;
+  const int64_t lim = 0x7ffffffeLL;
+  if (n > lim) return BFB_ERR_TOO_LARGE;
+  if (D > lim / H || D * H > lim / W) return BFB_ERR_TOO_LARGE;
+  const int64_t dhw = D * H * W;
+  if (B > lim / dhw) return BFB_ERR_TOO_LARGE;
+  g->n = n; g->B = B; g->D = D; g->H = H; g->W = W;
+  g->dhw = dhw;
+  g->cells = B * dhw;
+  g->tpb = ceil_div(dhw, kTileCells);
+  g->tiles = B * g->tpb;
+  g->max_pieces = g->tiles + 2 * ceil_div(n, kPiecePoints) + 1;
+  if (g->max_pieces > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
+  return BFB_OK;
+}
+
+// Kept between forward and backward: the point permutation (points sorted by
+// cell, ascending index within a cell), every cell's [start, end) in it, and
+// the work list.
+struct PlanView {
+  PlanHeader* hdr;
+  uint32_t* perm;
+  int2* cell_se;
+  int4* pieces;
+};
+
+struct ScratchView {
+  uint32_t* keys0;
+  uint32_t* keys1;
+  uint32_t* vtmp;
+  uint32_t* hist;
+  uint32_t* scan;
+  uint32_t* tile_np;
+  uint32_t* tile_mask;
+};
+
+size_t carve_plan(void* base, const Geometry& g, PlanView* v) {
+  Carver c(base);
+  v->hdr = c.take<PlanHeader>(1);
+  v->perm = c.take<uint32_t>((size_t)g.n);
+  v->cell_se = c.take<int2>((size_t)g.cells + 1);
+  v->pieces = c.take<int4>((size_t)g.max_pieces);
+  return c.bytes();
+}
+
+size_t carve_scratch(void* base, const Geometry& g, ScratchView* v) {
+  const RadixPlan rp = make_radix_plan((uint32_t)g.cells);
+  Carver c(base);
+  v->keys0 = c.take<uint32_t>((size_t)g.n);
+  v->keys1 = c.take<uint32_t>((size_t)g.n);
+  v->vtmp = c.take<uint32_t>((size_t)g.n);
+  const size_t hist = radix_hist_elems(g.n, rp);
+  v->hist = c.take<uint32_t>(hist);
+  size_t scan_n = scan_scratch_elems((int64_t)hist);
+  size_t scan_t = scan_scratch_elems(g.tiles + 1);
+  v->scan = c.take<uint32_t>(scan_n > scan_t ? scan_n : scan_t);
+  v->tile_np = c.take<uint32_t>((size_t)g.tiles + 1);
+  v->tile_mask = c.take<uint32_t>((size_t)g.tiles);
+  return c.bytes();
+}
+
+// ---------------------------------------------------------------------------
+// 1. cell ranks
+// ---------------------------------------------------------------------------
+template <class IT>
+__device__ __forceinline__ void load_coord(const IT* coords, int64_t p, int64_t& x, int64_t& y,
+                                           int64_t& z, int64_t& b);
+template <>
+__device__ __forceinline__ void load_coord<int32_t>(const int32_t* coords, int64_t p, int64_t& x,
+                                                    int64_t& y, int64_t& z, int64_t& b) {
+  const int4 c = __ldg(reinterpret_cast<const int4*>(coords) + p);
+  x = c.x; y = c.y; z = c.z; b = c.w;
+}
+template <>
+__device__ __forceinline__ void load_coord<int64_t>(const int64_t* coords, int64_t p, int64_t& x,
+                                                    int64_t& y, int64_t& z, int64_t& b) {
+  const longlong2* q = reinterpret_cast<const longlong2*>(coords) + 2 * p;
+  const longlong2 c0 = __ldg(q), c1 = __ldg(q + 1);
+  x = c0.x; y = c0.y; z = c1.x; b = c1.y;
+}
+
+template <class IT>
+__global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
+    const IT* __restrict__ coords, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
+    uint32_t* __restrict__ keys, int bits0, uint32_t* __restrict__ hist, int64_t ntiles,
+    PlanHeader* hdr) {
+  extern __shared__ uint32_t s_hist[];
+  const int nd = 1 << bits0;
+  for (int i = threadIdx.x; i < nd; i += kRadixThreads) s_hist[i] = 0;
+  __syncthreads();
+  const uint32_t sentinel = (uint32_t)(B * D * H * W);
+  const int64_t base = (int64_t)blockIdx.x * kRadixTile;
+  const int64_t end = min(n, base + kRadixTile);
+  uint32_t bad = 0;
+  for (int64_t p0 = base; p0 < end; p0 += kRadixThreads) {
+    const int64_t p = p0 + threadIdx.x;
+    uint32_t digit = 0u;
+    if (p < end) {
+      int64_t x, y, z, b;
+      load_coord<IT>(coords, p, x, y, z, b);
+      const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W &&
+                      (uint64_t)z < (uint64_t)D && (uint64_t)b < (uint64_t)B;
+      const uint32_t k = ok ? (uint32_t)(((b * D + z) * H + x) * W + y) : sentinel;
+      bad += ok ? 0u : 1u;
+      keys[p] = k;
+      digit = k & ((1u << bits0) - 1u);
+    }
+    radix_count_aggregated(s_hist, digit, bits0, p < end);
+  }
+  // one atomic per warp for the dropped-point counter
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(&hdr->n_invalid, bad);
+  __syncthreads();
+  for (int d = threadIdx.x; d < nd; d += kRadixThreads) hist[(int64_t)d * ntiles + blockIdx.x] = s_hist[d];
+}
+
+// ---------------------------------------------------------------------------
+// 3. per-cell [start, end) in the sorted order; number of in-grid points
+// ---------------------------------------------------------------------------
+__global__ void bev_bounds_kernel(const uint32_t* __restrict__ keys, int64_t n, uint32_t sentinel,
+                                  int2* __restrict__ cell_se, PlanHeader* hdr) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const uint32_t k = keys[p];
+  const bool first = (p == 0) || keys[p - 1] != k;
+  const bool last = (p == n - 1) || keys[p + 1] != k;
+  if (first) cell_se[k].x = (int)p;
+  if (last) cell_se[k].y = (int)(p + 1);
+  if (k != sentinel && last && (p == n - 1 || keys[p + 1] == sentinel)) hdr->n_valid = (uint32_t)(p + 1);
+}
+
+// ---------------------------------------------------------------------------
+// 4. tile -> pieces (greedy, cut at cell boundaries)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int tile_cells(int64_t t, int64_t tpb, int64_t dhw, int64_t* r0, int64_t* s0) {
+  const int64_t b = t / tpb;
+  const int64_t s = (t - b * tpb) * kTileCells;
+  *s0 = s;
+  *r0 = b * dhw + s;
+  const int64_t rem = dhw - s;
+  return rem < kTileCells ? (int)rem : kTileCells;
+}
+
+__global__ void bev_tile_plan_kernel(const int2* __restrict__ cell_se, int64_t tiles, int64_t tpb,
+                                     int64_t dhw, uint32_t* __restrict__ tile_np,
+                                     uint32_t* __restrict__ tile_mask) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= tiles) return;  // warp-uniform
+  int64_t r0, s0;
+  const int nc = tile_cells(t, tpb, dhw, &r0, &s0);
+  int cnt = 0;
+  if (lane < nc) {
+    const int2 se = cell_se[r0 + lane];
+    cnt = se.y - se.x;
+  }
+  uint32_t mask = 1u;
+  int run = __shfl_sync(0xffffffffu, cnt, 0);
+  for (int l = 1; l < nc; ++l) {
+    const int c = __shfl_sync(0xffffffffu, cnt, l);
+    if (run > 0 && run + c > kPiecePoints) {
+      mask |= 1u << l;
+      run = c;
+    } else {
+      run += c;
+    }
+  }
+  if (lane == 0) {
+    tile_np[t] = __popc(mask);
+    tile_mask[t] = mask;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 5. work descriptors: {tile, ca | cb << 8, pa, pb}
+// ---------------------------------------------------------------------------
+__global__ void bev_emit_kernel(const int2* __restrict__ cell_se, int64_t tiles, int64_t tpb,
+                                int64_t dhw, const uint32_t* __restrict__ piece_base,
+                                const uint32_t* __restrict__ tile_mask, int4* __restrict__ pieces) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= tiles) return;
+  int64_t r0, s0;
+  const int nc = tile_cells(t, tpb, dhw, &r0, &s0);
+  int cnt = 0, start = 0x7fffffff;
+  if (lane < nc) {
+    const int2 se = cell_se[r0 + lane];
+    cnt = se.y - se.x;
+    if (cnt > 0) start = se.x;
+  }
+  int tile_pa = start;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tile_pa = min(tile_pa, __shfl_xor_sync(0xffffffffu, tile_pa, o));
+  if (tile_pa == 0x7fffffff) tile_pa = 0;
+  int incl = cnt;  // inclusive prefix of counts over cells
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t mask = tile_mask[t];
+  const bool is_start = lane < nc && ((mask >> lane) & 1u);
+  // piece [ca, cb): cb = next start after ca, or nc
+  const uint32_t later = lane < 31 ? (mask & (0xfffffffeu << lane)) : 0u;
+  const int cb = later ? __ffs(later) - 1 : nc;
+  const int cb_clamped = cb < nc ? cb : nc;
+  const int pref_cb = __shfl_sync(0xffffffffu, incl, (cb_clamped - 1) & 31);
+  const int pref_ca = incl - cnt;  // exclusive prefix at this lane
+  if (is_start) {
+    const uint32_t idx = piece_base[t] + __popc(mask & ((1u << lane) - 1u));
+    pieces[idx] = make_int4((int)t, lane | (cb_clamped << 8), tile_pa + pref_ca, tile_pa + pref_cb);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// vector helpers: VE elements of T per lane, 16-byte loads/stores when VE*sizeof(T) == 16
+// ---------------------------------------------------------------------------
+template <class T, int VE>
+struct VecIO;
+
+template <class T>
+struct VecIO<T, 1> {
+  static __device__ __forceinline__ void load(const T* p, float (&f)[1]) { f[0] = to_f32<T>(__ldg(p)); }
+};
+template <>
+struct VecIO<float, 4> {
+  static __device__ __forceinline__ void load(const float* p, float (&f)[4]) {
+    const uint4 r = ld_stream16(p);
+    f[0] = __uint_as_float(r.x); f[1] = __uint_as_float(r.y);
+    f[2] = __uint_as_float(r.z); f[3] = __uint_as_float(r.w);
+  }
+};
+template <>
+struct VecIO<__half, 8> {
+  static __device__ __forceinline__ void load(const __half* p, float (&f)[8]) {
+    const uint4 r = ld_stream16(p);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    }
+  }
+};
+template <>
+struct VecIO<__nv_bfloat16, 8> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&f)[8]) {
+    const uint4 r = ld_stream16(p);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    }
+  }
+};
+
+// Shared row stride (bytes) for a [cell][channel] tile: a multiple of 16 that is
+// 16 mod 128, so 16-byte accesses of 32 consecutive cells use every bank group.
+__host__ __device__ inline int tile_row_bytes(int chs, int elem) {
+  int s = (chs * elem + 15) / 16 * 16;
+  while (s % 128 != 16) s += 16;
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// Piece prologue (warp 0): cell offsets in the permutation and a split of the
+// piece's cells into kPoolWarps contiguous runs with balanced point counts.
+// s_off[l] = first sorted position of local cell l (l = 0..nc, s_off[nc] = pb);
+// warp w owns local cells [s_wc[w], s_wc[w+1]).  A cell is never split, so
+// each cell is summed by one warp in ascending point order.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_piece(const int2* __restrict__ cell_se, uint32_t r0, int ca, int cb,
+                                            int pa, int* s_off, int* s_wc) {
+  const int lane = threadIdx.x & 31;
+  const int nc = cb - ca;
+  int cnt = 0;
+  if (lane < nc) {
+    const int2 se = cell_se[r0 + ca + lane];
+    cnt = se.y - se.x;
+  }
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int excl = incl - cnt;
+  const int np = __shfl_sync(0xffffffffu, incl, 31);
+  s_off[lane] = pa + excl;
+  if (lane == 31) s_off[32] = pa + np;
+  const int owner = lane < nc ? (np > 0 ? (int)(((int64_t)excl * kPoolWarps) / np) : 0) : kPoolWarps;
+#pragma unroll
+  for (int w = 0; w <= kPoolWarps; ++w) {
+    const unsigned below = __ballot_sync(0xffffffffu, owner < w);
+    if (lane == 0) s_wc[w] = __popc(below);
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Streams the permutation range [wa, wb) of one warp in 32-entry chunks with
+// the next chunk prefetched, so perm loads never sit on the critical path.
+struct PermStream {
+  const uint32_t* perm;
+  int wa, wb, chunk;
+  uint32_t cur, nxt;
+  __device__ __forceinline__ void init(const uint32_t* p, int a, int b, int lane) {
+    perm = p; wa = a; wb = b; chunk = 0;
+    cur = (a + lane < b) ? __ldg(p + a + lane) : 0u;
+    nxt = (a + 32 + lane < b) ? __ldg(p + a + 32 + lane) : 0u;
+  }
+  // point index at sorted position q (warp-uniform, non-decreasing q)
+  __device__ __forceinline__ uint32_t at(int q, int lane) {
+    const int k = q - wa;
+    if ((k >> 5) != chunk) {
+      chunk = k >> 5;
+      cur = nxt;
+      const int r = wa + (chunk + 1) * 32 + lane;
+      nxt = r < wb ? __ldg(perm + r) : 0u;
+    }
+    return __shfl_sync(0xffffffffu, cur, k & 31);
+  }
+};
+
+template <class T, int VE>
+__device__ __forceinline__ void smem_row_load(const unsigned char* p, float (&f)[VE]);
+template <>
+__device__ __forceinline__ void smem_row_load<float, 4>(const unsigned char* p, float (&f)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void smem_row_load<__half, 8>(const unsigned char* p, float (&f)[8]) {
+  const uint4 r = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = t.x; f[2 * i + 1] = t.y;
+  }
+}
+template <>
+__device__ __forceinline__ void smem_row_load<__nv_bfloat16, 8>(const unsigned char* p, float (&f)[8]) {
+  const uint4 r = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    f[2 * i] = t.x; f[2 * i + 1] = t.y;
+  }
+}
+
+// cp.async ring per warp: kStages batches of kBatch rows; kStages - 1 batches
+// are in flight while one is summed.
+constexpr int kBatch = 8;
+constexpr int kStages = 3;
+constexpr int kRing = kBatch * kStages;
+
+// ---------------------------------------------------------------------------
+// 6. forward: one CTA per (piece, channel slice of 32 vectors)
+// ---------------------------------------------------------------------------
+template <class T, int VE>
+__global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
+    const T* __restrict__ feats, int64_t C, int nvec, int64_t dhw, int64_t tpb,
+    const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
+    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_off[33];
+  __shared__ int s_wc[kPoolWarps + 1];
+  const int e = blockIdx.x;
+  if (e >= (int)hdr->total_pieces) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v0 = blockIdx.y * 32;
+  const int nvs = min(32, nvec - v0);                // vectors in this slice
+  const int nvs_full = min(32, nvec);
+  const int chs_full = nvs_full * VE;                 // channel capacity per row
+  const int chs = nvs * VE;                           // channels in this slice
+  const int row_f = tile_row_bytes(chs_full, 4) / 4;  // floats per acc row
+  float* acc_s = reinterpret_cast<float*>(smem);      // [32][row_f]
+  constexpr bool kRingPath = (VE * sizeof(T) == 16);
+  const int slot_b = nvs_full * 16;
+  unsigned char* ring = smem + kTileCells * row_f * 4 + warp * kRing * slot_b;
+
+  const int4 pc = pieces[e];
+  const int64_t t = pc.x;
+  const int ca = pc.y & 0xff, cb = pc.y >> 8;
+  const int64_t b = t / tpb;
+  const int64_t s0 = (t - b * tpb) * kTileCells;
+  const uint32_t r0 = (uint32_t)(b * dhw + s0);
+
+  for (int i = threadIdx.x; i < kTileCells * row_f / 4; i += kPoolThreads)
+    reinterpret_cast<float4*>(acc_s)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp == 0) split_piece(cell_se, r0, ca, cb, pc.z, s_off, s_wc);
+  __syncthreads();
+
+  const bool active = lane < nvs;
+  const T* fbase = feats + (int64_t)(v0 + lane) * VE;
+  int c = s_wc[warp];
+  const int ce = s_wc[warp + 1];
+  const int wa = s_off[c], wb = s_off[ce];
+  if (wa < wb) {
+    PermStream ps;
+    ps.init(perm, wa, wb, lane);
+    while (s_off[c + 1] == wa) ++c;  // first non-empty cell
+    int cend = s_off[c + 1];
+    float acc[VE];
+#pragma unroll
+    for (int q = 0; q < VE; ++q) acc[q] = 0.f;
+    if constexpr (kRingPath) {
+      unsigned char* my = ring + lane * 16;
+      const int nb = (wb - wa + kBatch - 1) / kBatch;
+      // rows [wa + bi * kBatch, +kBatch) of batch bi go to stage bi % kStages
+      auto issue = [&](int bi) {
+        if (bi < nb) {
+          const int q0 = wa + bi * kBatch;
+          unsigned char* dst = my + (bi % kStages) * kBatch * slot_b;
+#pragma unroll
+          for (int j = 0; j < kBatch; ++j) {
+            const uint32_t pid = ps.at(q0 + j, lane);  // uniform; reads past wb return 0
+            if (q0 + j < wb && active) cp_async16(dst + j * slot_b, fbase + (int64_t)pid * C);
+          }
+        }
+        cp_async_commit();
+      };
+#pragma unroll
+      for (int bi = 0; bi < kStages - 1; ++bi) issue(bi);
+      for (int bi = 0; bi < nb; ++bi) {
+        issue(bi + kStages - 1);
+        cp_async_wait<kStages - 1>();
+        const unsigned char* src = my + (bi % kStages) * kBatch * slot_b;
+        const int p0 = wa + bi * kBatch;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int p = p0 + j;
+          if (p < wb) {
+            if (p == cend) {
+              if (active) {
+                float* dst = acc_s + (ca + c) * row_f + lane * VE;
+#pragma unroll
+                for (int q = 0; q < VE; ++q) dst[q] = acc[q];
+              }
+#pragma unroll
+              for (int q = 0; q < VE; ++q) acc[q] = 0.f;
+              do { ++c; } while (s_off[c + 1] == p);
+              cend = s_off[c + 1];
+            }
+            if (active) {
+              float v[VE];
+              smem_row_load<T, VE>(src + j * slot_b, v);
+#pragma unroll
+              for (int q = 0; q < VE; ++q) acc[q] += v[q];
+            }
+          }
+        }
+      }
+    } else {
+      for (int p = wa; p < wb; ++p) {
+        if (p == cend) {
+          if (active) acc_s[(ca + c) * row_f + lane * VE] = acc[0];
+          acc[0] = 0.f;
+          do { ++c; } while (s_off[c + 1] == p);
+          cend = s_off[c + 1];
+        }
+        const uint32_t pid = ps.at(p, lane);
+        if (active) {
+          float v[VE];
+          VecIO<T, VE>::load(fbase + (int64_t)pid * C, v);
+#pragma unroll
+          for (int q = 0; q < VE; ++q) acc[q] += v[q];
+        }
+      }
+    }
+    if (active) {
+      float* dst = acc_s + (ca + c) * row_f + lane * VE;
+#pragma unroll
+      for (int q = 0; q < VE; ++q) dst[q] = acc[q];
+    }
+  }
+  __syncthreads();
+
+  // write channel-plane segments [ca, cb) of this slice, coalesced along cells
+  const int64_t c0 = (int64_t)v0 * VE;
+  T* obase = out + (b * C + c0) * dhw + s0;
+  const int cell = ca + lane;
+  for (int g4 = warp; g4 * 4 < chs; g4 += kPoolWarps) {
+    if (cell < cb) {
+      const float4 q = *reinterpret_cast<const float4*>(acc_s + cell * row_f + g4 * 4);
+      const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = g4 * 4 + i;
+        if (ch < chs) obase[(int64_t)ch * dhw + cell] = from_f32<T>(qv[i]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 7. backward: one CTA per (piece, channel slice); extra CTAs zero dropped rows
+// ---------------------------------------------------------------------------
+template <class T, int VE>
+struct RowIO;
+template <class T>
+struct RowIO<T, 1> {
+  static __device__ __forceinline__ void copy(const T* s, T* d) { d[0] = s[0]; }
+  static __device__ __forceinline__ void zero(T* d) { d[0] = from_f32<T>(0.f); }
+};
+struct RowIO16 {
+  static __device__ __forceinline__ void copy(const void* s, void* d) {
+    st_stream16(d, *reinterpret_cast<const uint4*>(s));
+  }
+  static __device__ __forceinline__ void zero(void* d) { st_stream16(d, make_uint4(0, 0, 0, 0)); }
+};
+template <>
+struct RowIO<float, 4> : RowIO16 {};
+template <>
+struct RowIO<__half, 8> : RowIO16 {};
+template <>
+struct RowIO<__nv_bfloat16, 8> : RowIO16 {};
+
+template <class T, int VE>
+__global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
+    const T* __restrict__ gout, int64_t C, int nvec, int64_t dhw, int64_t tpb, int64_t n,
+    const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
+    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ gfeat) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_off[33];
+  __shared__ int s_wc[kPoolWarps + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v0 = blockIdx.y * 32;
+  const int nvs = min(32, nvec - v0);
+  const bool active = lane < nvs;
+  const int total = (int)hdr->total_pieces;
+  const int e = blockIdx.x;
+  T* gbase = gfeat + (int64_t)(v0 + lane) * VE;
+
+  if (e >= total) {  // rows of points dropped as out of range -> 0
+    const int64_t nvalid = hdr->n_valid;
+    const int64_t start = nvalid + (int64_t)(e - total) * kPiecePoints;
+    const int64_t end = min(n, start + kPiecePoints);
+    for (int64_t p = start + warp; p < end; p += kPoolWarps) {
+      const uint32_t pid = __ldg(perm + p);
+      if (active) RowIO<T, VE>::zero(gbase + (int64_t)pid * C);
+    }
+    return;
+  }
+
+  const int chs_full = min(32, nvec) * VE;
+  const int chs = nvs * VE;
+  const int row_b = tile_row_bytes(chs_full, sizeof(T));
+  const int4 pc = pieces[e];
+  if (pc.z == pc.w) return;  // no points in this piece
+  const int64_t t = pc.x;
+  const int ca = pc.y & 0xff, cb = pc.y >> 8;
+  const int64_t b = t / tpb;
+  const int64_t s0 = (t - b * tpb) * kTileCells;
+  const uint32_t r0 = (uint32_t)(b * dhw + s0);
+
+  if (warp == 0) split_piece(cell_se, r0, ca, cb, pc.z, s_off, s_wc);
+
+  // stage grad_out[b, c0 + ch, s0 + cell] -> smem[cell][ch], 4 channels per
+  // access; skip 8-cell (32-byte) groups without points
+  const int cell = ca + lane;
+  bool need = false;
+  if (cell < cb) {
+    const int2 se = cell_se[r0 + cell];
+    need = se.y > se.x;
+  }
+  const unsigned nz = __ballot_sync(0xffffffffu, need);
+  const bool load = cell < cb && ((nz >> (lane & ~7)) & 0xffu);
+  const int64_t c0 = (int64_t)v0 * VE;
+  const T* gsrc = gout + (b * C + c0) * dhw + s0;
+  for (int g4 = warp; g4 * 4 < chs; g4 += kPoolWarps) {
+    if (load) {
+      T q[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = g4 * 4 + i;
+        q[i] = ch < chs ? __ldg(gsrc + (int64_t)ch * dhw + cell) : from_f32<T>(0.f);
+      }
+      T* dst = reinterpret_cast<T*>(smem + cell * row_b) + g4 * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = q[i];
+    }
+  }
+  __syncthreads();
+
+  int c = s_wc[warp];
+  const int ce = s_wc[warp + 1];
+  const int wa = s_off[c], wb = s_off[ce];
+  if (wa >= wb) return;
+  PermStream ps;
+  ps.init(perm, wa, wb, lane);
+  while (s_off[c + 1] == wa) ++c;
+  int cend = s_off[c + 1];
+  const T* row = reinterpret_cast<const T*>(smem + (ca + c) * row_b) + lane * VE;
+#pragma unroll 4
+  for (int p = wa; p < wb; ++p) {
+    if (p == cend) {
+      do { ++c; } while (s_off[c + 1] == p);
+      cend = s_off[c + 1];
+      row = reinterpret_cast<const T*>(smem + (ca + c) * row_b) + lane * VE;
+    }
+    const uint32_t pid = ps.at(p, lane);
+    if (active) RowIO<T, VE>::copy(row, gbase + (int64_t)pid * C);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <class T, int VE>
+int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out,
+               cudaStream_t st) {
+  const int nvec = (int)(C / VE);
+  const int slices = (nvec + 31) / 32;
+  const int chs_full = (nvec < 32 ? nvec : 32) * VE;
+  size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4);
+  if (VE * sizeof(T) == 16) smem += (size_t)kPoolWarps * kRing * (chs_full / VE) * 16;
+  if (smem > 48 * 1024)
+    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
+  bev_fwd_kernel<T, VE><<<grid, kPoolThreads, smem, st>>>(
+      static_cast<const T*>(feats), C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
+      static_cast<T*>(out));
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+template <class T, int VE>
+int launch_bwd(const void* gout, int64_t C, const Geometry& g, const PlanView& pv, void* gfeat,
+               cudaStream_t st) {
+  const int nvec = (int)(C / VE);
+  const int slices = (nvec + 31) / 32;
+  const int chs_full = (nvec < 32 ? nvec : 32) * VE;
+  const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, sizeof(T));
+  if (smem > 48 * 1024)
+    BFB_CUDA(cudaFuncSetAttribute(bev_bwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((unsigned)(g.max_pieces + ceil_div(g.n, kPiecePoints)), (unsigned)slices);
+  bev_bwd_kernel<T, VE><<<grid, kPoolThreads, smem, st>>>(
+      static_cast<const T*>(gout), C, nvec, g.dhw, g.tpb, g.n, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
+      static_cast<T*>(gfeat));
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+bool vec16_ok(const void* p, int64_t C, int esz) {
+  return (C * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+int run_fwd(int dtype, const void* feats, int64_t C, const Geometry& g, const PlanView& pv,
+            void* out, cudaStream_t st) {
+  switch (dtype) {
+    case BFB_F32:
+      return vec16_ok(feats, C, 4) ? launch_fwd<float, 4>(feats, C, g, pv, out, st)
+                                   : launch_fwd<float, 1>(feats, C, g, pv, out, st);
+    case BFB_F16:
+      return vec16_ok(feats, C, 2) ? launch_fwd<__half, 8>(feats, C, g, pv, out, st)
+                                   : launch_fwd<__half, 1>(feats, C, g, pv, out, st);
+    case BFB_BF16:
+      return vec16_ok(feats, C, 2) ? launch_fwd<__nv_bfloat16, 8>(feats, C, g, pv, out, st)
+                                   : launch_fwd<__nv_bfloat16, 1>(feats, C, g, pv, out, st);
+    default:
+      return BFB_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int run_bwd(int dtype, const void* gout, int64_t C, const Geometry& g, const PlanView& pv,
+            void* gfeat, cudaStream_t st) {
+  switch (dtype) {
+    case BFB_F32:
+      return vec16_ok(gfeat, C, 4) ? launch_bwd<float, 4>(gout, C, g, pv, gfeat, st)
+                                   : launch_bwd<float, 1>(gout, C, g, pv, gfeat, st);
+    case BFB_F16:
+      return vec16_ok(gfeat, C, 2) ? launch_bwd<__half, 8>(gout, C, g, pv, gfeat, st)
+                                   : launch_bwd<__half, 1>(gout, C, g, pv, gfeat, st);
+    case BFB_BF16:
+      return vec16_ok(gfeat, C, 2) ? launch_bwd<__nv_bfloat16, 8>(gout, C, g, pv, gfeat, st)
+                                   : launch_bwd<__nv_bfloat16, 1>(gout, C, g, pv, gfeat, st);
+    default:
+      return BFB_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int check_channels(int64_t c) { return (c <= 0 || c > (1 << 20)) ? BFB_ERR_INVALID_ARG : BFB_OK; }
+
+}  // namespace
+}  // namespace bfb
+
+using namespace bfb;
+
+extern "C" int bfb_bev_pool_workspace_sizes(int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
+                                            int64_t W, size_t* plan_bytes, size_t* scratch_bytes) {
+  (void)c;
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  PlanView pv;
+  ScratchView sv;
+  if (plan_bytes) *plan_bytes = carve_plan(nullptr, g, &pv);
+  if (scratch_bytes) *scratch_bytes = carve_scratch(nullptr, g, &sv);
+  return BFB_OK;
+}
+
+extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64_t B, int64_t D,
+                                 int64_t H, int64_t W, void* plan, size_t plan_bytes, void* scratch,
+                                 size_t scratch_bytes, void* stream) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!plan || !scratch) return BFB_ERR_WORKSPACE;
+  if (n > 0 && !coords) return BFB_ERR_INVALID_ARG;
+  if (n > 0 && (reinterpret_cast<uintptr_t>(coords) & 15)) return BFB_ERR_INVALID_ARG;
+  PlanView pv;
+  ScratchView sv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes || carve_scratch(nullptr, g, &sv) > scratch_bytes)
+    return BFB_ERR_WORKSPACE;
+  carve_plan(plan, g, &pv);
+  carve_scratch(scratch, g, &sv);
+  cudaStream_t st = as_stream(stream);
+  const RadixPlan rp = make_radix_plan((uint32_t)g.cells);
+
+  BFB_CUDA(cudaMemsetAsync(pv.hdr, 0, sizeof(PlanHeader), st));
+  uint32_t* keys_sorted = sv.keys0;
+  if (n > 0) {
+    const int64_t ntiles = radix_tiles(n);
+    const size_t hsm = sizeof(uint32_t) << rp.digit_bits[0];
+    if (itype == BFB_I32)
+      bev_keys_kernel<int32_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
+          static_cast<const int32_t*>(coords), n, B, D, H, W, sv.keys0, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
+    else
+      bev_keys_kernel<int64_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
+          static_cast<const int64_t*>(coords), n, B, D, H, W, sv.keys0, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
+    BFB_CHECK_LAUNCH();
+    BFB_TRY(radix_sort_index(sv.keys0, sv.keys1, sv.vtmp, pv.perm, n, rp, sv.hist, sv.scan,
+                             /*hist0_ready=*/true, st, &keys_sorted));
+  }
+  BFB_CUDA(cudaMemsetAsync(pv.cell_se, 0, sizeof(int2) * (size_t)(g.cells + 1), st));
+  if (n > 0) {
+    bev_bounds_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(keys_sorted, n, (uint32_t)g.cells,
+                                                                  pv.cell_se, pv.hdr);
+    BFB_CHECK_LAUNCH();
+  }
+  const unsigned wblocks = (unsigned)ceil_div(g.tiles * 32, 256);
+  bev_tile_plan_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np, sv.tile_mask);
+  BFB_CHECK_LAUNCH();
+  BFB_TRY(exclusive_scan_u32(sv.tile_np, sv.tile_np, g.tiles, sv.scan, &pv.hdr->total_pieces, st));
+  bev_emit_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np,
+                                           sv.tile_mask, pv.pieces);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+extern "C" int bfb_bev_pool_forward_planned(const void* feats, int dtype, int64_t n, int64_t c,
+                                            int64_t B, int64_t D, int64_t H, int64_t W,
+                                            const void* plan, size_t plan_bytes, void* out,
+                                            void* stream) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  BFB_TRY(check_channels(c));
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!plan) return BFB_ERR_WORKSPACE;
+  if (!out || (n > 0 && !feats)) return BFB_ERR_INVALID_ARG;
+  PlanView pv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
+  carve_plan(const_cast<void*>(plan), g, &pv);
+  return run_fwd(dtype, feats, c, g, pv, out, as_stream(stream));
+}
+
+extern "C" int bfb_bev_pool_forward(const void* feats, int dtype, const void* coords, int itype,
+                                    int64_t n, int64_t c, int64_t B, int64_t D, int64_t H, int64_t W,
+                                    void* out, void* plan, size_t plan_bytes, void* scratch,
+                                    size_t scratch_bytes, void* stream) {
+  BFB_TRY(check_channels(c));
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  BFB_TRY(bfb_bev_pool_plan(coords, itype, n, B, D, H, W, plan, plan_bytes, scratch, scratch_bytes, stream));
+  return bfb_bev_pool_forward_planned(feats, dtype, n, c, B, D, H, W, plan, plan_bytes, out, stream);
+}
+
+extern "C" int bfb_bev_pool_backward(const void* gout, int dtype, int64_t n, int64_t c, int64_t B,
+                                     int64_t D, int64_t H, int64_t W, const void* plan,
+                                     size_t plan_bytes, void* gfeat, void* stream) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  BFB_TRY(check_channels(c));
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!plan) return BFB_ERR_WORKSPACE;
+  if (n == 0) return BFB_OK;
+  if (!gout || !gfeat) return BFB_ERR_INVALID_ARG;
+  PlanView pv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
+  carve_plan(const_cast<void*>(plan), g, &pv);
+  return run_bwd(dtype, gout, c, g, pv, gfeat, as_stream(stream));
+}
+
+extern "C" int bfb_bev_pool_invalid_count(const void* plan, int64_t* count, void* stream) {
+  if (!plan || !count) return BFB_ERR_INVALID_ARG;
+  uint32_t v = 0;
+  cudaStream_t st = as_stream(stream);
+  BFB_CUDA(cudaMemcpyAsync(&v, &static_cast<const PlanHeader*>(plan)->n_invalid, sizeof(v),
+                           cudaMemcpyDeviceToHost, st));
+  BFB_CUDA(cudaStreamSynchronize(st));
+  *count = v;
+  return BFB_OK;
+}

@@ -1,0 +1,170 @@
+/*
+ * bfb_b200.h -- C ABI of the B200 (sm_100a) grid scatter-reduce hot path of
+ * BEVFusion: LSS camera->BEV pooling (bev_pool, forward + backward), LiDAR
+ * hard / dynamic voxelisation and dynamic scatter.
+ *
+ * Conventions
+ *  - Every pointer argument named *_dev is CUDA device memory; nothing here
+ *    allocates device memory.  Callers size workspaces with the *_sizes()
+ *    queries and pass them in.  Outputs are caller-allocated.
+ *  - Every entry point is asynchronous on `stream` (a cudaStream_t passed as
+ *    void*, NULL = legacy default stream) unless documented otherwise, and
+ *    returns a bfb_status (0 = success).  No C++ exception crosses the ABI and
+ *    no kernel traps: device-side problems (out-of-range coordinates, full
+ *    hash tables) are counted into status words that the host reads on
+ *    request.
+ *  - Element types are given as bfb_dtype / bfb_itype codes.
+ *
+ * Each declaration cites the reference interface it replaces, by path within
+ * the ziyangyeh/bevfusion-triton project.
+ */
+#ifndef BFB_B200_H_
+#define BFB_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BFB_ABI_VERSION 1
+
+typedef enum bfb_dtype {
+  BFB_F32 = 0,
+  BFB_F16 = 1,
+  BFB_BF16 = 2,
+} bfb_dtype;
+
+typedef enum bfb_itype {
+  BFB_I32 = 0,
+  BFB_I64 = 1,
+} bfb_itype;
+
+typedef enum bfb_status {
+  BFB_OK = 0,
+  BFB_ERR_INVALID_ARG = -1,       /* bad shape, size, pointer or enum */
+  BFB_ERR_UNSUPPORTED_DTYPE = -2, /* dtype code not accepted by this op */
+  BFB_ERR_WORKSPACE = -3,         /* workspace NULL or smaller than required */
+  BFB_ERR_TOO_LARGE = -4,         /* sizes exceed the 32-bit index space */
+  BFB_ERR_CUDA = -5,              /* a CUDA runtime call or launch failed */
+  BFB_ERR_DEVICE_STATUS = -6,     /* device-side check failed (see op doc) */
+} bfb_status;
+
+/* Library ABI version (BFB_ABI_VERSION of the build). */
+int bfb_abi_version(void);
+/* Static description of a status code. */
+const char* bfb_status_string(int status);
+/* Text of the last CUDA error seen by this thread inside the library. */
+const char* bfb_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------
+ * bev_pool: out[b, c, z, x, y] = sum_{n : coords[n] = (x, y, z, b)} feats[n, c]
+ *
+ * Replaces ops/bev_pool/src/bev_pool_triton.py:219-227 (`bev_pool`), its
+ * autograd pair :153-216, and the legacy extension entry points
+ * ops/bev_pool/csrc/bev_pool_cpu.cpp:89-94 (`bev_pool_forward`,
+ * `bev_pool_backward`).
+ *
+ * feats [n, c] row-major (f32 / f16 / bf16), coords [n, 4] row-major int32
+ * or int64 with columns (x, y, z, b), 0 <= x < H, 0 <= y < W, 0 <= z < D,
+ * 0 <= b < B.  out [B, c, D, H, W] contiguous, same dtype as feats; every
+ * element is written (empty cells get 0), so `out` needs no zero-fill.
+ * Points whose coordinates fall outside the grid are dropped and counted
+ * (bfb_bev_pool_invalid_count); the reference CPU path raises for them.
+ *
+ * Within a cell, values are summed in fp32 in ascending point order
+ * (the order of torch.index_add_ in the reference CPU path), so results are
+ * bitwise deterministic run to run.
+ *
+ * The plan (sorted cell ranks, point permutation and work list) is written by
+ * bfb_bev_pool_plan / bfb_bev_pool_forward into `plan_dev` and reused by
+ * bfb_bev_pool_forward_planned and bfb_bev_pool_backward, so keep it alive
+ * between the forward and the backward.  `scratch_dev` is only used during
+ * the call.
+ * ---------------------------------------------------------------------- */
+int bfb_bev_pool_workspace_sizes(int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
+                                 int64_t W, size_t* plan_bytes, size_t* scratch_bytes);
+
+int bfb_bev_pool_plan(const void* coords_dev, int coords_itype, int64_t n, int64_t B, int64_t D,
+                      int64_t H, int64_t W, void* plan_dev, size_t plan_bytes, void* scratch_dev,
+                      size_t scratch_bytes, void* stream);
+
+int bfb_bev_pool_forward_planned(const void* feats_dev, int feats_dtype, int64_t n, int64_t c,
+                                 int64_t B, int64_t D, int64_t H, int64_t W, const void* plan_dev,
+                                 size_t plan_bytes, void* out_dev, void* stream);
+
+int bfb_bev_pool_forward(const void* feats_dev, int feats_dtype, const void* coords_dev,
+                         int coords_itype, int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
+                         int64_t W, void* out_dev, void* plan_dev, size_t plan_bytes,
+                         void* scratch_dev, size_t scratch_bytes, void* stream);
+
+/* grad_feats[n, :] = grad_out[b, :, z, x, y] for every in-grid point, 0 for
+ * dropped points.  grad_out [B, c, D, H, W] contiguous, same dtype as
+ * grad_feats. */
+int bfb_bev_pool_backward(const void* grad_out_dev, int dtype, int64_t n, int64_t c, int64_t B,
+                          int64_t D, int64_t H, int64_t W, const void* plan_dev,
+                          size_t plan_bytes, void* grad_feats_dev, void* stream);
+
+/* Synchronously reads how many points the plan dropped as out of range. */
+int bfb_bev_pool_invalid_count(const void* plan_dev, int64_t* count, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Voxelisation.
+ *
+ * voxel_size[3] = (vx, vy, vz), coors_range[6] = (xmin, ymin, zmin, xmax,
+ * ymax, zmax); the grid is round((max - min) / size) per axis, computed in
+ * double as the reference does (ops/voxel/src/voxelization_triton.py:23-39).
+ * A point's cell is floor((p - min) / size) in IEEE fp32.
+ * ---------------------------------------------------------------------- */
+
+/* coors[n, 3] int32 = (cx, cy, cz) per point, or (-1, -1, -1) when the point
+ * is outside the grid.  Replaces ops/voxel/voxel_layer.py:33-36 ->
+ * ops/voxel/src/voxelization_triton.py:428-463 (`dynamic_voxelize`) and the
+ * legacy ops/voxel/csrc/voxelization.h:115-130. */
+int bfb_dynamic_voxelize(const void* points_dev, int points_dtype, int64_t n, int64_t f,
+                         const float* voxel_size, const float* coors_range, int32_t* coors_dev,
+                         void* stream);
+
+/* Hard voxelisation, first-occurrence order.  Replaces
+ * ops/voxel/voxel_layer.py:27-30 -> ops/voxel/src/voxelization_triton.py:674-710
+ * (`hard_voxelize`) and the legacy ops/voxel/csrc/voxelization.h:86-113.
+ *
+ * Voxel ids follow the first in-range point of each voxel; at most
+ * max_voxels voxels are created (points of later new voxels are dropped) and
+ * each voxel keeps its first max_points points in input order
+ * (max_points = -1: no per-voxel limit; max_voxels = -1: no voxel limit; the
+ * output buffers must then be sized for n).  Outputs: voxels
+ * [max_voxels, max_points, f] (dtype of points), coors [max_voxels, 3] int32
+ * (x, y, z), num_points [max_voxels] int32, voxel_num [1] int32 (device).
+ * Rows [0, voxel_num) are written in full (unused point slots are 0); rows
+ * [voxel_num, max_voxels) are zero-filled only when zero_tail != 0.
+ * The `deterministic` flag of the reference is accepted by the Python layer
+ * and always served by this deterministic kernel. */
+int bfb_hard_voxelize_workspace_size(int64_t n, int64_t batch, size_t* scratch_bytes);
+
+int bfb_hard_voxelize(const void* points_dev, int points_dtype, int64_t n, int64_t f,
+                      const float* voxel_size, const float* coors_range, int64_t max_points,
+                      int64_t max_voxels, void* voxels_dev, int32_t* coors_dev,
+                      int32_t* num_points_dev, int32_t* voxel_num_dev, int zero_tail,
+                      void* scratch_dev, size_t scratch_bytes, void* stream);
+
+/* Batched hard voxelisation of `batch` independent samples in one set of
+ * launches (no reference counterpart as one call: it replaces the per-sample
+ * loop of models/fusion_models/bevfusion.py:269-296 over
+ * `Voxelization.forward`).  Sample s owns points [offsets[s], offsets[s+1])
+ * (offsets_dev: int64 [batch + 1], device) and the output slices
+ * voxels[s] = [max_voxels, max_points, f], coors[s] = [max_voxels, 3],
+ * num_points[s] = [max_voxels]; voxel_num_dev [batch]. */
+int bfb_hard_voxelize_batch(const void* points_dev, int points_dtype, const int64_t* offsets_dev,
+                            int64_t batch, int64_t n_total, int64_t f, const float* voxel_size,
+                            const float* coors_range, int64_t max_points, int64_t max_voxels,
+                            void* voxels_dev, int32_t* coors_dev, int32_t* num_points_dev,
+                            int32_t* voxel_num_dev, int zero_tail, void* scratch_dev,
+                            size_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BFB_B200_H_ */

@@ -1,0 +1,104 @@
+"""Host-side logic that needs no GPU: the C-ABI library loads and exports
+every declared symbol, argument validation, workspace queries, error types
+of the Python drop-ins (tests/test_ops/test_bev_pool.py:122-131 style)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / 'include').glob('*.h'):
+        names |= set(re.findall(r'^\s*(?:int|const char\*|size_t|void)\s+(bfb_\w+)\s*\(', h.read_text(), re.M))
+    return sorted(names)
+
+
+@pytest.fixture(scope='module')
+def cabi():
+    from bevfusion_triton_b200 import load_native
+    return load_native()
+
+
+def test_header_declares_symbols():
+    assert len(declared_symbols()) >= 10
+
+
+def test_cabi_exports_every_declared_symbol(cabi):
+    missing = [n for n in declared_symbols() if not hasattr(cabi, n)]
+    assert not missing, missing
+
+
+def test_version_and_status_strings(cabi):
+    assert cabi.bfb_abi_version() == 1
+    cabi.bfb_status_string.restype = ctypes.c_char_p
+    assert cabi.bfb_status_string(0) == b'ok'
+    assert cabi.bfb_status_string(-3).startswith(b'workspace')
+    assert cabi.bfb_status_string(12345) == b'unknown status'
+
+
+def _i64(*v):
+    return [ctypes.c_int64(x) for x in v]
+
+
+def test_bev_pool_workspace_query(cabi):
+    plan, scratch = ctypes.c_size_t(), ctypes.c_size_t()
+    rc = cabi.bfb_bev_pool_workspace_sizes(*_i64(1770765, 80, 8, 1, 360, 360), ctypes.byref(plan), ctypes.byref(scratch))
+    assert rc == 0
+    assert plan.value >= 2 * 4 * 1770765 and scratch.value >= 2 * 4 * 1770765
+    # monotone in n
+    plan2 = ctypes.c_size_t()
+    assert cabi.bfb_bev_pool_workspace_sizes(*_i64(10, 80, 8, 1, 360, 360), ctypes.byref(plan2), None) == 0
+    assert plan2.value < plan.value
+
+
+@pytest.mark.parametrize('args,code', [
+    ((10, 80, 0, 1, 2, 2), -1),       # B = 0
+    ((-1, 80, 1, 1, 2, 2), -1),       # negative n
+    ((10, 80, 1 << 20, 1 << 12, 1, 1), -4),  # > 2^31 cells
+])
+def test_bev_pool_bad_sizes(cabi, args, code):
+    a = ctypes.c_size_t()
+    assert cabi.bfb_bev_pool_workspace_sizes(*_i64(*args), ctypes.byref(a), ctypes.byref(a)) == code
+
+
+def test_bev_pool_rejects_missing_workspace(cabi):
+    rc = cabi.bfb_bev_pool_plan(ctypes.c_void_p(16), 1, *_i64(10, 1, 1, 2, 2), None, ctypes.c_size_t(0),
+                                None, ctypes.c_size_t(0), None)
+    assert rc == -3
+
+
+def test_bev_pool_rejects_bad_itype(cabi):
+    rc = cabi.bfb_bev_pool_plan(ctypes.c_void_p(16), 7, *_i64(10, 1, 1, 2, 2), ctypes.c_void_p(16),
+                                ctypes.c_size_t(1 << 30), ctypes.c_void_p(16), ctypes.c_size_t(1 << 30), None)
+    assert rc == -2
+
+
+def test_bev_pool_rejects_invalid_inputs():
+    """Same exception types as the reference (test_bev_pool.py:122-131)."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool
+    feats = torch.randint(0, 4, (4, 3), dtype=torch.int32)
+    coords = torch.zeros((4, 4), dtype=torch.int32)
+    with pytest.raises(TypeError):
+        bev_pool(feats, coords, 1, 1, 1, 1)
+    feats = torch.randn((4, 3), dtype=torch.float32)
+    with pytest.raises(TypeError):
+        bev_pool(feats, torch.zeros((4, 4), dtype=torch.float32), 1, 1, 1, 1)
+    with pytest.raises(ValueError):
+        bev_pool(torch.randn(4), coords, 1, 1, 1, 1)
+    with pytest.raises(ValueError):
+        bev_pool(feats, torch.zeros((4, 3), dtype=torch.int32), 1, 1, 1, 1)
+    with pytest.raises(ValueError):
+        bev_pool(feats, torch.zeros((5, 4), dtype=torch.int32), 1, 1, 1, 1)
+    with pytest.raises(ValueError):
+        bev_pool(feats, coords, 0, 1, 1, 1)
+
+
+def test_bev_pool_has_no_cpu_path():
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool
+    with pytest.raises(RuntimeError, match='CUDA'):
+        bev_pool(torch.randn(4, 3), torch.zeros((4, 4), dtype=torch.int32), 1, 1, 1, 1)

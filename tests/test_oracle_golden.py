@@ -1,0 +1,105 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures made by
+tests/golden/make_golden.py from the reference checkout).  CPU only."""
+import numpy as np
+import pytest
+import torch
+
+from bevfusion_triton_b200 import synth
+from oracle import oracle
+from tests._util import sha
+
+
+def test_bev_known_case(golden):
+    g = golden('bev_known')
+    out, bad = oracle.bev_pool(g['feats'], g['coords'], *g['shape'])
+    assert bad == 0
+    np.testing.assert_array_equal(out, g['out'])
+
+
+@pytest.mark.parametrize('name', ['bev_rand_small_f32', 'bev_rand_medium_i64', 'bev_rand_odd_c'])
+def test_bev_rand_fp32_bit_exact(golden, name):
+    """fp32 sums in ascending point order reproduce index_add_ bit for bit."""
+    g = golden(name)
+    out, bad = oracle.bev_pool(g['feats'], g['coords'], *g['shape'])
+    assert bad == 0
+    np.testing.assert_array_equal(out, g['out'])
+    grad = oracle.bev_pool_backward(g['upstream'], g['coords'], *g['shape'])
+    np.testing.assert_array_equal(grad, g['grad'])
+
+
+def test_bev_rand_fp16_within_tolerance(golden):
+    """The reference CPU path accumulates fp16 in fp16; the oracle in fp32."""
+    g = golden('bev_rand_small_f16')
+    out, _ = oracle.bev_pool(g['feats'], g['coords'], *g['shape'])
+    np.testing.assert_allclose(out, g['out'], rtol=1e-2, atol=1e-2)
+    grad = oracle.bev_pool_backward(g['upstream'], g['coords'], *g['shape'])
+    np.testing.assert_array_equal(grad, g['grad'])
+
+
+def test_det_full_size_digest(digests):
+    d = digests['det_b1_dyadic']
+    case = synth.det_bev_pool_case(1, dyadic=True)
+    assert sha(case.coords) == d['coords_sha'] and sha(case.feats) == d['feats_sha'], 'generator drifted'
+    out, bad = oracle.bev_pool(case.feats.numpy(), case.coords.numpy(), case.B, case.D, case.H, case.W)
+    assert bad == 0
+    assert sha(out) == d['out_sha']
+
+
+def test_dynamic_voxelize_points8(golden):
+    g = golden('voxel_points8')
+    c = oracle.dynamic_voxelize(g['points'], [1, 1, 1], [0, 0, 0, 4, 4, 4])
+    np.testing.assert_array_equal(c, g['dyn_coors'])
+
+
+@pytest.mark.parametrize('mp,mv', [(2, 8), (3, 8), (1, 2)])
+def test_hard_voxelize_points8(golden, mp, mv):
+    g = golden('voxel_points8')
+    v, c, n, vn = oracle.hard_voxelize(g['points'], [1, 1, 1], [0, 0, 0, 4, 4, 4], mp, mv)
+    k = f'mp{mp}_mv{mv}'
+    assert vn == int(g[f'{k}_vn'])
+    np.testing.assert_array_equal(c, g[f'{k}_coors'])
+    np.testing.assert_array_equal(n, g[f'{k}_num'])
+    np.testing.assert_array_equal(v, g[f'{k}_voxels'])
+
+
+def test_dynamic_voxelize_noncubic_edges(golden):
+    g = golden('voxel_rand_noncubic')
+    c = oracle.dynamic_voxelize(g['points'], g['vsize'], g['crange'])
+    np.testing.assert_array_equal(c, g['dyn_coors'])
+
+
+@pytest.mark.parametrize('mp,mv', [(5, 300), (5, 100000), (32, 50)])
+def test_hard_voxelize_noncubic(golden, mp, mv):
+    g = golden('voxel_rand_noncubic')
+    v, c, n, vn = oracle.hard_voxelize(g['points'], g['vsize'], g['crange'], mp, mv)
+    k = f'mp{mp}_mv{mv}'
+    assert vn == int(g[f'{k}_vn'])
+    np.testing.assert_array_equal(c, g[f'{k}_coors'])
+    np.testing.assert_array_equal(n, g[f'{k}_num'])
+    np.testing.assert_array_equal(v, g[f'{k}_voxels'])
+
+
+def test_lidar_full_size_digest(digests):
+    d = digests['lidar_s0']
+    pts = synth.lidar_sweeps(0)
+    assert sha(pts) == d['points_sha'], 'generator drifted'
+    v, c, n, vn = oracle.hard_voxelize(pts.numpy(), synth.LIDAR_VOXEL_SIZE, synth.LIDAR_RANGE,
+                                       synth.LIDAR_MAX_POINTS, synth.LIDAR_MAX_VOXELS)
+    assert vn == d['voxel_num']
+    assert sha(c[:vn]) == d['coors_sha']
+    assert sha(n[:vn]) == d['num_sha']
+    assert sha(v[:vn]) == d['voxels_sha']
+
+
+@pytest.mark.parametrize('case', ['fix', 'rand'])
+@pytest.mark.parametrize('red', ['sum', 'mean', 'max'])
+def test_dynamic_scatter(golden, case, red):
+    g = golden('scatter_cases')
+    f, c = g[f'{case}_feats'], g[f'{case}_coors']
+    vf, vc, mp, cnt = oracle.dynamic_scatter(f, c, red)
+    np.testing.assert_array_equal(vc, g[f'{case}_{red}_vc'])
+    np.testing.assert_array_equal(mp, g[f'{case}_{red}_map'])
+    np.testing.assert_array_equal(cnt, g[f'{case}_{red}_cnt'])
+    np.testing.assert_allclose(vf, g[f'{case}_{red}_vf'], rtol=1e-6, atol=1e-6)
+    grad = oracle.dynamic_scatter_backward(g[f'{case}_{red}_up'], f, vf, mp, cnt, red)
+    np.testing.assert_allclose(grad, g[f'{case}_{red}_grad'], rtol=1e-6, atol=1e-6)
