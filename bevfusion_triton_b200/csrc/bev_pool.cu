@@ -352,14 +352,6 @@ __device__ __forceinline__ void split_piece(const int2* __restrict__ cell_se, ui
   }
 }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 // Streams the permutation range [wa, wb) of one warp in 32-entry chunks with
 // the next chunk prefetched, so perm loads never sit on the critical path.
 struct PermStream {
@@ -384,40 +376,6 @@ struct PermStream {
   }
 };
 
-template <class T, int VE>
-__device__ __forceinline__ void smem_row_load(const unsigned char* p, float (&f)[VE]);
-template <>
-__device__ __forceinline__ void smem_row_load<float, 4>(const unsigned char* p, float (&f)[4]) {
-  const float4 v = *reinterpret_cast<const float4*>(p);
-  f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
-}
-template <>
-__device__ __forceinline__ void smem_row_load<__half, 8>(const unsigned char* p, float (&f)[8]) {
-  const uint4 r = *reinterpret_cast<const uint4*>(p);
-  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-    f[2 * i] = t.x; f[2 * i + 1] = t.y;
-  }
-}
-template <>
-__device__ __forceinline__ void smem_row_load<__nv_bfloat16, 8>(const unsigned char* p, float (&f)[8]) {
-  const uint4 r = *reinterpret_cast<const uint4*>(p);
-  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-    f[2 * i] = t.x; f[2 * i + 1] = t.y;
-  }
-}
-
-// cp.async ring per warp: kStages batches of kBatch rows; kStages - 1 batches
-// are in flight while one is summed.
-constexpr int kBatch = 8;
-constexpr int kStages = 3;
-constexpr int kRing = kBatch * kStages;
-
 // ---------------------------------------------------------------------------
 // 6. forward: one CTA per (piece, channel slice of 32 vectors)
 // ---------------------------------------------------------------------------
@@ -440,8 +398,6 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
   const int row_f = tile_row_bytes(chs_full, 4) / 4;  // floats per acc row
   float* acc_s = reinterpret_cast<float*>(smem);      // [32][row_f]
   constexpr bool kRingPath = (VE * sizeof(T) == 16);
-  const int slot_b = nvs_full * 16;
-  unsigned char* ring = smem + kTileCells * row_f * 4 + warp * kRing * slot_b;
 
   const int4 pc = pieces[e];
   const int64_t t = pc.x;
@@ -469,30 +425,30 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
 #pragma unroll
     for (int q = 0; q < VE; ++q) acc[q] = 0.f;
     if constexpr (kRingPath) {
-      unsigned char* my = ring + lane * 16;
-      const int nb = (wb - wa + kBatch - 1) / kBatch;
-      // rows [wa + bi * kBatch, +kBatch) of batch bi go to stage bi % kStages
-      auto issue = [&](int bi) {
-        if (bi < nb) {
-          const int q0 = wa + bi * kBatch;
-          unsigned char* dst = my + (bi % kStages) * kBatch * slot_b;
+      // register double buffering: batch bi+1's rows are in flight while
+      // batch bi is summed (ascending point order within every cell)
+      constexpr int U = (sizeof(T) == 4) ? 8 : 4;
+      float vb[2][U][VE];
+      auto load = [&](int q0, float (&dst)[U][VE]) {
 #pragma unroll
-          for (int j = 0; j < kBatch; ++j) {
-            const uint32_t pid = ps.at(q0 + j, lane);  // uniform; reads past wb return 0
-            if (q0 + j < wb && active) cp_async16(dst + j * slot_b, fbase + (int64_t)pid * C);
+        for (int j = 0; j < U; ++j) {
+          const uint32_t pid = ps.at(q0 + j, lane);
+          if (q0 + j < wb && active) {
+            VecIO<T, VE>::load(fbase + (int64_t)pid * C, dst[j]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < VE; ++q) dst[j][q] = 0.f;
           }
         }
-        cp_async_commit();
       };
+      load(wa, vb[0]);
+      int cur = 0;
+      for (int p0 = wa; p0 < wb; p0 += U) {
+        if (p0 + U < wb) {
+          if (cur == 0) load(p0 + U, vb[1]); else load(p0 + U, vb[0]);
+        }
 #pragma unroll
-      for (int bi = 0; bi < kStages - 1; ++bi) issue(bi);
-      for (int bi = 0; bi < nb; ++bi) {
-        issue(bi + kStages - 1);
-        cp_async_wait<kStages - 1>();
-        const unsigned char* src = my + (bi % kStages) * kBatch * slot_b;
-        const int p0 = wa + bi * kBatch;
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
+        for (int j = 0; j < U; ++j) {
           const int p = p0 + j;
           if (p < wb) {
             if (p == cend) {
@@ -506,14 +462,11 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
               do { ++c; } while (s_off[c + 1] == p);
               cend = s_off[c + 1];
             }
-            if (active) {
-              float v[VE];
-              smem_row_load<T, VE>(src + j * slot_b, v);
 #pragma unroll
-              for (int q = 0; q < VE; ++q) acc[q] += v[q];
-            }
+            for (int q = 0; q < VE; ++q) acc[q] += (cur == 0 ? vb[0][j][q] : vb[1][j][q]);
           }
         }
+        cur ^= 1;
       }
     } else {
       for (int p = wa; p < wb; ++p) {
@@ -678,7 +631,6 @@ int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& 
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
   size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4);
-  if (VE * sizeof(T) == 16) smem += (size_t)kPoolWarps * kRing * (chs_full / VE) * 16;
   if (smem > 48 * 1024)
     BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);

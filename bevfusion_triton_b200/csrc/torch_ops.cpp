@@ -8,6 +8,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #include "bfb_b200.h"
@@ -118,6 +121,177 @@ int64_t bev_pool_invalid_count(const at::Tensor& plan) {
   return v;
 }
 
+// ------------------------------------------------------------ voxelisation
+std::vector<float> as_floats(const c10::ArrayRef<double>& v, size_t n, const char* what) {
+  TORCH_CHECK_VALUE(v.size() == n, what, " must have length ", n);
+  std::vector<float> out(n);
+  for (size_t i = 0; i < n; ++i) out[i] = (float)v[i];
+  return out;
+}
+
+// One hash table per (device, stream), initialised once and left clean by
+// every successful call; dropped (and re-initialised next time) after a
+// failure.
+struct TableCache {
+  std::mutex mu;
+  std::map<std::pair<int, int64_t>, at::Tensor> tables;
+};
+TableCache& table_cache() {
+  static TableCache c;
+  return c;
+}
+
+at::Tensor table_for(const at::Tensor& like, size_t bytes, void* stream) {
+  auto key = std::make_pair((int)like.device().index(), (int64_t)reinterpret_cast<intptr_t>(stream));
+  auto& c = table_cache();
+  std::lock_guard<std::mutex> g(c.mu);
+  auto it = c.tables.find(key);
+  if (it != c.tables.end() && (size_t)it->second.numel() >= bytes) return it->second;
+  auto t = at::empty({(int64_t)bytes}, like.options().dtype(at::kByte));
+  check(bfb_hard_voxelize_table_init(t.data_ptr(), bytes, stream), "voxel table init");
+  c.tables[key] = t;
+  return t;
+}
+
+void drop_table(const at::Tensor& like, void* stream) {
+  auto& c = table_cache();
+  std::lock_guard<std::mutex> g(c.mu);
+  c.tables.erase(std::make_pair((int)like.device().index(), (int64_t)reinterpret_cast<intptr_t>(stream)));
+}
+
+void require_contig(const at::Tensor& t, const char* name) {
+  TORCH_CHECK_VALUE(t.is_contiguous(), name, " must be contiguous");
+}
+
+void dynamic_voxelize(const at::Tensor& points_in, at::Tensor& coors, c10::ArrayRef<double> voxel_size,
+                      c10::ArrayRef<double> coors_range) {
+  require_cuda(points_in, "points");
+  require_cuda(coors, "coors");
+  c10::cuda::CUDAGuard guard(points_in.device());
+  auto points = points_in.contiguous();
+  TORCH_CHECK_VALUE(points.dim() == 2 && points.size(1) >= 3, "points must have shape [N, >=3]");
+  TORCH_CHECK_TYPE(coors.scalar_type() == at::kInt, "coors must be int32");
+  TORCH_CHECK_VALUE(coors.dim() == 2 && coors.size(0) == points.size(0) && coors.size(1) == 3,
+                    "coors must have shape [N, 3]");
+  auto vs = as_floats(voxel_size, 3, "voxel_size");
+  auto cr = as_floats(coors_range, 6, "coors_range");
+  at::Tensor out = coors.is_contiguous() ? coors : at::empty_like(coors, at::MemoryFormat::Contiguous);
+  check(bfb_dynamic_voxelize(points.data_ptr(), dtype_code(points), points.size(0), points.size(1), vs.data(),
+                             cr.data(), out.data_ptr<int32_t>(), stream_of(points)),
+        "dynamic_voxelize");
+  if (!coors.is_contiguous()) coors.copy_(out);
+}
+
+void hard_voxelize_batch(const at::Tensor& points_in, c10::ArrayRef<int64_t> offsets, at::Tensor& voxels,
+                         at::Tensor& coors, at::Tensor& num_points, at::Tensor& voxel_num,
+                         c10::ArrayRef<double> voxel_size, c10::ArrayRef<double> coors_range, int64_t max_points,
+                         int64_t max_voxels, bool zero_tail) {
+  require_cuda(points_in, "points");
+  c10::cuda::CUDAGuard guard(points_in.device());
+  auto points = points_in.contiguous();
+  TORCH_CHECK_VALUE(points.dim() == 2 && points.size(1) >= 3, "points must have shape [N, >=3]");
+  for (auto* t : {&voxels, &coors, &num_points, &voxel_num}) {
+    require_cuda(*t, "output");
+    require_contig(*t, "outputs");
+  }
+  TORCH_CHECK_TYPE(voxels.scalar_type() == points.scalar_type(), "voxels must have the dtype of points");
+  TORCH_CHECK_TYPE(coors.scalar_type() == at::kInt && num_points.scalar_type() == at::kInt &&
+                       voxel_num.scalar_type() == at::kInt,
+                   "coors, num_points and voxel_num must be int32");
+  const int64_t n = points.size(0), f = points.size(1);
+  const int64_t batch = (int64_t)offsets.size() - 1;
+  TORCH_CHECK_VALUE(batch >= 1, "offsets must hold batch + 1 entries");
+  const int64_t P = max_points < 0 ? n : max_points;
+  const int64_t MV = max_voxels < 0 ? n : max_voxels;
+  TORCH_CHECK_VALUE(voxels.numel() >= batch * MV * P * f && coors.numel() >= batch * MV * 3 &&
+                        num_points.numel() >= batch * MV && voxel_num.numel() >= batch,
+                    "output buffers are too small for max_voxels / max_points");
+  auto vs = as_floats(voxel_size, 3, "voxel_size");
+  auto cr = as_floats(coors_range, 6, "coors_range");
+  size_t table_b = 0, scratch_b = 0;
+  check(bfb_hard_voxelize_workspace_sizes(n, batch, &table_b, &scratch_b), "hard_voxelize workspace query");
+  void* st = stream_of(points);
+  auto table = table_for(points, table_b, st);
+  auto scratch = at::empty({(int64_t)scratch_b}, points.options().dtype(at::kByte));
+  const int rc = bfb_hard_voxelize_batch(points.data_ptr(), dtype_code(points), offsets.data(), batch, n, f,
+                                         vs.data(), cr.data(), max_points, max_voxels, voxels.data_ptr(),
+                                         coors.data_ptr<int32_t>(), num_points.data_ptr<int32_t>(),
+                                         voxel_num.data_ptr<int32_t>(), zero_tail ? 1 : 0, table.data_ptr(),
+                                         (size_t)table.numel(), scratch.data_ptr(), scratch_b, st);
+  if (rc != BFB_OK) drop_table(points, st);
+  check(rc, "hard_voxelize");
+}
+
+int64_t hard_voxelize(const at::Tensor& points, at::Tensor& voxels, at::Tensor& coors, at::Tensor& num_points,
+                      c10::ArrayRef<double> voxel_size, c10::ArrayRef<double> coors_range, int64_t max_points,
+                      int64_t max_voxels, bool zero_tail) {
+  require_cuda(points, "points");
+  c10::cuda::CUDAGuard guard(points.device());
+  auto vn = at::empty({1}, points.options().dtype(at::kInt));
+  const int64_t offs[2] = {0, points.size(0)};
+  hard_voxelize_batch(points, c10::ArrayRef<int64_t>(offs, 2), voxels, coors, num_points, vn, voxel_size,
+                      coors_range, max_points, max_voxels, zero_tail);
+  return vn.item<int32_t>();  // the reference API returns a Python int
+}
+
+// ------------------------------------------------------------ dynamic scatter
+int reduce_code(c10::string_view r) {
+  if (r == "sum" || r == "none") return 0;
+  if (r == "mean") return 1;
+  if (r == "max") return 2;
+  TORCH_CHECK_VALUE(false, "Unsupported reduce_type: ", r);
+  return -1;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> dynamic_scatter_forward(const at::Tensor& feats_in,
+                                                                                   const at::Tensor& coors_in,
+                                                                                   c10::string_view reduce) {
+  require_cuda(feats_in, "feats");
+  require_cuda(coors_in, "coors");
+  c10::cuda::CUDAGuard guard(feats_in.device());
+  auto feats = feats_in.contiguous();
+  auto coors = coors_in.to(at::kInt).contiguous();
+  const int64_t n = feats.size(0), c = feats.size(1), ndim = coors.size(1);
+  const int r = reduce_code(reduce);
+  size_t wb = 0;
+  check(bfb_dynamic_scatter_workspace_size(n, c, ndim, &wb), "dynamic_scatter workspace query");
+  auto ws = at::empty({(int64_t)wb}, feats.options().dtype(at::kByte));
+  auto out = at::empty({n, c}, feats.options());
+  auto oc = at::empty({n, ndim}, coors.options());
+  auto map = at::empty({n}, coors.options());
+  auto cnt = at::empty({n}, coors.options());
+  int64_t m = 0;
+  check(bfb_dynamic_scatter_forward(feats.data_ptr(), dtype_code(feats), coors.data_ptr<int32_t>(), n, c, ndim, r,
+                                    out.data_ptr(), oc.data_ptr<int32_t>(), map.data_ptr<int32_t>(),
+                                    cnt.data_ptr<int32_t>(), &m, ws.data_ptr(), wb, stream_of(feats)),
+        "dynamic_scatter forward");
+  return {out.narrow(0, 0, m), oc.narrow(0, 0, m), map, cnt.narrow(0, 0, m)};
+}
+
+void dynamic_scatter_backward(at::Tensor& grad_feats, const at::Tensor& grad_out_in, const at::Tensor& feats_in,
+                              const at::Tensor& reduced_in, const at::Tensor& map_in, const at::Tensor& counts_in,
+                              c10::string_view reduce) {
+  require_cuda(grad_feats, "grad_feats");
+  c10::cuda::CUDAGuard guard(grad_feats.device());
+  require_contig(grad_feats, "grad_feats");
+  auto gout = grad_out_in.contiguous();
+  auto feats = feats_in.contiguous();
+  auto reduced = reduced_in.to(feats.scalar_type()).contiguous();
+  auto map = map_in.to(at::kInt).contiguous();
+  auto counts = counts_in.to(at::kInt).contiguous();
+  TORCH_CHECK_TYPE(gout.scalar_type() == grad_feats.scalar_type() && feats.scalar_type() == grad_feats.scalar_type(),
+                   "grad_feats, grad_out and feats must share a dtype");
+  const int64_t n = feats.size(0), c = feats.size(1), m = reduced.size(0);
+  const int r = reduce_code(reduce);
+  at::Tensor from;
+  if (r == 2) from = at::empty({std::max<int64_t>(m * c, 1)}, map.options());
+  check(bfb_dynamic_scatter_backward(grad_feats.data_ptr(), gout.data_ptr(), feats.data_ptr(), reduced.data_ptr(),
+                                     map.data_ptr<int32_t>(), counts.data_ptr<int32_t>(), dtype_code(feats), n, m, c, r,
+                                     r == 2 ? from.data_ptr<int32_t>() : nullptr,
+                                     r == 2 ? sizeof(int32_t) * (size_t)from.numel() : 0, stream_of(feats)),
+        "dynamic_scatter backward");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(bfb_b200, m) {
@@ -126,6 +300,18 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward_planned(Tensor feats, Tensor plan, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_backward(Tensor grad_out, Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_invalid_count(Tensor plan) -> int");
+  m.def("dynamic_voxelize(Tensor points, Tensor(a!) coors, float[] voxel_size, float[] coors_range) -> ()");
+  m.def(
+      "hard_voxelize(Tensor points, Tensor(a!) voxels, Tensor(b!) coors, Tensor(c!) num_points, "
+      "float[] voxel_size, float[] coors_range, int max_points, int max_voxels, bool zero_tail) -> int");
+  m.def(
+      "hard_voxelize_batch(Tensor points, int[] offsets, Tensor(a!) voxels, Tensor(b!) coors, "
+      "Tensor(c!) num_points, Tensor(d!) voxel_num, float[] voxel_size, float[] coors_range, int max_points, "
+      "int max_voxels, bool zero_tail) -> ()");
+  m.def("dynamic_scatter_forward(Tensor feats, Tensor coors, str reduce) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def(
+      "dynamic_scatter_backward(Tensor(a!) grad_feats, Tensor grad_out, Tensor feats, Tensor reduced, Tensor map, "
+      "Tensor counts, str reduce) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
@@ -134,4 +320,9 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("bev_pool_forward_planned", &bev_pool_forward_planned);
   m.impl("bev_pool_backward", &bev_pool_backward);
   m.impl("bev_pool_invalid_count", &bev_pool_invalid_count);
+  m.impl("dynamic_voxelize", &dynamic_voxelize);
+  m.impl("hard_voxelize", &hard_voxelize);
+  m.impl("hard_voxelize_batch", &hard_voxelize_batch);
+  m.impl("dynamic_scatter_forward", &dynamic_scatter_forward);
+  m.impl("dynamic_scatter_backward", &dynamic_scatter_backward);
 }

@@ -1,0 +1,535 @@
+// Hard and dynamic voxelisation for sm_100a.
+//
+// Reference semantics (the sequential CPU algorithm is the authority):
+//   ops/voxel/src/voxelization_triton.py:23-39   grid size, argument checks
+//   ops/voxel/src/voxelization_triton.py:328-349 cell = floor((p - min) / size) in fp32,
+//                                                 (-1, -1, -1) when out of range
+//   ops/voxel/src/voxelization_triton.py:466-513 voxel ids in first-occurrence order,
+//                                                 at most max_voxels voxels, each keeps
+//                                                 its first max_points points in input
+//                                                 order, buffers zero-filled
+//
+// Pipeline for a batch of samples (one launch per stage for the whole batch):
+//   vox_insert   cell + 64-bit key (sample, cell) per point; warp-aggregated insert into
+//                an open-addressing table that records the voxel's first point
+//                (atomicMin) and its point count
+//   vox_flags    flag = the point is its voxel's first point; exclusive scan over the
+//                flags numbers voxels in first-occurrence order (per sample by offset)
+//   vox_assign   per first point: keep / drop against max_voxels, write coors and
+//                num_points, record the voxel's table slot and member count
+//   vox_fill     bucket every kept point by voxel (slots from a scan of the counts)
+//   vox_emit     a warp per voxel: order its members ascending (bitonic sort, or
+//                repeated minimum selection for large voxels), write the [P, F] row with
+//                zero padding, and reset the voxel's table slot
+// The table therefore stays clean between calls: it is initialised once
+// (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
+#include <algorithm>
+#include <cmath>
+
+#include "scan.cuh"
+
+namespace bfb {
+namespace {
+
+constexpr uint64_t kEmptyKey = ~0ull;
+constexpr uint32_t kNoFirst = 0xffffffffu;
+constexpr int kLinBits = 40;  // cell index bits inside a key; the rest hold the sample
+constexpr int kVoxThreads = 256;
+constexpr int kEmitBlocks = 148 * 8;
+
+struct TableView {
+  uint64_t* keys;
+  uint32_t* first;
+  uint32_t* cnt;
+  int32_t* gvid;
+  uint64_t cap;  // power of two
+};
+
+size_t carve_table(void* base, uint64_t cap, TableView* t) {
+  Carver c(base);
+  t->keys = c.take<uint64_t>(cap);
+  t->first = c.take<uint32_t>(cap);
+  t->cnt = c.take<uint32_t>(cap);
+  t->gvid = c.take<int32_t>(cap);
+  t->cap = cap;
+  return c.bytes();
+}
+
+uint64_t table_cap_for_bytes(size_t bytes) {
+  uint64_t cap = 1;
+  TableView t;
+  while (carve_table(nullptr, cap * 2, &t) <= bytes) cap *= 2;
+  return carve_table(nullptr, cap, &t) <= bytes ? cap : 0;
+}
+
+uint64_t table_cap_for_points(int64_t n) {
+  uint64_t cap = 1024;
+  while (cap < (uint64_t)(2 * n)) cap *= 2;
+  return cap;
+}
+
+struct VoxScratch {
+  int64_t* offs;     // [batch + 1]
+  int32_t* slot_of;  // [n]   table slot per point, -1 when out of range
+  uint32_t* excl;    // [n+1] first-point flags, then their exclusive scan
+  uint32_t* gcnt;    // [n+1] members per voxel (0 when dropped)
+  uint32_t* cursor;  // [n+1] bucket offsets (scan of gcnt), advanced to bucket ends by vox_fill
+  int32_t* gslot;    // [n]   table slot per voxel
+  int2* vinfo;       // [n]   (sample, voxel id within the sample)
+  uint32_t* members; // [n]
+  uint32_t* scan;
+  uint32_t* err;     // [4]   0: table full (insert gave up)
+};
+
+size_t carve_scratch(void* base, int64_t n, int64_t batch, VoxScratch* v) {
+  Carver c(base);
+  v->offs = c.take<int64_t>((size_t)batch + 1);
+  v->slot_of = c.take<int32_t>((size_t)n);
+  v->excl = c.take<uint32_t>((size_t)n + 1);
+  v->gcnt = c.take<uint32_t>((size_t)n + 1);
+  v->cursor = c.take<uint32_t>((size_t)n + 1);
+  v->gslot = c.take<int32_t>((size_t)n);
+  v->vinfo = c.take<int2>((size_t)n);
+  v->members = c.take<uint32_t>((size_t)n);
+  v->scan = c.take<uint32_t>(scan_scratch_elems(n + 1));
+  v->err = c.take<uint32_t>(4);
+  return c.bytes();
+}
+
+struct Grid {
+  float vs[3];
+  float mn[3];
+  int64_t g[3];
+};
+
+int make_grid(const float* vsize, const float* range, Grid* gr) {
+  if (!vsize || !range) return BFB_ERR_INVALID_ARG;
+  for (int i = 0; i < 3; ++i) {
+    gr->vs[i] = vsize[i];
+    gr->mn[i] = range[i];
+    const double v = ((double)range[3 + i] - (double)range[i]) / (double)vsize[i];
+    if (!(v == v) || v > 1e15 || v < -1e15) return BFB_ERR_INVALID_ARG;
+    gr->g[i] = (int64_t)std::nearbyint(v);  // Python round(): half to even
+  }
+  return BFB_OK;
+}
+
+// floor((p - min) / size) in IEEE fp32 (no contraction); false when outside.
+__device__ __forceinline__ bool cell_of(const float p[3], const Grid& gr, int32_t c[3]) {
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float f = floorf(__fdiv_rn(__fsub_rn(p[j], gr.mn[j]), gr.vs[j]));
+    if (!(f >= 0.f) || !(f < (float)gr.g[j])) return false;
+    c[j] = (int32_t)f;
+  }
+  return true;
+}
+
+template <class T>
+__device__ __forceinline__ void load_xyz(const T* pts, int64_t p, int64_t f, float out[3]) {
+  const T* r = pts + p * f;
+  out[0] = to_f32<T>(r[0]);
+  out[1] = to_f32<T>(r[1]);
+  out[2] = to_f32<T>(r[2]);
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t k) {
+  k ^= k >> 33; k *= 0xff51afd7ed558ccdull; k ^= k >> 33; k *= 0xc4ceb9fe1a85ec53ull; k ^= k >> 33;
+  return k;
+}
+
+// Sample of point p: offs is ascending with offs[0] = 0, offs[batch] = n.
+__device__ __forceinline__ int sample_of(const int64_t* offs, int batch, int64_t p) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(offs + mid) <= p) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------------------
+// dynamic voxelisation
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void dyn_voxelize_kernel(const T* __restrict__ pts, int64_t n, int64_t f, Grid gr,
+                                    int32_t* __restrict__ coors) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  float xyz[3];
+  load_xyz<T>(pts, p, f, xyz);
+  int32_t c[3];
+  if (!cell_of(xyz, gr, c)) c[0] = c[1] = c[2] = -1;
+  coors[3 * p + 0] = c[0];
+  coors[3 * p + 1] = c[1];
+  coors[3 * p + 2] = c[2];
+}
+
+// ---------------------------------------------------------------------------
+// hard voxelisation stages
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __restrict__ pts, int64_t n, int64_t f,
+                                                                 Grid gr, const int64_t* __restrict__ offs, int batch,
+                                                                 TableView tb, int32_t* __restrict__ slot_of,
+                                                                 uint32_t* err) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  bool valid = false;
+  uint64_t key = kEmptyKey;
+  if (p < n) {
+    float xyz[3];
+    load_xyz<T>(pts, p, f, xyz);
+    int32_t c[3];
+    if (cell_of(xyz, gr, c)) {
+      valid = true;
+      const uint64_t lin = ((uint64_t)c[0] * (uint64_t)gr.g[1] + (uint64_t)c[1]) * (uint64_t)gr.g[2] + (uint64_t)c[2];
+      const uint64_t s = batch > 1 ? (uint64_t)sample_of(offs, batch, p) : 0ull;
+      key = (s << kLinBits) | lin;
+    }
+  }
+  // lanes holding the same voxel insert once; the lowest lane holds the first point
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  const int leader = __ffs(peers) - 1;
+  int64_t slot = -1;
+  if (valid && lane == leader) {
+    const uint64_t mask = tb.cap - 1;
+    uint64_t h = mix64(key) & mask;
+    for (uint64_t probe = 0; probe < tb.cap; ++probe) {
+      uint64_t k = tb.keys[h];
+      if (k == kEmptyKey) k = atomicCAS(reinterpret_cast<unsigned long long*>(tb.keys + h), kEmptyKey, key);
+      if (k == kEmptyKey || k == key) {
+        slot = (int64_t)h;
+        break;
+      }
+      h = (h + 1) & mask;
+    }
+    if (slot >= 0) {
+      atomicMin(tb.first + slot, (uint32_t)p);
+      atomicAdd(tb.cnt + slot, (uint32_t)__popc(peers));
+    } else {
+      atomicAdd(err, 1u);  // table full: cannot happen when cap >= n
+    }
+  }
+  slot = __shfl_sync(0xffffffffu, slot, leader);
+  if (p < n) slot_of[p] = valid ? (int32_t)slot : -1;
+}
+
+__global__ void vox_flags_kernel(const int32_t* __restrict__ slot_of, int64_t n, const uint32_t* __restrict__ first,
+                                 uint32_t* __restrict__ flags) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const int32_t s = slot_of[p];
+  flags[p] = (s >= 0 && first[s] == (uint32_t)p) ? 1u : 0u;
+}
+
+template <class T>
+__global__ void vox_assign_kernel(const T* __restrict__ pts, int64_t n, int64_t f, Grid gr,
+                                  const int64_t* __restrict__ offs, int batch, TableView tb,
+                                  const int32_t* __restrict__ slot_of, const uint32_t* __restrict__ excl,
+                                  int64_t max_points, int64_t max_voxels, int32_t* __restrict__ coors,
+                                  int32_t* __restrict__ num_points, uint32_t* __restrict__ gcnt,
+                                  int32_t* __restrict__ gslot, int2* __restrict__ vinfo) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const int32_t slot = slot_of[p];
+  if (slot < 0 || tb.first[slot] != (uint32_t)p) return;
+  const uint32_t g = excl[p];
+  const int s = batch > 1 ? sample_of(offs, batch, p) : 0;
+  const int64_t local = (int64_t)g - (int64_t)excl[offs[s]];
+  const uint32_t c = tb.cnt[slot];
+  const bool kept = max_voxels < 0 || local < max_voxels;
+  gslot[g] = slot;
+  gcnt[g] = kept ? c : 0u;
+  vinfo[g] = make_int2(s, (int)local);
+  tb.gvid[slot] = kept ? (int32_t)g : -1;
+  if (kept) {
+    float xyz[3];
+    load_xyz<T>(pts, p, f, xyz);
+    int32_t cc[3];
+    cell_of(xyz, gr, cc);
+    const int64_t row = (int64_t)s * max_voxels + local;
+    coors[3 * row + 0] = cc[0];
+    coors[3 * row + 1] = cc[1];
+    coors[3 * row + 2] = cc[2];
+    num_points[row] = (int32_t)(max_points < 0 ? c : min((int64_t)c, max_points));
+  }
+}
+
+__global__ void vox_count_kernel(const int64_t* __restrict__ offs, int batch, const uint32_t* __restrict__ excl,
+                                 int64_t max_voxels, int32_t* __restrict__ voxel_num) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= batch) return;
+  const int64_t tot = (int64_t)excl[offs[s + 1]] - (int64_t)excl[offs[s]];
+  voxel_num[s] = (int32_t)(max_voxels < 0 ? tot : min(tot, max_voxels));
+}
+
+__global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __restrict__ slot_of, int64_t n,
+                                                               const int32_t* __restrict__ gvid,
+                                                               uint32_t* __restrict__ cursor,
+                                                               uint32_t* __restrict__ members) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  int32_t g = -1;
+  if (p < n) {
+    const int32_t s = slot_of[p];
+    if (s >= 0) g = gvid[s];
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, g);
+  const int leader = __ffs(peers) - 1;
+  uint32_t base = 0;
+  if (g >= 0 && lane == leader) base = atomicAdd(cursor + g, (uint32_t)__popc(peers));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (g >= 0) members[base + __popc(peers & lanemask_lt())] = (uint32_t)p;
+}
+
+// Ascending bitonic sort of one value per lane.
+__device__ __forceinline__ uint32_t warp_sort_asc(uint32_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j);
+      const bool up = ((lane & k) == 0);
+      const bool lower = (lane & j) == 0;
+      v = (lower == up) ? min(v, o) : max(v, o);
+    }
+  }
+  return v;
+}
+
+template <class T>
+__global__ __launch_bounds__(kVoxThreads) void vox_emit_kernel(
+    const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, TableView tb,
+    const uint32_t* __restrict__ gcnt, const uint32_t* __restrict__ cursor, const int32_t* __restrict__ gslot,
+    const int2* __restrict__ vinfo, const uint32_t* __restrict__ members, int64_t P, int64_t max_voxels,
+    T* __restrict__ voxels) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = *total_dev;
+  const int64_t row_len = P * f;
+  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < total; g += warps) {
+    const int32_t slot = gslot[g];
+    const uint32_t cnt = gcnt[g];
+    if (lane == 0) {  // leave the table clean for the next call
+      tb.keys[slot] = kEmptyKey;
+      tb.first[slot] = kNoFirst;
+      tb.cnt[slot] = 0u;
+    }
+    if (cnt == 0) continue;  // voxel beyond max_voxels
+    const int2 vi = vinfo[g];
+    const uint32_t end = cursor[g];
+    const uint32_t start = end - cnt;
+    T* dst = voxels + ((int64_t)vi.x * max_voxels + vi.y) * row_len;
+    const int64_t keep = min((int64_t)cnt, P);
+    if (cnt <= 32) {
+      uint32_t m = lane < (int)cnt ? members[start + lane] : 0xffffffffu;
+      m = warp_sort_asc(m);
+      for (int64_t base = 0; base < row_len; base += 32) {  // warp-uniform trip count
+        const int64_t idx = base + lane;
+        const int64_t j = idx / f, q = idx - j * f;
+        const uint32_t src = __shfl_sync(0xffffffffu, m, (int)(j & 31));
+        if (idx < row_len) dst[idx] = j < keep ? pts[(int64_t)src * f + q] : from_f32<T>(0.f);
+      }
+    } else {
+      // repeated minimum selection: O(keep * cnt / 32), exact input order
+      uint32_t last = 0;
+      for (int64_t j = 0; j < keep; ++j) {
+        uint32_t best = 0xffffffffu;
+        for (uint32_t i = start + lane; i < end; i += 32) {
+          const uint32_t v = members[i];
+          if ((j == 0 || v > last) && v < best) best = v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+        last = best;
+        for (int64_t q = lane; q < f; q += 32) dst[j * f + q] = pts[(int64_t)best * f + q];
+      }
+      for (int64_t idx = keep * f + lane; idx < row_len; idx += 32) dst[idx] = from_f32<T>(0.f);
+    }
+  }
+}
+
+// rows [voxel_num[s], max_voxels) of every sample -> 0
+template <class T>
+__global__ void vox_zero_tail_kernel(const int32_t* __restrict__ voxel_num, int64_t max_voxels, int64_t row_len,
+                                     T* __restrict__ voxels, int32_t* __restrict__ coors,
+                                     int32_t* __restrict__ num_points) {
+  const int s = blockIdx.y;
+  const int64_t vn = voxel_num[s];
+  const int64_t start = vn * row_len;
+  const int64_t total = max_voxels * row_len;
+  T* vb = voxels + (int64_t)s * total;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = start + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride)
+    vb[i] = from_f32<T>(0.f);
+  for (int64_t r = vn + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < max_voxels; r += stride) {
+    const int64_t row = (int64_t)s * max_voxels + r;
+    coors[3 * row + 0] = 0;
+    coors[3 * row + 1] = 0;
+    coors[3 * row + 2] = 0;
+    num_points[row] = 0;
+  }
+}
+
+template <class T>
+int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr, const int64_t* offs_host,
+                       int64_t batch, int64_t max_points, int64_t max_voxels, void* voxels, int32_t* coors,
+                       int32_t* num_points, int32_t* voxel_num, int zero_tail, const TableView& tb,
+                       const VoxScratch& sv, cudaStream_t st) {
+  const T* pts = static_cast<const T*>(points);
+  const int64_t P = max_points < 0 ? n : max_points;
+  const int64_t MV = max_voxels < 0 ? n : max_voxels;
+  BFB_CUDA(cudaMemcpyAsync(sv.offs, offs_host, sizeof(int64_t) * (size_t)(batch + 1), cudaMemcpyHostToDevice, st));
+  BFB_CUDA(cudaMemsetAsync(sv.err, 0, 4 * sizeof(uint32_t), st));
+  const unsigned nb = (unsigned)ceil_div(n > 0 ? n : 1, kVoxThreads);
+  if (n > 0) {
+    vox_insert_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, n, f, gr, sv.offs, (int)batch, tb, sv.slot_of, sv.err);
+    BFB_CHECK_LAUNCH();
+    vox_flags_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.first, sv.excl);
+    BFB_CHECK_LAUNCH();
+  }
+  // excl[n] = number of distinct voxels over the batch
+  BFB_TRY(exclusive_scan_u32(sv.excl, sv.excl, n, sv.scan, sv.excl + n, st));
+  if (n > 0) {
+    vox_assign_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, n, f, gr, sv.offs, (int)batch, tb, sv.slot_of, sv.excl,
+                                                     max_points, MV, coors, num_points, sv.gcnt, sv.gslot,
+                                                     sv.vinfo);
+    BFB_CHECK_LAUNCH();
+  }
+  vox_count_kernel<<<(unsigned)ceil_div(batch, 128), 128, 0, st>>>(sv.offs, (int)batch, sv.excl, max_voxels,
+                                                                    voxel_num);
+  BFB_CHECK_LAUNCH();
+  if (n > 0) {
+    // bucket offsets over voxel ids; entries past the voxel count are never read
+    BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n, sv.scan, nullptr, st));
+    vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members);
+    BFB_CHECK_LAUNCH();
+    vox_emit_kernel<T><<<kEmitBlocks, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot,
+                                                            sv.vinfo, sv.members, P, MV, static_cast<T*>(voxels));
+    BFB_CHECK_LAUNCH();
+  }
+  if (zero_tail) {
+    dim3 grid((unsigned)std::min<int64_t>(ceil_div(MV * P * f, 256), 4096), (unsigned)batch);
+    vox_zero_tail_kernel<T><<<grid, 256, 0, st>>>(voxel_num, MV, P * f, static_cast<T*>(voxels), coors, num_points);
+    BFB_CHECK_LAUNCH();
+  }
+  return BFB_OK;
+}
+
+int check_common(const void* points, int dtype, int64_t n, int64_t f) {
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (n < 0 || f < 3) return BFB_ERR_INVALID_ARG;
+  if (n > 0x7ffffffeLL) return BFB_ERR_TOO_LARGE;
+  if (n > 0 && !points) return BFB_ERR_INVALID_ARG;
+  return BFB_OK;
+}
+
+}  // namespace
+}  // namespace bfb
+
+using namespace bfb;
+
+extern "C" int bfb_dynamic_voxelize(const void* points, int dtype, int64_t n, int64_t f, const float* voxel_size,
+                                    const float* coors_range, int32_t* coors, void* stream) {
+  BFB_TRY(check_common(points, dtype, n, f));
+  Grid gr;
+  BFB_TRY(make_grid(voxel_size, coors_range, &gr));
+  if (n == 0) return BFB_OK;
+  if (!coors) return BFB_ERR_INVALID_ARG;
+  cudaStream_t st = as_stream(stream);
+  const unsigned nb = (unsigned)ceil_div(n, 256);
+  switch (dtype) {
+    case BFB_F32: dyn_voxelize_kernel<float><<<nb, 256, 0, st>>>(static_cast<const float*>(points), n, f, gr, coors); break;
+    case BFB_F16: dyn_voxelize_kernel<__half><<<nb, 256, 0, st>>>(static_cast<const __half*>(points), n, f, gr, coors); break;
+    default: dyn_voxelize_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(points), n, f, gr, coors); break;
+  }
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+extern "C" int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, size_t* table_bytes, size_t* scratch_bytes) {
+  if (n < 0 || batch < 1) return BFB_ERR_INVALID_ARG;
+  if (n > 0x7ffffffeLL || batch >= (1LL << (64 - kLinBits))) return BFB_ERR_TOO_LARGE;
+  TableView tv;
+  VoxScratch sv;
+  if (table_bytes) *table_bytes = carve_table(nullptr, table_cap_for_points(n), &tv);
+  if (scratch_bytes) *scratch_bytes = carve_scratch(nullptr, n, batch, &sv);
+  return BFB_OK;
+}
+
+extern "C" int bfb_hard_voxelize_table_init(void* table, size_t table_bytes, void* stream) {
+  const uint64_t cap = table_cap_for_bytes(table_bytes);
+  if (!table || cap == 0) return BFB_ERR_WORKSPACE;
+  TableView tv;
+  carve_table(table, cap, &tv);
+  cudaStream_t st = as_stream(stream);
+  BFB_CUDA(cudaMemsetAsync(tv.keys, 0xff, sizeof(uint64_t) * cap, st));
+  BFB_CUDA(cudaMemsetAsync(tv.first, 0xff, sizeof(uint32_t) * cap, st));
+  BFB_CUDA(cudaMemsetAsync(tv.cnt, 0, sizeof(uint32_t) * cap, st));
+  return BFB_OK;
+}
+
+extern "C" int bfb_hard_voxelize_batch(const void* points, int dtype, const int64_t* offsets, int64_t batch,
+                                       int64_t n, int64_t f, const float* voxel_size, const float* coors_range,
+                                       int64_t max_points, int64_t max_voxels, void* voxels, int32_t* coors,
+                                       int32_t* num_points, int32_t* voxel_num, int zero_tail, void* table,
+                                       size_t table_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+  BFB_TRY(check_common(points, dtype, n, f));
+  if (batch < 1 || !offsets || !voxel_num) return BFB_ERR_INVALID_ARG;
+  if (batch >= (1LL << (64 - kLinBits))) return BFB_ERR_TOO_LARGE;
+  if (max_points == 0 || max_points < -1 || max_voxels == 0 || max_voxels < -1) return BFB_ERR_INVALID_ARG;
+  if (offsets[0] != 0 || offsets[batch] != n) return BFB_ERR_INVALID_ARG;
+  for (int64_t s = 0; s < batch; ++s)
+    if (offsets[s + 1] < offsets[s]) return BFB_ERR_INVALID_ARG;
+  if (!voxels || !coors || !num_points) return BFB_ERR_INVALID_ARG;
+  Grid gr;
+  BFB_TRY(make_grid(voxel_size, coors_range, &gr));
+  for (int i = 0; i < 3; ++i)
+    if (gr.g[i] <= 0) return BFB_ERR_INVALID_ARG;
+  if (gr.g[0] > (1LL << kLinBits) / gr.g[1] / gr.g[2]) return BFB_ERR_TOO_LARGE;
+  const uint64_t cap = table_cap_for_bytes(table_bytes);
+  VoxScratch sv;
+  if (!table || !scratch || cap < (uint64_t)(2 * n) || carve_scratch(nullptr, n, batch, &sv) > scratch_bytes)
+    return BFB_ERR_WORKSPACE;
+  TableView tv;
+  carve_table(table, cap, &tv);
+  carve_scratch(scratch, n, batch, &sv);
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case BFB_F32:
+      return hard_voxelize_impl<float>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels, coors,
+                                       num_points, voxel_num, zero_tail, tv, sv, st);
+    case BFB_F16:
+      return hard_voxelize_impl<__half>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels, coors,
+                                        num_points, voxel_num, zero_tail, tv, sv, st);
+    default:
+      return hard_voxelize_impl<__nv_bfloat16>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels,
+                                               coors, num_points, voxel_num, zero_tail, tv, sv, st);
+  }
+}
+
+extern "C" int bfb_hard_voxelize(const void* points, int dtype, int64_t n, int64_t f, const float* voxel_size,
+                                 const float* coors_range, int64_t max_points, int64_t max_voxels, void* voxels,
+                                 int32_t* coors, int32_t* num_points, int32_t* voxel_num, int zero_tail, void* table,
+                                 size_t table_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+  const int64_t offs[2] = {0, n};
+  return bfb_hard_voxelize_batch(points, dtype, offs, 1, n, f, voxel_size, coors_range, max_points, max_voxels,
+                                 voxels, coors, num_points, voxel_num, zero_tail, table, table_bytes, scratch,
+                                 scratch_bytes, stream);
+}
+
+extern "C" int bfb_hard_voxelize_status(const void* scratch, int64_t n, int64_t batch, int64_t* table_full,
+                                        void* stream) {
+  if (!scratch || !table_full || n < 0 || batch < 1) return BFB_ERR_INVALID_ARG;
+  VoxScratch sv;
+  carve_scratch(const_cast<void*>(scratch), n, batch, &sv);
+  uint32_t v = 0;
+  cudaStream_t st = as_stream(stream);
+  BFB_CUDA(cudaMemcpyAsync(&v, sv.err, sizeof(v), cudaMemcpyDeviceToHost, st));
+  BFB_CUDA(cudaStreamSynchronize(st));
+  *table_full = v;
+  return BFB_OK;
+}
+

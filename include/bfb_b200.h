@@ -133,35 +133,87 @@ int bfb_dynamic_voxelize(const void* points_dev, int points_dtype, int64_t n, in
  * Voxel ids follow the first in-range point of each voxel; at most
  * max_voxels voxels are created (points of later new voxels are dropped) and
  * each voxel keeps its first max_points points in input order
- * (max_points = -1: no per-voxel limit; max_voxels = -1: no voxel limit; the
- * output buffers must then be sized for n).  Outputs: voxels
- * [max_voxels, max_points, f] (dtype of points), coors [max_voxels, 3] int32
- * (x, y, z), num_points [max_voxels] int32, voxel_num [1] int32 (device).
- * Rows [0, voxel_num) are written in full (unused point slots are 0); rows
- * [voxel_num, max_voxels) are zero-filled only when zero_tail != 0.
- * The `deterministic` flag of the reference is accepted by the Python layer
- * and always served by this deterministic kernel. */
-int bfb_hard_voxelize_workspace_size(int64_t n, int64_t batch, size_t* scratch_bytes);
+ * (max_points = -1: no per-voxel limit, the voxels buffer then holds n slots
+ * per voxel; max_voxels = -1: no voxel limit, the buffers then hold n
+ * voxels).  Outputs: voxels [max_voxels, max_points, f] (dtype of points),
+ * coors [max_voxels, 3] int32 (x, y, z), num_points [max_voxels] int32,
+ * voxel_num [1] int32 (device).  Rows [0, voxel_num) are written in full
+ * (unused point slots are 0); rows [voxel_num, max_voxels) are zero-filled
+ * only when zero_tail != 0.  The `deterministic` flag of the reference is
+ * accepted by the Python layer and always served by this deterministic
+ * kernel.
+ *
+ * Workspaces: `table` is a hash table that must be initialised once with
+ * bfb_hard_voxelize_table_init; every successful call leaves it clean, so it
+ * can be reused call after call (re-initialise it after a failed call).  Its
+ * capacity (from table_bytes) must be at least twice the point count of a
+ * call.  `scratch` is only used during the call. */
+int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, size_t* table_bytes,
+                                      size_t* scratch_bytes);
+
+int bfb_hard_voxelize_table_init(void* table_dev, size_t table_bytes, void* stream);
 
 int bfb_hard_voxelize(const void* points_dev, int points_dtype, int64_t n, int64_t f,
                       const float* voxel_size, const float* coors_range, int64_t max_points,
                       int64_t max_voxels, void* voxels_dev, int32_t* coors_dev,
                       int32_t* num_points_dev, int32_t* voxel_num_dev, int zero_tail,
-                      void* scratch_dev, size_t scratch_bytes, void* stream);
+                      void* table_dev, size_t table_bytes, void* scratch_dev, size_t scratch_bytes,
+                      void* stream);
 
 /* Batched hard voxelisation of `batch` independent samples in one set of
- * launches (no reference counterpart as one call: it replaces the per-sample
- * loop of models/fusion_models/bevfusion.py:269-296 over
- * `Voxelization.forward`).  Sample s owns points [offsets[s], offsets[s+1])
- * (offsets_dev: int64 [batch + 1], device) and the output slices
- * voxels[s] = [max_voxels, max_points, f], coors[s] = [max_voxels, 3],
- * num_points[s] = [max_voxels]; voxel_num_dev [batch]. */
-int bfb_hard_voxelize_batch(const void* points_dev, int points_dtype, const int64_t* offsets_dev,
-                            int64_t batch, int64_t n_total, int64_t f, const float* voxel_size,
+ * launches.  It has no single reference counterpart: it replaces the
+ * per-sample loop of models/fusion_models/bevfusion.py:269-296 over
+ * `Voxelization.forward`.  Sample s owns points [offsets[s], offsets[s+1])
+ * (offsets: int64 [batch + 1], HOST memory, offsets[0] = 0,
+ * offsets[batch] = n) and the output slices voxels[s] =
+ * [max_voxels, max_points, f], coors[s] = [max_voxels, 3],
+ * num_points[s] = [max_voxels]; voxel_num_dev holds [batch] counts. */
+int bfb_hard_voxelize_batch(const void* points_dev, int points_dtype, const int64_t* offsets,
+                            int64_t batch, int64_t n, int64_t f, const float* voxel_size,
                             const float* coors_range, int64_t max_points, int64_t max_voxels,
                             void* voxels_dev, int32_t* coors_dev, int32_t* num_points_dev,
-                            int32_t* voxel_num_dev, int zero_tail, void* scratch_dev,
-                            size_t scratch_bytes, void* stream);
+                            int32_t* voxel_num_dev, int zero_tail, void* table_dev,
+                            size_t table_bytes, void* scratch_dev, size_t scratch_bytes,
+                            void* stream);
+
+/* Synchronously reads the device status of the last call that used this
+ * scratch: *table_full = points whose insert found no free table slot
+ * (always 0 when the table capacity rule above holds). */
+int bfb_hard_voxelize_status(const void* scratch_dev, int64_t n, int64_t batch,
+                             int64_t* table_full, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Dynamic scatter: per-voxel reduce of point features.  Replaces
+ * ops/voxel/voxel_layer.py:39-48 -> ops/voxel/src/scatter_points_triton.py:253-424
+ * (`dynamic_point_to_voxel_forward` / `_backward`) and the legacy
+ * ops/voxel/csrc/voxelization.h:132-140.
+ *
+ * Rows of coors [n, ndim] int32 with any negative entry are ignored; the
+ * unique remaining rows are numbered in ascending lexicographic order.
+ * reduce: 0 = sum (also the reference's 'none'), 1 = mean, 2 = max.  Outputs
+ * are sized for the worst case (n voxels): out_feats [n, c] (dtype of feats),
+ * out_coors [n, ndim], point2voxel [n] (-1 for ignored rows), counts [n];
+ * the first *num_voxels rows are valid.  Synchronous: the voxel count is
+ * returned on the host.  The packed lexicographic key of a row must fit in 31
+ * bits (BFB_ERR_TOO_LARGE otherwise).
+ * ---------------------------------------------------------------------- */
+int bfb_dynamic_scatter_workspace_size(int64_t n, int64_t c, int64_t ndim, size_t* bytes);
+
+int bfb_dynamic_scatter_forward(const void* feats_dev, int dtype, const int32_t* coors_dev, int64_t n,
+                                int64_t c, int64_t ndim, int reduce, void* out_feats_dev,
+                                int32_t* out_coors_dev, int32_t* point2voxel_dev,
+                                int32_t* counts_dev, int64_t* num_voxels, void* ws_dev,
+                                size_t ws_bytes, void* stream);
+
+/* grad_feats [n, c] (fully written): sum copies grad_out[map], mean divides
+ * it by the voxel's count, max sends each channel's gradient to the lowest
+ * point index whose feature equals the reduced value (others 0).  max needs
+ * argmax_ws of m * c int32. */
+int bfb_dynamic_scatter_backward(void* grad_feats_dev, const void* grad_out_dev,
+                                 const void* feats_dev, const void* reduced_dev,
+                                 const int32_t* point2voxel_dev, const int32_t* counts_dev,
+                                 int dtype, int64_t n, int64_t m, int64_t c, int reduce,
+                                 int32_t* argmax_ws_dev, size_t argmax_ws_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,222 @@
+"""Voxelisation and dynamic scatter on the GPU against the reference's golden
+outputs and the CPU oracle.  Voxel coordinates, counts, per-voxel point order
+and stored features are compared bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from bevfusion_triton_b200 import synth
+from bevfusion_triton_b200.ops.voxel import DynamicScatter, Voxelization, dynamic_scatter, voxelization, voxelize_batch
+from bevfusion_triton_b200.ops.voxel.voxel_layer import (dynamic_point_to_voxel_backward,
+                                                         dynamic_point_to_voxel_forward, dynamic_voxelize,
+                                                         hard_voxelize, hard_voxelize_batch)
+from oracle import oracle
+from tests._util import sha
+
+pytestmark = pytest.mark.gpu
+
+VS8, CR8 = [1.0, 1.0, 1.0], [0.0, 0.0, 0.0, 4.0, 4.0, 4.0]
+
+
+def run_hard(points, vsize, crange, mp, mv, fill=None, deterministic=True):
+    dev = 'cuda'
+    pts = points.to(dev)
+    n = pts.size(0)
+    P = n if mp == -1 else mp
+    MV = n if mv == -1 else mv
+    mk = (lambda shape, dt: torch.full(shape, fill, dtype=dt, device=dev)) if fill is not None else \
+        (lambda shape, dt: torch.zeros(shape, dtype=dt, device=dev))
+    voxels = mk((MV, P, pts.size(1)), pts.dtype)
+    coors = mk((MV, 3), torch.int32)
+    num = mk((MV,), torch.int32)
+    vn = hard_voxelize(pts, voxels, coors, num, vsize, crange, mp, mv, 3, deterministic)
+    return voxels.cpu(), coors.cpu(), num.cpu(), vn
+
+
+def assert_hard_equal(got, ref):
+    v, c, n, vn = got
+    rv, rc, rn, rvn = ref
+    assert vn == rvn
+    np.testing.assert_array_equal(c.numpy(), np.asarray(rc))
+    np.testing.assert_array_equal(n.numpy(), np.asarray(rn))
+    np.testing.assert_array_equal(v.float().numpy(), np.asarray(rv, dtype=np.float32))
+
+
+def test_dynamic_voxelize_golden(cuda, golden):
+    g = golden('voxel_points8')
+    c = torch.zeros((8, 3), dtype=torch.int32, device='cuda')
+    dynamic_voxelize(torch.from_numpy(g['points']).cuda(), c, VS8, CR8, 3)
+    np.testing.assert_array_equal(c.cpu().numpy(), g['dyn_coors'])
+    g = golden('voxel_rand_noncubic')
+    c = torch.zeros((g['points'].shape[0], 3), dtype=torch.int32, device='cuda')
+    dynamic_voxelize(torch.from_numpy(g['points']).cuda(), c, g['vsize'].tolist(), g['crange'].tolist(), 3)
+    np.testing.assert_array_equal(c.cpu().numpy(), g['dyn_coors'])
+
+
+@pytest.mark.parametrize('dtype', [torch.float16, torch.bfloat16])
+def test_dynamic_voxelize_low_precision(cuda, golden, dtype):
+    g = golden('voxel_rand_noncubic')
+    pts = torch.from_numpy(g['points']).to(dtype)
+    c = torch.zeros((pts.size(0), 3), dtype=torch.int32, device='cuda')
+    dynamic_voxelize(pts.cuda(), c, g['vsize'].tolist(), g['crange'].tolist(), 3)
+    ref = oracle.dynamic_voxelize(pts.float().numpy(), g['vsize'], g['crange'])
+    np.testing.assert_array_equal(c.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize('mp,mv', [(2, 8), (3, 8), (1, 2)])
+@pytest.mark.parametrize('deterministic', [True, False])
+def test_hard_voxelize_points8(cuda, golden, mp, mv, deterministic):
+    g = golden('voxel_points8')
+    k = f'mp{mp}_mv{mv}'
+    got = run_hard(torch.from_numpy(g['points']), VS8, CR8, mp, mv, deterministic=deterministic)
+    assert_hard_equal(got, (g[f'{k}_voxels'], g[f'{k}_coors'], g[f'{k}_num'], int(g[f'{k}_vn'])))
+
+
+@pytest.mark.parametrize('mp,mv', [(5, 300), (5, 100000), (32, 50)])
+def test_hard_voxelize_noncubic(cuda, golden, mp, mv):
+    g = golden('voxel_rand_noncubic')
+    k = f'mp{mp}_mv{mv}'
+    got = run_hard(torch.from_numpy(g['points']), g['vsize'].tolist(), g['crange'].tolist(), mp, mv, fill=7)
+    assert_hard_equal(got, (g[f'{k}_voxels'], g[f'{k}_coors'], g[f'{k}_num'], int(g[f'{k}_vn'])))
+
+
+def test_hard_voxelize_lidar_full_size_digest(cuda, digests):
+    """Config 3 (346,880 points, 1440 x 1440 x 40 grid): equal to the
+    reference CPU path's output bit for bit."""
+    d = digests['lidar_s0']
+    pts = synth.lidar_sweeps(0)
+    assert sha(pts) == d['points_sha']
+    for _ in range(2):  # second call checks that the hash table was left clean
+        v, c, n, vn = run_hard(pts, list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE), synth.LIDAR_MAX_POINTS,
+                               synth.LIDAR_MAX_VOXELS, fill=3)
+        assert vn == d['voxel_num']
+        assert sha(c[:vn]) == d['coors_sha'] and sha(n[:vn]) == d['num_sha'] and sha(v[:vn]) == d['voxels_sha']
+        assert not v[vn:].any() and not c[vn:].any() and not n[vn:].any()
+
+
+@pytest.mark.parametrize('mp,mv', [(-1, 64), (4, -1), (3, 5)])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
+def test_hard_voxelize_random_vs_oracle(cuda, mp, mv, dtype):
+    g = torch.Generator().manual_seed(mp * 7 + mv)
+    n = 1500
+    pts = torch.rand((n, 4), generator=g) * torch.tensor([6.0, 5.0, 3.0, 1.0]) - torch.tensor([3.0, 2.5, 1.5, 0.0])
+    pts[::5, :3] = pts[0, :3]  # one crowded voxel
+    pts = pts.to(dtype)
+    vs, cr = [0.5, 0.5, 0.75], [-2.5, -2.0, -1.5, 2.5, 2.0, 1.5]
+    got = run_hard(pts, vs, cr, mp, mv)
+    ref = oracle.hard_voxelize(pts.float().numpy(), vs, cr, mp if mp != -1 else n, mv)
+    rv, rc, rn, rvn = ref
+    v, c, nn, vn = got
+    assert vn == rvn
+    np.testing.assert_array_equal(c[:vn].numpy(), rc[:vn])
+    np.testing.assert_array_equal(nn[:vn].numpy(), rn[:vn])
+    np.testing.assert_array_equal(v[:vn].float().numpy(), rv[:vn])
+
+
+def test_hard_voxelize_empty_and_all_outside(cuda):
+    for pts in (torch.zeros((0, 4)), torch.full((50, 4), 100.0)):
+        v, c, n, vn = run_hard(pts, VS8, CR8, 3, 8, fill=9)
+        assert vn == 0
+        assert not v.any() and not c.any() and not n.any()
+
+
+def test_voxelization_module_matches_function(cuda, golden):
+    g = golden('voxel_points8')
+    pts = torch.from_numpy(g['points']).cuda()
+    m = Voxelization(voxel_size=VS8, point_cloud_range=CR8, max_num_points=3, max_voxels=8, deterministic=True)
+    m.eval()
+    a = m(pts)
+    b = voxelization(pts, VS8, CR8, 3, 8, True)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    k = 'mp3_mv8'
+    vn = int(g[f'{k}_vn'])
+    np.testing.assert_array_equal(a[0].cpu().numpy(), g[f'{k}_voxels'][:vn])
+    np.testing.assert_array_equal(a[1].cpu().numpy(), g[f'{k}_coors'][:vn])
+    dyn = voxelization(pts, VS8, CR8, -1, -1, True)
+    np.testing.assert_array_equal(dyn.cpu().numpy(), g['dyn_coors'])
+
+
+def test_hard_voxelize_batch_matches_single(cuda):
+    clouds = [synth.lidar_sweeps(s)[: 50000 + 7000 * s] for s in range(3)] + [torch.zeros((0, 5))]
+    clouds = [clouds[0], clouds[3], clouds[1], clouds[2]]  # an empty sample in the middle
+    offs = [0]
+    for c in clouds:
+        offs.append(offs[-1] + c.size(0))
+    pts = torch.cat(clouds).cuda()
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    V, C, N, VN = hard_voxelize_batch(pts, offs, vs, cr, 10, 20000)
+    for s, cl in enumerate(clouds):
+        v, c, n, vn = run_hard(cl, vs, cr, 10, 20000)
+        assert int(VN[s]) == vn
+        assert torch.equal(V[s, :vn].cpu(), v[:vn]) and torch.equal(C[s, :vn].cpu(), c[:vn])
+        assert torch.equal(N[s, :vn].cpu(), n[:vn])
+
+
+def test_voxelize_batch_mean_features(cuda):
+    clouds = [synth.lidar_sweeps(s)[:30000].cuda() for s in range(2)]
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    feats, coords, sizes = voxelize_batch(clouds, vs, cr, 10, 12000)
+    rf, rc, rs = [], [], []
+    for b, c in enumerate(clouds):  # models/fusion_models/bevfusion.py:269-296
+        v, cc, nn = voxelization(c, vs, cr, 10, 12000, True)
+        rf.append(v)
+        rc.append(torch.nn.functional.pad(cc, (1, 0), mode='constant', value=b))
+        rs.append(nn)
+    rs = torch.cat(rs)
+    ref = torch.cat(rf).sum(1) / rs.to(torch.float32).unsqueeze(1)
+    assert torch.equal(coords, torch.cat(rc)) and torch.equal(sizes, rs)
+    assert torch.equal(feats, ref)
+
+
+# ----------------------------------------------------------------- scatter
+@pytest.mark.parametrize('case', ['fix', 'rand'])
+@pytest.mark.parametrize('red', ['sum', 'mean', 'max'])
+def test_dynamic_scatter_golden(cuda, golden, case, red):
+    g = golden('scatter_cases')
+    f = torch.from_numpy(g[f'{case}_feats']).cuda()
+    c = torch.from_numpy(g[f'{case}_coors']).cuda()
+    vf, vc, mp, cnt = dynamic_point_to_voxel_forward(f, c, red)
+    np.testing.assert_array_equal(vc.cpu().numpy(), g[f'{case}_{red}_vc'])
+    np.testing.assert_array_equal(mp.cpu().numpy(), g[f'{case}_{red}_map'])
+    np.testing.assert_array_equal(cnt.cpu().numpy(), g[f'{case}_{red}_cnt'])
+    np.testing.assert_array_equal(vf.cpu().numpy(), g[f'{case}_{red}_vf'])
+    gf = torch.zeros_like(f)
+    dynamic_point_to_voxel_backward(gf, torch.from_numpy(g[f'{case}_{red}_up']).cuda(), f, vf, mp, cnt, red)
+    np.testing.assert_array_equal(gf.cpu().numpy(), g[f'{case}_{red}_grad'])
+
+
+@pytest.mark.parametrize('red', ['sum', 'mean', 'max'])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
+def test_dynamic_scatter_random_vs_oracle(cuda, red, dtype):
+    g = torch.Generator().manual_seed(11)
+    n, C = 5000, 37
+    f = torch.randn((n, C), generator=g).to(dtype)
+    c = torch.randint(-1, 40, (n, 3), generator=g).to(torch.int32)
+    x = f.cuda().requires_grad_(True)
+    vf, vc = dynamic_scatter(x, c.cuda(), red)
+    rf, rc, rm, rcnt = oracle.dynamic_scatter(f.float().numpy(), c.numpy(), red)
+    np.testing.assert_array_equal(vc.cpu().numpy(), rc)
+    tol = dict(rtol=0, atol=0) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(vf.detach().float().cpu().numpy(), rf, **tol)
+    up = torch.linspace(0.1, 1.0, vf.numel(), device='cuda', dtype=vf.dtype).view_as(vf)
+    (vf * up).sum().backward()
+    rg = oracle.dynamic_scatter_backward(up.float().cpu().numpy(), f.float().numpy(),
+                                         vf.detach().float().cpu().numpy(), rm, rcnt, red)
+    np.testing.assert_allclose(x.grad.float().cpu().numpy(), rg, **tol)
+
+
+def test_dynamic_scatter_module(cuda, golden):
+    g = golden('scatter_cases')
+    f = torch.from_numpy(g['fix_feats']).cuda()
+    c = torch.from_numpy(g['fix_coors']).cuda()
+    m = DynamicScatter(VS8, CR8, average_points=True)
+    a = m(f, c)
+    b = dynamic_scatter(f, c, 'mean')
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    # batched form: (b, x, y, z) rows
+    cb = torch.cat([torch.zeros((c.size(0), 1), dtype=torch.int32, device='cuda'), c], 1)
+    cb = torch.cat([cb, cb.clone().index_fill_(1, torch.tensor([0], device='cuda'), 1)])
+    fb = torch.cat([f, f * 2])
+    ob, ocb = m(fb, cb)
+    assert ob.shape[0] == 2 * b[0].shape[0] and torch.equal(ocb[:, 1:], torch.cat([b[1], b[1]]))
