@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the BEVFusion grid scatter-reduce hot path on B200.
+
+One step on every GPU = config 1 of BASELINE.json (det bev_pool forward +
+backward over a batch of 8 camera samples, fp32, 1,770,765 points x 80
+channels per sample, 360 x 360 grid) plus hard voxelisation of a batch of 8
+synthetic LiDAR sweeps (config 3 shape, 346,880 points each).  Sample i of
+rank r is sample r * 8 + i of one global batch, so 8 GPUs run exactly the
+batch-64 scaling sweep (config 5); per-GPU work is fixed ("weak" scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is milliseconds per sample over the
+whole job (step time, max over ranks, divided by all samples of all ranks),
+with inputs resident in HBM; `e2e` is the same metric through the public
+Python API with the step's inputs copied from pinned host memory and its
+outputs copied back inside the timed region.  `--impl reference` times the
+reference's own CPU algorithms (oracle/ref_cpu.py) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from bevfusion_triton_b200 import synth  # noqa: E402
+
+METRIC = 'bev_pool fwd+bwd & voxelize ms/sample and GB/s (% of B200 HBM peak), 1/2/4/8 GPU'
+UNIT = 'ms/sample'
+SAMPLES_PER_GPU = 8
+C = synth.CHANNELS
+FALLBACK_HBM_GBS = 6650.0
+
+# DRAM traffic (read + write bytes) of the dominant kernels from ncu, per unit
+# of work, from the captures summarised in profiles/ (scaled by the units a
+# launch processes).  None until captured.
+NCU_TRAFFIC_PER_POINT = {
+    'bev_fwd_kernel': None,
+    'bev_bwd_kernel': None,
+}
+
+
+def measured_peak():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    try:
+        d = json.loads(p.read_text())
+        return float(d['hbm_gbs']), 'measured'
+    except Exception:
+        return FALLBACK_HBM_GBS, 'fallback'
+
+
+# ------------------------------------------------------------------ dist
+def dist_setup(args):
+    ws = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if ws > 1:
+        import torch.distributed as dist
+        backend = 'nccl' if torch.cuda.is_available() else 'gloo'
+        if backend == 'nccl':
+            torch.cuda.set_device(local)
+            dist.init_process_group(backend, timeout=timedelta(seconds=600),
+                                    device_id=torch.device('cuda', local))
+        else:
+            dist.init_process_group(backend, timeout=timedelta(seconds=600))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device='cuda' if torch.cuda.is_available() else 'cpu')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device='cuda' if torch.cuda.is_available() else 'cpu')
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def _gpu_id(self):
+        try:
+            p = torch.cuda.get_device_properties(self.dev)
+            return f'{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0'
+        except Exception:
+            return None
+
+    def start(self):
+        cmd = ['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits', '-lms', '100']
+        gid = self._gpu_id()
+        if gid:
+            cmd += ['-i', gid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ------------------------------------------------------------------ inputs
+class Workload:
+    """The rank's shard: det bev_pool batch + LiDAR batch, resident on the GPU."""
+
+    def __init__(self, rank: int, samples: int, device):
+        self.S = samples
+        case = synth.det_bev_pool_case(samples, device=device, sample_offset=rank * samples)
+        self.feats, self.coords = case.feats, case.coords
+        self.shape = (case.B, case.D, case.H, case.W)
+        self.n = self.feats.size(0)
+        g = torch.Generator(device=device)
+        g.manual_seed(1000 + rank)
+        self.up = torch.randn((case.B, C, case.D, case.H, case.W), generator=g, device=device)
+        dhw = case.D * case.H * case.W
+        r = (self.coords[:, 3] * dhw + (self.coords[:, 2] * case.H + self.coords[:, 0]) * case.W + self.coords[:, 1])
+        self.nonempty = int(torch.unique(r).numel())
+        clouds = [synth.lidar_sweeps(rank * samples + i) for i in range(samples)]
+        self.offs = [0]
+        for c in clouds:
+            self.offs.append(self.offs[-1] + c.size(0))
+        self.points_cpu = torch.cat(clouds)
+        self.points = self.points_cpu.to(device)
+        self.vsize, self.crange = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+        self.mp, self.mv = synth.LIDAR_MAX_POINTS, synth.LIDAR_MAX_VOXELS
+        F = self.points.size(1)
+        self.voxels = torch.empty((samples, self.mv, self.mp, F), device=device)
+        self.vcoors = torch.empty((samples, self.mv, 3), dtype=torch.int32, device=device)
+        self.vnum = torch.empty((samples, self.mv), dtype=torch.int32, device=device)
+        self.vn = torch.empty((samples,), dtype=torch.int32, device=device)
+
+    # algorithmic bytes per rank: fwd = N*C*4 + N*4*8 + B*C*D*H*W*4, bwd = N*C*4 + N*4*8 + U*C*4
+    # (U non-empty cells), voxelize = N*F*4 + M*(P*F*4 + 3*4 + 4) (M voxels)
+    def bytes_fwd(self):
+        B, D, H, W = self.shape
+        return self.n * C * 4 + self.n * 4 * 8 + B * C * D * H * W * 4
+
+    def bytes_bwd(self):
+        return self.n * C * 4 + self.n * 4 * 8 + self.nonempty * C * 4
+
+    def bytes_vox(self, vn_total: int):
+        F = self.points.size(1)
+        return self.points.numel() * 4 + vn_total * (self.mp * F * 4 + 3 * 4 + 4)
+
+
+def run_ours(args, ws, rank, local):
+    from bevfusion_triton_b200 import load_native
+    from bevfusion_triton_b200._lib import ops
+    cdll = load_native()
+    cdll.bfb_kernel_launches.restype = ctypes.c_uint64
+    O = ops()
+    dev = torch.device('cuda', local)
+    wl = Workload(rank, args.samples_per_gpu, dev)
+    B, D, H, W = wl.shape
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        plan = O.bev_pool_plan(wl.coords, B, D, H, W)
+        if ev:
+            ev[1].record(stream)
+        out = O.bev_pool_forward_planned(wl.feats, plan, B, D, H, W)
+        if ev:
+            ev[2].record(stream)
+        g = O.bev_pool_backward(wl.up, plan, wl.n, B, D, H, W)
+        if ev:
+            ev[3].record(stream)
+        O.hard_voxelize_batch(wl.points, wl.offs, wl.voxels, wl.vcoors, wl.vnum, wl.vn, wl.vsize, wl.crange,
+                              wl.mp, wl.mv, False)
+        if ev:
+            ev[4].record(stream)
+        return out, g
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    launches0 = cdll.bfb_kernel_launches()
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0.record(stream)
+    for k in range(args.steps):
+        step(evs[k])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    launches = int(cdll.bfb_kernel_launches() - launches0)
+    clocks = clk.stop()
+    total_ms = max_over_ranks(t0.elapsed_time(t1), ws)
+    ms_step = total_ms / args.steps
+    phase = [statistics.median(e[i].elapsed_time(e[i + 1]) for e in evs) for i in range(4)]
+    vn_total = int(wl.vn.sum().item())
+
+    samples_total = args.samples_per_gpu * ws
+    per_rank_bytes = wl.bytes_fwd() + wl.bytes_bwd() + wl.bytes_vox(vn_total)
+    job_bytes = sum_over_ranks(per_rank_bytes, ws)
+    peak, peak_kind = measured_peak()
+    gbs = job_bytes / (ms_step * 1e-3) / 1e9
+
+    # roofline of the dominant kernel (one launch per step each)
+    B_, D_, H_, W_ = wl.shape
+    fwd_alg = wl.n * C * 4 + B_ * C * D_ * H_ * W_ * 4
+    bwd_alg = wl.n * C * 4 + wl.nonempty * C * 4
+    cand = {'bev_fwd_kernel': (phase[1], fwd_alg), 'bev_bwd_kernel': (phase[2], bwd_alg)}
+    kname = max(cand, key=lambda k: cand[k][0])
+    kms, kbytes = cand[kname]
+    achieved = kbytes / (kms * 1e-3) / 1e9
+    tpp = NCU_TRAFFIC_PER_POINT.get(kname)
+    roofline = {'kernel': kname, 'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
+                'peak_kind': peak_kind, 'unit': 'GB/s', 'frac': round(achieved / peak, 4),
+                'traffic': (round(tpp * wl.n) if tpp else None), 'algorithmic_bytes': kbytes,
+                'ms_per_launch': round(kms, 4)}
+
+    line = {
+        'metric': METRIC, 'value': round(ms_step / samples_total, 5), 'unit': UNIT, 'n_gpus': ws,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms_step, 4),
+        'higher_is_better': False, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded stand-ins for nuScenes: 6-camera det frustum, 32-beam 10-sweep LiDAR)',
+        'config': {
+            'workload': (f'per GPU: det bev_pool fwd+bwd batch {args.samples_per_gpu} (config 1, 360x360, C=80, fp32, '
+                         f'int64 coords) + LiDAR hard_voxelize batch {args.samples_per_gpu} (config 3 shape, '
+                         f'1440x1440x40, max_points 10, max_voxels 120000)'),
+            'samples_per_gpu': args.samples_per_gpu, 'global_batch': samples_total,
+            'points_per_det_sample': wl.n // args.samples_per_gpu,
+            'l2': 'inputs larger than L2 (det feats %.1f GB per GPU)' % (wl.feats.numel() * 4 / 1e9),
+            'parallelism': f'batch-sample sharding over {ws} GPU(s), no collective on the hot path',
+        },
+        'gbs': round(gbs, 1), 'hbm_frac': round(gbs / (peak * ws), 4),
+        'breakdown_ms_per_step': {'plan': round(phase[0], 4), 'bev_fwd': round(phase[1], 4),
+                                  'bev_bwd': round(phase[2], 4), 'voxelize': round(phase[3], 4)},
+        'roofline': roofline, 'gpu_launches': launches, 'clocks': clocks,
+    }
+    if not args.no_e2e:
+        line['e2e'] = run_e2e(args, wl, ws, samples_total)
+    if not args.no_cpu_baseline and ws == 1 and rank == 0:
+        line['cpu_baseline'] = cpu_baseline(args)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, wl, ws, samples_total):
+    """Public API, host buffers: pinned H2D of the step's inputs, bev_pool
+    forward + backward through autograd, batched voxelisation, D2H of every
+    output, all inside the timed region."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool
+    from bevfusion_triton_b200.ops.voxel.voxel_layer import hard_voxelize_batch
+    feats_h = wl.feats.cpu().pin_memory()
+    coords_h = wl.coords.cpu().pin_memory()
+    up_h = wl.up.cpu().pin_memory()
+    pts_h = wl.points_cpu.pin_memory()
+    out_h = torch.empty(wl.up.shape, dtype=torch.float32).pin_memory()
+    grad_h = torch.empty(wl.feats.shape, dtype=torch.float32).pin_memory()
+    vox_h = torch.empty(wl.voxels.shape, dtype=torch.float32).pin_memory()
+    vc_h = torch.empty(wl.vcoors.shape, dtype=torch.int32).pin_memory()
+    vnum_h = torch.empty(wl.vnum.shape, dtype=torch.int32).pin_memory()
+    vn_h = torch.empty(wl.vn.shape, dtype=torch.int32).pin_memory()
+    B, D, H, W = wl.shape
+    h2d = sum(t.numel() * t.element_size() for t in (feats_h, coords_h, up_h, pts_h))
+    d2h = sum(t.numel() * t.element_size() for t in (out_h, grad_h, vox_h, vc_h, vnum_h, vn_h))
+
+    def step():
+        feats = feats_h.to('cuda', non_blocking=True).requires_grad_(True)
+        coords = coords_h.to('cuda', non_blocking=True)
+        up = up_h.to('cuda', non_blocking=True)
+        pts = pts_h.to('cuda', non_blocking=True)
+        out = bev_pool(feats, coords, B, D, H, W)
+        out.backward(up)
+        V, Cc, N, VN = hard_voxelize_batch(pts, wl.offs, wl.vsize, wl.crange, wl.mp, wl.mv)
+        out_h.copy_(out.detach(), non_blocking=True)
+        grad_h.copy_(feats.grad, non_blocking=True)
+        vox_h.copy_(V, non_blocking=True)
+        vc_h.copy_(Cc, non_blocking=True)
+        vnum_h.copy_(N, non_blocking=True)
+        vn_h.copy_(VN, non_blocking=True)
+
+    steps = max(2, min(args.steps, args.e2e_steps))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    ms = max_over_ranks(s.elapsed_time(e), ws) / steps
+    return {'value': round(ms / samples_total, 4), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
+            'd2h_bytes_per_step': d2h, 'steps': steps, 'ms_per_step': round(ms, 3)}
+
+
+# ------------------------------------------------------------------ CPU
+def cpu_reference_sample(threads: int, det=None, clouds=None):
+    """One bounded sample of the reference's CPU algorithms: det bev_pool
+    fwd+bwd of one camera sample (torch CPU, `threads` threads) and hard
+    voxelisation of `threads` LiDAR samples in parallel.  Returns
+    (ms per sample, description)."""
+    from oracle import ref_cpu
+    torch.set_num_threads(threads)
+    if det is None:
+        det = synth.det_bev_pool_case(1, device='cpu')
+        g = torch.Generator().manual_seed(5)
+        det.up = torch.randn((1, C, det.D, det.H, det.W), generator=g)
+    if clouds is None:
+        clouds = [synth.lidar_sweeps(i) for i in range(threads)]
+    t = time.perf_counter()
+    ref_cpu.bev_pool_fwd_bwd_cpu(det.feats, det.coords, det.B, det.D, det.H, det.W, det.up)
+    t_bev = time.perf_counter() - t
+    t = time.perf_counter()
+    ref_cpu.hard_voxelize_many(clouds, list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE),
+                               synth.LIDAR_MAX_POINTS, synth.LIDAR_MAX_VOXELS, threads=threads)
+    t_vox = (time.perf_counter() - t) / len(clouds)
+    return (t_bev + t_vox) * 1e3, det, clouds, t_bev * 1e3, t_vox * 1e3
+
+
+def cpu_baseline(args):
+    threads = os.cpu_count() or 1
+    cpu_reference_sample(threads)  # warm
+    ms, det, clouds, tb, tv = cpu_reference_sample(threads)
+    return {'value': round(ms, 2), 'unit': UNIT, 'cores': threads, 'kind': 'port',
+            'sample': (f'1 det sample bev_pool fwd+bwd via torch CPU index_add_ ({tb:.1f} ms, {threads} threads) + '
+                       f'{len(clouds)} LiDAR samples hard_voxelize via the C restatement of the reference loop, '
+                       f'one per thread ({tv:.1f} ms/sample)')}
+
+
+def run_reference(args, ws, rank):
+    """--impl reference: the reference's own CPU algorithms on the host cores
+    (rank 0 only; other ranks exit without work)."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    ms0, det, clouds, _, _ = cpu_reference_sample(threads)
+    vals, tbs, tvs = [], [], []
+    steps = max(1, min(args.steps, args.ref_steps))
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_reference_sample(threads, det, clouds)
+    for _ in range(steps):
+        ms, _, _, tb, tv = cpu_reference_sample(threads, det, clouds)
+        vals.append(ms)
+        tbs.append(tb)
+        tvs.append(tv)
+    v = statistics.median(vals)
+    sample = (f'per step: 1 det sample bev_pool fwd+bwd via torch CPU index_add_ ({statistics.median(tbs):.1f} ms, '
+              f'{threads} threads) + {len(clouds)} LiDAR samples hard_voxelize via the C restatement of the '
+              f'reference loop, one per thread ({statistics.median(tvs):.1f} ms/sample)')
+    line = {
+        'metric': METRIC, 'value': round(v, 3), 'unit': UNIT, 'n_gpus': ws, 'steps': steps,
+        'warmup': args.warmup, 'ms_per_step': round(v, 3), 'higher_is_better': False, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'impl': 'reference',
+        'config': {'workload': 'det bev_pool fwd+bwd + LiDAR hard_voxelize, one sample each, reference CPU '
+                               'algorithms on the host cores', 'samples_per_gpu': args.samples_per_gpu},
+        'cpu_baseline': {'value': round(v, 3), 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': round(v, 3), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=50)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--samples-per-gpu', type=int, default=SAMPLES_PER_GPU)
+    ap.add_argument('--e2e-steps', type=int, default=5)
+    ap.add_argument('--ref-steps', type=int, default=3)
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == 'ours':
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+    ws, rank, local = dist_setup(args)
+    try:
+        if args.impl == 'reference':
+            run_reference(args, ws, rank)
+        else:
+            run_ours(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -1,4 +1,5 @@
 // Library-wide C-ABI entry points: version, status text, last CUDA error.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 
@@ -7,7 +8,10 @@
 namespace bfb {
 namespace {
 thread_local char g_last_error[256] = "";
+std::atomic<uint64_t> g_launches{0};
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int record_cuda_error(cudaError_t e) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
@@ -32,3 +36,5 @@ extern "C" const char* bfb_status_string(int status) {
 }
 
 extern "C" const char* bfb_last_cuda_error(void) { return bfb::g_last_error; }
+
+extern "C" uint64_t bfb_kernel_launches(void) { return bfb::g_launches.load(std::memory_order_relaxed); }

@@ -37,9 +37,13 @@ struct Carver {
 
 // Records the CUDA error text for bfb_last_cuda_error() and maps it to a status.
 int record_cuda_error(cudaError_t e);
+// Counts one kernel launch of this library (bfb_kernel_launches()).
+void count_launch();
 
+// Follows every kernel launch: counts it and maps a launch error to a status.
 #define BFB_CHECK_LAUNCH()                                   \
   do {                                                       \
+    ::bfb::count_launch();                                   \
     cudaError_t bfb_e_ = cudaGetLastError();                 \
     if (bfb_e_ != cudaSuccess) return ::bfb::record_cuda_error(bfb_e_); \
   } while (0)

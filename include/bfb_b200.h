@@ -57,6 +57,8 @@ int bfb_abi_version(void);
 const char* bfb_status_string(int status);
 /* Text of the last CUDA error seen by this thread inside the library. */
 const char* bfb_last_cuda_error(void);
+/* Number of kernels this library has launched in this process (all threads). */
+uint64_t bfb_kernel_launches(void);
 
 /* ------------------------------------------------------------------------
  * bev_pool: out[b, c, z, x, y] = sum_{n : coords[n] = (x, y, z, b)} feats[n, c]

@@ -14,7 +14,7 @@ ROOT = Path(__file__).resolve().parent.parent
 def declared_symbols():
     names = set()
     for h in (ROOT / 'include').glob('*.h'):
-        names |= set(re.findall(r'^\s*(?:int|const char\*|size_t|void)\s+(bfb_\w+)\s*\(', h.read_text(), re.M))
+        names |= set(re.findall(r'^\s*(?:int|const char\*|size_t|void|uint64_t)\s+(bfb_\w+)\s*\(', h.read_text(), re.M))
     return sorted(names)
 
 
