@@ -319,37 +319,30 @@ __host__ __device__ inline int tile_row_bytes(int chs, int elem) {
 }
 
 // ---------------------------------------------------------------------------
-// Piece prologue (warp 0): cell offsets in the permutation and a split of the
-// piece's cells into kPoolWarps contiguous runs with balanced point counts.
-// s_off[l] = first sorted position of local cell l (l = 0..nc, s_off[nc] = pb);
-// warp w owns local cells [s_wc[w], s_wc[w+1]).  A cell is never split, so
-// each cell is summed by one warp in ascending point order.
+// Piece prologue (warp 0): the piece's non-empty cells, largest first.
+// s_cell[i] = local cell, s_beg[i] = its first sorted position minus pa,
+// s_cnt[i] = its point count; *s_m = number of non-empty cells.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void split_piece(const int2* __restrict__ cell_se, uint32_t r0, int ca, int cb,
-                                            int pa, int* s_off, int* s_wc) {
+__device__ __forceinline__ void order_piece_cells(const int2* __restrict__ cell_se, uint32_t r0, int ca, int cb,
+                                                  int pa, int* s_cell, int* s_beg, int* s_cnt, int* s_m) {
   const int lane = threadIdx.x & 31;
-  const int nc = cb - ca;
-  int cnt = 0;
-  if (lane < nc) {
-    const int2 se = cell_se[r0 + ca + lane];
-    cnt = se.y - se.x;
+  const int cell = ca + lane;
+  int2 se = make_int2(0, 0);
+  if (cell < cb) se = cell_se[r0 + cell];
+  const int cnt = (cell < cb) ? se.y - se.x : 0;
+  int rank = 0;
+#pragma unroll 8
+  for (int o = 0; o < 32; ++o) {
+    const int co = __shfl_sync(0xffffffffu, cnt, o);
+    rank += (co > cnt) || (co == cnt && o < lane);
   }
-  int incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
+  if (cnt > 0) {
+    s_cell[rank] = cell;
+    s_beg[rank] = se.x - pa;
+    s_cnt[rank] = cnt;
   }
-  const int excl = incl - cnt;
-  const int np = __shfl_sync(0xffffffffu, incl, 31);
-  s_off[lane] = pa + excl;
-  if (lane == 31) s_off[32] = pa + np;
-  const int owner = lane < nc ? (np > 0 ? (int)(((int64_t)excl * kPoolWarps) / np) : 0) : kPoolWarps;
-#pragma unroll
-  for (int w = 0; w <= kPoolWarps; ++w) {
-    const unsigned below = __ballot_sync(0xffffffffu, owner < w);
-    if (lane == 0) s_wc[w] = __popc(below);
-  }
+  const unsigned nz = __ballot_sync(0xffffffffu, cnt > 0);
+  if (lane == 0) *s_m = __popc(nz);
 }
 
 // Streams the permutation range [wa, wb) of one warp in 32-entry chunks with
@@ -385,108 +378,78 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
     const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_off[33];
-  __shared__ int s_wc[kPoolWarps + 1];
+  __shared__ int s_cell[kTileCells], s_beg[kTileCells], s_cnt[kTileCells];
+  __shared__ int s_m, s_next;
   const int e = blockIdx.x;
   if (e >= (int)hdr->total_pieces) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v0 = blockIdx.y * 32;
   const int nvs = min(32, nvec - v0);                // vectors in this slice
-  const int nvs_full = min(32, nvec);
-  const int chs_full = nvs_full * VE;                 // channel capacity per row
+  const int chs_full = min(32, nvec) * VE;           // channel capacity per row
   const int chs = nvs * VE;                           // channels in this slice
   const int row_f = tile_row_bytes(chs_full, 4) / 4;  // floats per acc row
   float* acc_s = reinterpret_cast<float*>(smem);      // [32][row_f]
-  constexpr bool kRingPath = (VE * sizeof(T) == 16);
+  uint32_t* s_perm = reinterpret_cast<uint32_t*>(smem + kTileCells * row_f * 4);  // [kPiecePoints]
 
   const int4 pc = pieces[e];
   const int64_t t = pc.x;
   const int ca = pc.y & 0xff, cb = pc.y >> 8;
+  const int pa = pc.z, np = pc.w - pc.z;
+  const bool staged = np <= kPiecePoints;  // else: one cell larger than a piece
   const int64_t b = t / tpb;
   const int64_t s0 = (t - b * tpb) * kTileCells;
   const uint32_t r0 = (uint32_t)(b * dhw + s0);
 
   for (int i = threadIdx.x; i < kTileCells * row_f / 4; i += kPoolThreads)
     reinterpret_cast<float4*>(acc_s)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (warp == 0) split_piece(cell_se, r0, ca, cb, pc.z, s_off, s_wc);
+  if (staged)
+    for (int i = threadIdx.x; i < np; i += kPoolThreads) s_perm[i] = __ldg(perm + pa + i);
+  if (warp == 0) order_piece_cells(cell_se, r0, ca, cb, pa, s_cell, s_beg, s_cnt, &s_m);
+  if (threadIdx.x == 0) s_next = 0;
   __syncthreads();
 
   const bool active = lane < nvs;
   const T* fbase = feats + (int64_t)(v0 + lane) * VE;
-  int c = s_wc[warp];
-  const int ce = s_wc[warp + 1];
-  const int wa = s_off[c], wb = s_off[ce];
-  if (wa < wb) {
+  const int m = s_m;
+  for (;;) {
+    int i = 0;
+    if (lane == 0) i = atomicAdd(&s_next, 1);
+    i = __shfl_sync(0xffffffffu, i, 0);
+    if (i >= m) break;
+    const int cell = s_cell[i], beg = s_beg[i], cnt = s_cnt[i];
     PermStream ps;
-    ps.init(perm, wa, wb, lane);
-    while (s_off[c + 1] == wa) ++c;  // first non-empty cell
-    int cend = s_off[c + 1];
+    if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
     float acc[VE];
 #pragma unroll
     for (int q = 0; q < VE; ++q) acc[q] = 0.f;
-    if constexpr (kRingPath) {
-      // register double buffering: batch bi+1's rows are in flight while
-      // batch bi is summed (ascending point order within every cell)
-      constexpr int U = (sizeof(T) == 4) ? 8 : 4;
-      float vb[2][U][VE];
-      auto load = [&](int q0, float (&dst)[U][VE]) {
+    for (int k = 0; k < cnt; k += kUnroll) {
+      float v[kUnroll][VE];
 #pragma unroll
-        for (int j = 0; j < U; ++j) {
-          const uint32_t pid = ps.at(q0 + j, lane);
-          if (q0 + j < wb && active) {
-            VecIO<T, VE>::load(fbase + (int64_t)pid * C, dst[j]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < VE; ++q) dst[j][q] = 0.f;
-          }
+      for (int u = 0; u < kUnroll; ++u) {
+        uint32_t pid = 0;
+        if (staged) {
+          if (k + u < cnt) pid = s_perm[beg + k + u];
+        } else {
+          pid = ps.at(pa + beg + k + u, lane);
         }
-      };
-      load(wa, vb[0]);
-      int cur = 0;
-      for (int p0 = wa; p0 < wb; p0 += U) {
-        if (p0 + U < wb) {
-          if (cur == 0) load(p0 + U, vb[1]); else load(p0 + U, vb[0]);
+        if (k + u < cnt && active) {
+          VecIO<T, VE>::load(fbase + (int64_t)pid * C, v[u]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
         }
-#pragma unroll
-        for (int j = 0; j < U; ++j) {
-          const int p = p0 + j;
-          if (p < wb) {
-            if (p == cend) {
-              if (active) {
-                float* dst = acc_s + (ca + c) * row_f + lane * VE;
-#pragma unroll
-                for (int q = 0; q < VE; ++q) dst[q] = acc[q];
-              }
-#pragma unroll
-              for (int q = 0; q < VE; ++q) acc[q] = 0.f;
-              do { ++c; } while (s_off[c + 1] == p);
-              cend = s_off[c + 1];
-            }
-#pragma unroll
-            for (int q = 0; q < VE; ++q) acc[q] += (cur == 0 ? vb[0][j][q] : vb[1][j][q]);
-          }
-        }
-        cur ^= 1;
       }
-    } else {
-      for (int p = wa; p < wb; ++p) {
-        if (p == cend) {
-          if (active) acc_s[(ca + c) * row_f + lane * VE] = acc[0];
-          acc[0] = 0.f;
-          do { ++c; } while (s_off[c + 1] == p);
-          cend = s_off[c + 1];
-        }
-        const uint32_t pid = ps.at(p, lane);
-        if (active) {
-          float v[VE];
-          VecIO<T, VE>::load(fbase + (int64_t)pid * C, v);
+      // ascending point order, one fp32 add per element per point
 #pragma unroll
-          for (int q = 0; q < VE; ++q) acc[q] += v[q];
+      for (int u = 0; u < kUnroll; ++u) {
+        if (k + u < cnt) {
+#pragma unroll
+          for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
         }
       }
     }
     if (active) {
-      float* dst = acc_s + (ca + c) * row_f + lane * VE;
+      float* dst = acc_s + cell * row_f + lane * VE;
 #pragma unroll
       for (int q = 0; q < VE; ++q) dst[q] = acc[q];
     }
@@ -539,8 +502,8 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
     const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ gfeat) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_off[33];
-  __shared__ int s_wc[kPoolWarps + 1];
+  __shared__ int s_cell[kTileCells], s_beg[kTileCells], s_cnt[kTileCells];
+  __shared__ int s_m, s_next;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v0 = blockIdx.y * 32;
   const int nvs = min(32, nvec - v0);
@@ -571,7 +534,13 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
   const int64_t s0 = (t - b * tpb) * kTileCells;
   const uint32_t r0 = (uint32_t)(b * dhw + s0);
 
-  if (warp == 0) split_piece(cell_se, r0, ca, cb, pc.z, s_off, s_wc);
+  const int pa = pc.z, np = pc.w - pc.z;
+  const bool staged = np <= kPiecePoints;
+  uint32_t* s_perm = reinterpret_cast<uint32_t*>(smem + kTileCells * row_b);
+  if (staged)
+    for (int i = threadIdx.x; i < np; i += kPoolThreads) s_perm[i] = __ldg(perm + pa + i);
+  if (warp == 0) order_piece_cells(cell_se, r0, ca, cb, pa, s_cell, s_beg, s_cnt, &s_m);
+  if (threadIdx.x == 0) s_next = 0;
 
   // stage grad_out[b, c0 + ch, s0 + cell] -> smem[cell][ch], 4 channels per
   // access; skip 8-cell (32-byte) groups without points
@@ -600,24 +569,28 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
   }
   __syncthreads();
 
-  int c = s_wc[warp];
-  const int ce = s_wc[warp + 1];
-  const int wa = s_off[c], wb = s_off[ce];
-  if (wa >= wb) return;
-  PermStream ps;
-  ps.init(perm, wa, wb, lane);
-  while (s_off[c + 1] == wa) ++c;
-  int cend = s_off[c + 1];
-  const T* row = reinterpret_cast<const T*>(smem + (ca + c) * row_b) + lane * VE;
+  const int m = s_m;
+  for (;;) {
+    int i = 0;
+    if (lane == 0) i = atomicAdd(&s_next, 1);
+    i = __shfl_sync(0xffffffffu, i, 0);
+    if (i >= m) break;
+    const int cl = s_cell[i], beg = s_beg[i], cnt = s_cnt[i];
+    const T* row = reinterpret_cast<const T*>(smem + cl * row_b) + lane * VE;
+    if (staged) {
 #pragma unroll 4
-  for (int p = wa; p < wb; ++p) {
-    if (p == cend) {
-      do { ++c; } while (s_off[c + 1] == p);
-      cend = s_off[c + 1];
-      row = reinterpret_cast<const T*>(smem + (ca + c) * row_b) + lane * VE;
+      for (int k = 0; k < cnt; ++k) {
+        const uint32_t pid = s_perm[beg + k];
+        if (active) RowIO<T, VE>::copy(row, gbase + (int64_t)pid * C);
+      }
+    } else {
+      PermStream ps;
+      ps.init(perm, pa + beg, pa + beg + cnt, lane);
+      for (int k = 0; k < cnt; ++k) {
+        const uint32_t pid = ps.at(pa + beg + k, lane);
+        if (active) RowIO<T, VE>::copy(row, gbase + (int64_t)pid * C);
+      }
     }
-    const uint32_t pid = ps.at(p, lane);
-    if (active) RowIO<T, VE>::copy(row, gbase + (int64_t)pid * C);
   }
 }
 
@@ -630,7 +603,7 @@ int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& 
   const int nvec = (int)(C / VE);
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
-  size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4);
+  const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4) + kPiecePoints * sizeof(uint32_t);
   if (smem > 48 * 1024)
     BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
@@ -647,7 +620,7 @@ int launch_bwd(const void* gout, int64_t C, const Geometry& g, const PlanView& p
   const int nvec = (int)(C / VE);
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
-  const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, sizeof(T));
+  const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, sizeof(T)) + kPiecePoints * sizeof(uint32_t);
   if (smem > 48 * 1024)
     BFB_CUDA(cudaFuncSetAttribute(bev_bwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)(g.max_pieces + ceil_div(g.n, kPiecePoints)), (unsigned)slices);
