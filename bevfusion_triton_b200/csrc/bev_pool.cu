@@ -140,48 +140,58 @@ __global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
     PlanHeader* hdr) {
   extern __shared__ uint32_t s_hist[];
   const int nd = 1 << bits0;
-  for (int i = threadIdx.x; i < nd; i += kRadixThreads) s_hist[i] = 0;
+  for (int i = threadIdx.x; i < skewed_size(nd); i += kRadixThreads) s_hist[i] = 0;
   __syncthreads();
   const uint32_t sentinel = (uint32_t)(B * D * H * W);
   const int64_t base = (int64_t)blockIdx.x * kRadixTile;
   const int64_t end = min(n, base + kRadixTile);
   uint32_t bad = 0;
-  for (int64_t p0 = base; p0 < end; p0 += kRadixThreads) {
-    const int64_t p = p0 + threadIdx.x;
-    uint32_t digit = 0u;
-    if (p < end) {
-      int64_t x, y, z, b;
-      load_coord<IT>(coords, p, x, y, z, b);
-      const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W &&
-                      (uint64_t)z < (uint64_t)D && (uint64_t)b < (uint64_t)B;
-      const uint32_t k = ok ? (uint32_t)(((b * D + z) * H + x) * W + y) : sentinel;
-      bad += ok ? 0u : 1u;
-      keys[p] = k;
-      digit = k & ((1u << bits0) - 1u);
-    }
-    radix_count_aggregated(s_hist, digit, bits0, p < end);
+  for (int64_t p = base + threadIdx.x; p < end; p += kRadixThreads) {
+    int64_t x, y, z, b;
+    load_coord<IT>(coords, p, x, y, z, b);
+    const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W &&
+                    (uint64_t)z < (uint64_t)D && (uint64_t)b < (uint64_t)B;
+    const uint32_t k = ok ? (uint32_t)(((b * D + z) * H + x) * W + y) : sentinel;
+    bad += ok ? 0u : 1u;
+    keys[p] = k;
+    atomicAdd(&s_hist[skew((int)(k & ((1u << bits0) - 1u)))], 1u);
   }
   // one atomic per warp for the dropped-point counter
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(&hdr->n_invalid, bad);
   __syncthreads();
-  for (int d = threadIdx.x; d < nd; d += kRadixThreads) hist[(int64_t)d * ntiles + blockIdx.x] = s_hist[d];
+  for (int d = threadIdx.x; d < nd; d += kRadixThreads) hist[(int64_t)d * ntiles + blockIdx.x] = s_hist[skew(d)];
 }
 
 // ---------------------------------------------------------------------------
 // 3. per-cell [start, end) in the sorted order; number of in-grid points
 // ---------------------------------------------------------------------------
+// Four consecutive sorted keys per thread (one 16-byte load).
 __global__ void bev_bounds_kernel(const uint32_t* __restrict__ keys, int64_t n, uint32_t sentinel,
                                   int2* __restrict__ cell_se, PlanHeader* hdr) {
-  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= n) return;
-  const uint32_t k = keys[p];
-  const bool first = (p == 0) || keys[p - 1] != k;
-  const bool last = (p == n - 1) || keys[p + 1] != k;
-  if (first) cell_se[k].x = (int)p;
-  if (last) cell_se[k].y = (int)(p + 1);
-  if (k != sentinel && last && (p == n - 1 || keys[p + 1] == sentinel)) hdr->n_valid = (uint32_t)(p + 1);
+  const int64_t p0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (p0 >= n) return;
+  uint32_t k[6];  // k[0] = key before p0, k[1..4] = keys p0..p0+3, k[5] = key after
+  k[0] = p0 > 0 ? __ldg(keys + p0 - 1) : 0xffffffffu;
+  if (p0 + 4 <= n) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(keys + p0));
+    k[1] = q.x; k[2] = q.y; k[3] = q.z; k[4] = q.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) k[1 + i] = p0 + i < n ? __ldg(keys + p0 + i) : 0xffffffffu;
+  }
+  k[5] = p0 + 4 < n ? __ldg(keys + p0 + 4) : 0xffffffffu;
+#pragma unroll
+  for (int i = 1; i <= 4; ++i) {
+    const int64_t p = p0 + i - 1;
+    if (p >= n) break;
+    const bool first = (p == 0) || k[i - 1] != k[i];
+    const bool last = (p == n - 1) || k[i + 1] != k[i];
+    if (first) cell_se[k[i]].x = (int)p;
+    if (last) cell_se[k[i]].y = (int)(p + 1);
+    if (k[i] != sentinel && last && (p == n - 1 || k[i + 1] == sentinel)) hdr->n_valid = (uint32_t)(p + 1);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -710,7 +720,7 @@ extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64
   uint32_t* keys_sorted = sv.keys0;
   if (n > 0) {
     const int64_t ntiles = radix_tiles(n);
-    const size_t hsm = sizeof(uint32_t) << rp.digit_bits[0];
+    const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
     if (itype == BFB_I32)
       bev_keys_kernel<int32_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
           static_cast<const int32_t*>(coords), n, B, D, H, W, sv.keys0, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
@@ -723,7 +733,7 @@ extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64
   }
   BFB_CUDA(cudaMemsetAsync(pv.cell_se, 0, sizeof(int2) * (size_t)(g.cells + 1), st));
   if (n > 0) {
-    bev_bounds_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(keys_sorted, n, (uint32_t)g.cells,
+    bev_bounds_kernel<<<(unsigned)ceil_div(ceil_div(n, 4), 256), 256, 0, st>>>(keys_sorted, n, (uint32_t)g.cells,
                                                                   pv.cell_se, pv.hdr);
     BFB_CHECK_LAUNCH();
   }

@@ -29,85 +29,133 @@ __global__ __launch_bounds__(kRadixThreads) void radix_upsweep_kernel(const uint
                                                                       int64_t ntiles) {
   extern __shared__ uint32_t s_hist[];
   const int nd = 1 << bits;
-  for (int i = threadIdx.x; i < nd; i += kRadixThreads) s_hist[i] = 0;
+  for (int i = threadIdx.x; i < skewed_size(nd); i += kRadixThreads) s_hist[i] = 0;
   __syncthreads();
   const int64_t base = (int64_t)blockIdx.x * kRadixTile;
   const int64_t end = min(n, base + kRadixTile);
-  for (int64_t p0 = base; p0 < end; p0 += kRadixThreads) {
-    const int64_t p = p0 + threadIdx.x;
-    const bool valid = p < end;
-    radix_count_aggregated(s_hist, valid ? ((__ldg(keys + p) >> shift) & (nd - 1)) : 0u, bits, valid);
-  }
+  for (int64_t p = base + threadIdx.x; p < end; p += kRadixThreads)
+    atomicAdd(&s_hist[skew((int)((__ldg(keys + p) >> shift) & (nd - 1)))], 1u);
   __syncthreads();
-  for (int d = threadIdx.x; d < nd; d += kRadixThreads) hist[(int64_t)d * ntiles + blockIdx.x] = s_hist[d];
+  for (int d = threadIdx.x; d < nd; d += kRadixThreads) hist[(int64_t)d * ntiles + blockIdx.x] = s_hist[skew(d)];
 }
 
-__global__ __launch_bounds__(kRadixThreads) void radix_downsweep_kernel(
+// Stable scatter of one tile.  Each warp owns 1024 consecutive elements,
+// held in registers as 32 steps of 32 lanes, and a private (skewed) row of
+// digit counters.  Elements are first ranked within the tile (digit-major,
+// input order within a digit) into shared memory, then every digit's run is
+// written to its global slot with consecutive threads on consecutive
+// addresses, so global writes are whole sectors.
+__global__ __launch_bounds__(kRadixThreads, 1) void radix_downsweep_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     int bits, const uint32_t* __restrict__ hist, int64_t ntiles) {
-  extern __shared__ uint32_t s_off[];  // [kRadixWarps][nd]
+  constexpr int kSteps = kRadixWarpItems / 32;
+  extern __shared__ __align__(16) uint32_t smem_u32[];
   const int nd = 1 << bits;
+  const int row = skewed_size(nd);
+  uint32_t* s_off = smem_u32;                        // [kRadixWarps][row]
+  uint32_t* s_key = s_off + kRadixWarps * row;       // [kRadixTile]
+  uint32_t* s_val = s_key + kRadixTile;              // [kRadixTile]
+  uint32_t* s_gbase = s_val + kRadixTile;            // [row] global digit start - local start
+  __shared__ uint32_t s_ws[kRadixWarps];
   const uint32_t dmask = (uint32_t)nd - 1u;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < kRadixWarps * nd; i += kRadixThreads) s_off[i] = 0;
-  __syncthreads();
+  for (int i = threadIdx.x; i < kRadixWarps * row; i += kRadixThreads) s_off[i] = 0;
 
-  const int64_t start = (int64_t)blockIdx.x * kRadixTile + (int64_t)warp * kRadixWarpItems;
-  const int64_t end = min(n, start + kRadixWarpItems);
-  uint32_t* my = s_off + warp * nd;
-
-  // A: per-warp digit counts; one leader per distinct digit in a step updates
-  // the warp-private row (input order clusters equal digits, so per-lane
-  // shared atomics would serialise)
-  {
-    const unsigned lt = lanemask_lt();
-    for (int64_t base = start; base < end; base += 32) {
-      const int64_t p = base + lane;
-      const bool valid = p < end;
-      const uint32_t d = valid ? ((__ldg(keys_in + p) >> shift) & dmask) : 0u;
-      const unsigned peers = digit_peers(d, bits, valid);
-      if (valid && (peers & lt) == 0) my[d] += __popc(peers);
-      __syncwarp();
-    }
-  }
-  __syncthreads();
-
-  // B: per-warp starting offsets = global (digit, tile) offset + counts of
-  // earlier warps in this tile
-  for (int d = threadIdx.x; d < nd; d += kRadixThreads) {
-    uint32_t run = hist[(int64_t)d * ntiles + blockIdx.x];
+  const int64_t tile0 = (int64_t)blockIdx.x * kRadixTile;
+  const int tile_n = (int)min((int64_t)kRadixTile, n - tile0);
+  const int64_t start = tile0 + (int64_t)warp * kRadixWarpItems;
+  uint32_t k[kSteps];
 #pragma unroll
-    for (int w = 0; w < kRadixWarps; ++w) {
-      uint32_t c = s_off[w * nd + d];
-      s_off[w * nd + d] = run;
-      run += c;
-    }
+  for (int j = 0; j < kSteps; ++j) {
+    const int64_t p = start + j * 32 + lane;
+    k[j] = p < n ? __ldg(keys_in + p) : 0xffffffffu;
+  }
+  uint32_t* my = s_off + warp * row;
+  const unsigned lt = lanemask_lt();
+  __syncthreads();
+
+  // A: per-warp digit counts; one leader per distinct digit in a step
+#pragma unroll
+  for (int j = 0; j < kSteps; ++j) {
+    const bool valid = start + j * 32 + lane < n;
+    const uint32_t d = (k[j] >> shift) & dmask;
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+    if (valid && (peers & lt) == 0) my[skew((int)d)] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
 
-  // C: stable scatter, 32 consecutive elements per step
-  const unsigned lt = lanemask_lt();
-  for (int64_t base = start; base < end; base += 32) {
-    const int64_t p = base + lane;
-    const bool valid = p < end;
-    uint32_t k = 0, v = 0;
-    if (valid) {
-      k = __ldg(keys_in + p);
-      v = vals_in ? __ldg(vals_in + p) : (uint32_t)p;
+  // B: tile totals per digit -> tile-local digit starts (block scan over
+  // digits, up to two digits per thread) and per-warp local offsets
+  const int per_thread = (nd + kRadixThreads - 1) / kRadixThreads;  // 1 or 2
+  uint32_t tot[2] = {0u, 0u};
+  for (int q = 0; q < per_thread; ++q) {
+    const int d = threadIdx.x * per_thread + q;
+    if (d < nd)
+      for (int w = 0; w < kRadixWarps; ++w) tot[q] += s_off[w * row + skew(d)];
+  }
+  {
+    const uint32_t mine = tot[0] + tot[1];
+    uint32_t x = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
     }
-    const uint32_t d = valid ? ((k >> shift) & dmask) : 0u;
-    const unsigned peers = digit_peers(d, bits, valid);
+    if (lane == 31) s_ws[warp] = x;
+    __syncthreads();
+    uint32_t wp = 0;
+    for (int w = 0; w < warp; ++w) wp += s_ws[w];
+    uint32_t run = wp + x - mine;  // exclusive prefix of this thread's first digit
+    for (int q = 0; q < per_thread; ++q) {
+      const int d = threadIdx.x * per_thread + q;
+      if (d < nd) {
+        const int sd = skew(d);
+        s_gbase[sd] = hist[(int64_t)d * ntiles + blockIdx.x] - run;
+        uint32_t r2 = run;
+        for (int w = 0; w < kRadixWarps; ++w) {
+          const uint32_t c = s_off[w * row + sd];
+          s_off[w * row + sd] = r2;
+          r2 += c;
+        }
+        run += tot[q];
+      }
+    }
+  }
+  uint32_t v[kSteps];
+#pragma unroll
+  for (int j = 0; j < kSteps; ++j) {
+    const int64_t p = start + j * 32 + lane;
+    v[j] = vals_in ? (p < n ? __ldg(vals_in + p) : 0u) : (uint32_t)p;
+  }
+  __syncthreads();
+
+  // C: stable rank within the tile -> shared memory
+#pragma unroll
+  for (int j = 0; j < kSteps; ++j) {
+    const bool valid = start + j * 32 + lane < n;
+    const uint32_t d = (k[j] >> shift) & dmask;
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
     const uint32_t rank = __popc(peers & lt);
-    uint32_t pos = 0;
+    const int sd = skew((int)d);
     if (valid) {
-      pos = my[d] + rank;
-      keys_out[pos] = k;
-      vals_out[pos] = v;
+      const uint32_t pos = my[sd] + rank;
+      s_key[pos] = k[j];
+      s_val[pos] = v[j];
     }
     __syncwarp();
-    if (valid && rank == 0) my[d] += __popc(peers);
+    if (valid && rank == 0) my[sd] += __popc(peers);
     __syncwarp();
+  }
+  __syncthreads();
+
+  // D: digit runs to global memory, consecutive threads -> consecutive slots
+  for (int i = threadIdx.x; i < tile_n; i += kRadixThreads) {
+    const uint32_t key = s_key[i];
+    const uint32_t pos = s_gbase[skew((int)((key >> shift) & dmask))] + (uint32_t)i;
+    keys_out[pos] = key;
+    vals_out[pos] = s_val[i];
   }
 }
 
@@ -129,12 +177,13 @@ int radix_sort_index(uint32_t* keys0, uint32_t* keys1, uint32_t* vals_tmp, uint3
     uint32_t* kout = kbuf[(ps + 1) & 1];
     uint32_t* vout = ((plan.passes - 1 - ps) & 1) ? vals_tmp : vals_out;
     if (!(ps == 0 && hist0_ready)) {
-      radix_upsweep_kernel<<<(unsigned)ntiles, kRadixThreads, nd * sizeof(uint32_t), stream>>>(
+      radix_upsweep_kernel<<<(unsigned)ntiles, kRadixThreads, skewed_size(nd) * sizeof(uint32_t), stream>>>(
           kin, n, shift, bits, hist, ntiles);
       BFB_CHECK_LAUNCH();
     }
     BFB_TRY(exclusive_scan_u32(hist, hist, (int64_t)nd * ntiles, scan_scratch, nullptr, stream));
-    const size_t smem = (size_t)kRadixWarps * nd * sizeof(uint32_t);
+    const size_t smem = ((size_t)kRadixWarps * skewed_size(nd) + 2 * (size_t)kRadixTile + skewed_size(nd)) *
+                        sizeof(uint32_t);
     if (smem > 48 * 1024)
       BFB_CUDA(cudaFuncSetAttribute(radix_downsweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem));

@@ -18,6 +18,13 @@ constexpr int kRadixWarpItems = 1024;                  // per warp
 constexpr int kRadixTile = kRadixWarps * kRadixWarpItems;  // 16384
 constexpr int kRadixMaxBits = 10;                      // digit width
 
+// Shared-memory slot of digit d in a per-warp / per-block counter array: one
+// padding word per 32 digits, so digits that differ by a multiple of 32 (keys
+// that step along a grid row of a multiple-of-32 width) land in different
+// banks.
+__host__ __device__ __forceinline__ int skew(int d) { return d + (d >> 5); }
+__host__ __device__ __forceinline__ int skewed_size(int nd) { return nd + (nd >> 5); }
+
 struct RadixPlan {
   int passes = 0;
   int digit_bits[4] = {0, 0, 0, 0};
@@ -44,23 +51,5 @@ inline size_t radix_hist_elems(int64_t n, const RadixPlan& p) {
 int radix_sort_index(uint32_t* keys0, uint32_t* keys1, uint32_t* vals_tmp, uint32_t* vals_out,
                      int64_t n, const RadixPlan& plan, uint32_t* hist, uint32_t* scan_scratch,
                      bool hist0_ready, cudaStream_t stream, uint32_t** keys_sorted);
-
-// Lanes of the warp whose digit equals this lane's.  Invalid lanes pass
-// valid = false and get an empty mask.
-__device__ __forceinline__ unsigned digit_peers(uint32_t d, int bits, bool valid) {
-  (void)bits;
-  const unsigned m = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
-  return valid ? m : 0u;
-}
-
-// Warp-aggregated shared histogram increment: lanes holding the same digit
-// elect one leader that adds the group size.  Every lane of the warp must
-// call it; lanes with valid = false contribute nothing.
-__device__ __forceinline__ void radix_count_aggregated(uint32_t* s_hist, uint32_t digit, int bits, bool valid) {
-  const unsigned peers = digit_peers(digit, bits, valid);
-  unsigned lt;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
-  if (valid && (peers & lt) == 0) atomicAdd(&s_hist[digit], (uint32_t)__popc(peers));
-}
 
 }  // namespace bfb

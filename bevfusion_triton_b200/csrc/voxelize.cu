@@ -18,9 +18,9 @@
 //   vox_assign   per first point: keep / drop against max_voxels, write coors and
 //                num_points, record the voxel's table slot and member count
 //   vox_fill     bucket every kept point by voxel (slots from a scan of the counts)
-//   vox_emit     a warp per voxel: order its members ascending (bitonic sort, or
-//                repeated minimum selection for large voxels), write the [P, F] row with
-//                zero padding, and reset the voxel's table slot
+//   vox_emit     32 voxels per warp: rank each voxel's members (input order) in shared
+//                memory (repeated minimum selection for voxels above 32 points), write
+//                the [P, F] rows with zero padding, and reset each voxel's table slot
 // The table therefore stays clean between calls: it is initialised once
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
@@ -283,63 +283,88 @@ __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __
   if (g >= 0) members[base + __popc(peers & lanemask_lt())] = (uint32_t)p;
 }
 
-// Ascending bitonic sort of one value per lane.
-__device__ __forceinline__ uint32_t warp_sort_asc(uint32_t v) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j);
-      const bool up = ((lane & k) == 0);
-      const bool lower = (lane & j) == 0;
-      v = (lower == up) ? min(v, o) : max(v, o);
-    }
-  }
-  return v;
-}
+constexpr int kEmitWarps = 4;
+constexpr int kFastMembers = 32;  // voxels with more points take the warp-cooperative path
 
+// Writes voxel rows.  A warp takes 32 consecutive voxel ids at a time, one per
+// lane: the lane ranks its voxel's members (rank = number of smaller point
+// indices, i.e. input order) in shared memory; then the warp writes the rows
+// one voxel after the other, each row with coalesced stores.  Voxels with more
+// than 32 points are done by the whole warp with repeated minimum selection.
+// Every voxel's table slot is reset on the way.
 template <class T>
-__global__ __launch_bounds__(kVoxThreads) void vox_emit_kernel(
+__global__ __launch_bounds__(kEmitWarps * 32) void vox_emit_kernel(
     const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, TableView tb,
     const uint32_t* __restrict__ gcnt, const uint32_t* __restrict__ cursor, const int32_t* __restrict__ gslot,
     const int2* __restrict__ vinfo, const uint32_t* __restrict__ members, int64_t P, int64_t max_voxels,
     T* __restrict__ voxels) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  __shared__ uint32_t s_mem[kEmitWarps][32][kFastMembers + 1];
+  __shared__ uint32_t s_sorted[kEmitWarps][32][kFastMembers + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t)gridDim.x * kEmitWarps;
   const int64_t total = *total_dev;
   const int64_t row_len = P * f;
-  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < total; g += warps) {
-    const int32_t slot = gslot[g];
-    const uint32_t cnt = gcnt[g];
-    if (lane == 0) {  // leave the table clean for the next call
-      tb.keys[slot] = kEmptyKey;
+  const int fi = (int)f;
+  uint32_t(*mem)[kFastMembers + 1] = s_mem[warp];
+  uint32_t(*srt)[kFastMembers + 1] = s_sorted[warp];
+  for (int64_t g0 = gw * 32; g0 < total; g0 += nwarps * 32) {
+    const int64_t g = g0 + lane;
+    uint32_t cnt = 0, end = 0;
+    int2 vi = make_int2(0, 0);
+    if (g < total) {
+      const int32_t slot = gslot[g];
+      tb.keys[slot] = kEmptyKey;  // leave the table clean for the next call
       tb.first[slot] = kNoFirst;
       tb.cnt[slot] = 0u;
+      cnt = gcnt[g];
+      end = cursor[g];
+      vi = vinfo[g];
     }
-    if (cnt == 0) continue;  // voxel beyond max_voxels
-    const int2 vi = vinfo[g];
-    const uint32_t end = cursor[g];
-    const uint32_t start = end - cnt;
-    T* dst = voxels + ((int64_t)vi.x * max_voxels + vi.y) * row_len;
-    const int64_t keep = min((int64_t)cnt, P);
-    if (cnt <= 32) {
-      uint32_t m = lane < (int)cnt ? members[start + lane] : 0xffffffffu;
-      m = warp_sort_asc(m);
-      for (int64_t base = 0; base < row_len; base += 32) {  // warp-uniform trip count
-        const int64_t idx = base + lane;
-        const int64_t j = idx / f, q = idx - j * f;
-        const uint32_t src = __shfl_sync(0xffffffffu, m, (int)(j & 31));
-        if (idx < row_len) dst[idx] = j < keep ? pts[(int64_t)src * f + q] : from_f32<T>(0.f);
+    const bool fast = cnt > 0 && cnt <= (uint32_t)kFastMembers;
+    if (fast) {
+      const uint32_t start = end - cnt;
+      for (uint32_t i = 0; i < cnt; ++i) mem[lane][i] = members[start + i];
+      for (uint32_t i = 0; i < cnt; ++i) {
+        const uint32_t mi = mem[lane][i];
+        uint32_t r = 0;
+        for (uint32_t j = 0; j < cnt; ++j) r += mem[lane][j] < mi;
+        srt[lane][r] = mi;
       }
-    } else {
-      // repeated minimum selection: O(keep * cnt / 32), exact input order
+    }
+    __syncwarp();
+    unsigned todo = __ballot_sync(0xffffffffu, fast);
+    while (todo) {
+      const int v = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const uint32_t cv = __shfl_sync(0xffffffffu, cnt, v);
+      const int sx = __shfl_sync(0xffffffffu, vi.x, v);
+      const int sy = __shfl_sync(0xffffffffu, vi.y, v);
+      T* dst = voxels + ((int64_t)sx * max_voxels + sy) * row_len;
+      const int keep = (int)min((int64_t)cv, P);
+      for (int idx = lane; idx < (int)row_len; idx += 32) {
+        const int j = idx / fi, q = idx - j * fi;
+        dst[idx] = j < keep ? pts[(int64_t)srt[v][j] * f + q] : from_f32<T>(0.f);
+      }
+    }
+    __syncwarp();
+    unsigned big = __ballot_sync(0xffffffffu, cnt > (uint32_t)kFastMembers);
+    while (big) {
+      const int b = __ffs(big) - 1;
+      big &= big - 1;
+      const uint32_t bc = __shfl_sync(0xffffffffu, cnt, b);
+      const uint32_t be = __shfl_sync(0xffffffffu, end, b);
+      const int bx = __shfl_sync(0xffffffffu, vi.x, b);
+      const int by = __shfl_sync(0xffffffffu, vi.y, b);
+      const uint32_t bs = be - bc;
+      T* dst = voxels + ((int64_t)bx * max_voxels + by) * row_len;
+      const int64_t keep = min((int64_t)bc, P);
       uint32_t last = 0;
       for (int64_t j = 0; j < keep; ++j) {
         uint32_t best = 0xffffffffu;
-        for (uint32_t i = start + lane; i < end; i += 32) {
-          const uint32_t v = members[i];
-          if ((j == 0 || v > last) && v < best) best = v;
+        for (uint32_t i = bs + lane; i < be; i += 32) {
+          const uint32_t m = members[i];
+          if ((j == 0 || m > last) && m < best) best = m;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
@@ -406,8 +431,9 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
     BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n, sv.scan, nullptr, st));
     vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members);
     BFB_CHECK_LAUNCH();
-    vox_emit_kernel<T><<<kEmitBlocks, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot,
-                                                            sv.vinfo, sv.members, P, MV, static_cast<T*>(voxels));
+    vox_emit_kernel<T><<<kEmitBlocks, kEmitWarps * 32, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor,
+                                                                sv.gslot, sv.vinfo, sv.members, P, MV,
+                                                                static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
   }
   if (zero_tail) {
