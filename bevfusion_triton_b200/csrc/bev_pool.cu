@@ -26,6 +26,8 @@
 //                             cell), then a warp per cell keeps the cell's gradient
 //                             row in registers and stores it to each of the cell's
 //                             points with 16-byte stores; dropped points get 0 rows.
+#include <mutex>
+
 #include "radix.cuh"
 #include "scan.cuh"
 
@@ -799,3 +801,51 @@ extern "C" int bfb_bev_pool_invalid_count(const void* plan, int64_t* count, void
   *count = v;
   return BFB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Forward without any allocation, for callers that cannot call cudaMalloc.
+//
+// The plan and scratch live in one fixed file-scope device array of
+// kNoAllocBytes (64 MiB), which every GPU that loads this library holds until
+// the process exits.  Host code may not pass the array's name to a kernel (on
+// the host it is only a stand-in symbol), so its device address is looked up
+// with cudaGetSymbolAddress once per device, on that device's first call.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocBytes = size_t(64) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch_address(void** out) {
+  int dev = -1;
+  BFB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return BFB_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    BFB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return BFB_OK;
+}
+}  // namespace
+
+extern "C" int bfb_bev_pool_forward_noalloc(const void* feats, int dtype, const void* coords, int itype,
+                                            int64_t n, int64_t c, int64_t B, int64_t D, int64_t H, int64_t W,
+                                            void* out, void* stream) {
+  size_t plan_b = 0, scratch_b = 0;
+  BFB_TRY(bfb_bev_pool_workspace_sizes(n, c, B, D, H, W, &plan_b, &scratch_b));
+  plan_b = align_up(plan_b);
+  if (plan_b + scratch_b > kNoAllocBytes) return BFB_ERR_TOO_LARGE;
+  void* base = nullptr;
+  BFB_TRY(noalloc_scratch_address(&base));
+  char* p = static_cast<char*>(base);
+  return bfb_bev_pool_forward(feats, dtype, coords, itype, n, c, B, D, H, W, out, p, plan_b, p + plan_b,
+                              scratch_b, stream);
+}
+
+extern "C" size_t bfb_bev_pool_noalloc_capacity(void) { return kNoAllocBytes; }

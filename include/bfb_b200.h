@@ -108,6 +108,23 @@ int bfb_bev_pool_backward(const void* grad_out_dev, int dtype, int64_t n, int64_
                           int64_t D, int64_t H, int64_t W, const void* plan_dev,
                           size_t plan_bytes, void* grad_feats_dev, void* stream);
 
+/* bev_pool forward that allocates nothing and takes no workspace.  It has no
+ * counterpart in the reference.  It is for callers that cannot allocate GPU
+ * memory at call time -- code in a real-time loop where cudaMalloc would
+ * stall, or code that may not own an allocator -- and uses one fixed 64 MiB
+ * device array inside this library instead (held on every GPU that loads the
+ * library, until exit; bfb_bev_pool_noalloc_capacity() returns its size).
+ * Sizes whose plan + scratch exceed it are refused with BFB_ERR_TOO_LARGE
+ * (one det sample of 1.77 M points on a 360 x 360 grid fits).  The first call
+ * on a device looks up the array's device address, so make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (other streams, other threads) race, and the plan is not kept for a
+ * backward. */
+int bfb_bev_pool_forward_noalloc(const void* feats_dev, int feats_dtype, const void* coords_dev,
+                                 int coords_itype, int64_t n, int64_t c, int64_t B, int64_t D,
+                                 int64_t H, int64_t W, void* out_dev, void* stream);
+size_t bfb_bev_pool_noalloc_capacity(void);
+
 /* Synchronously reads how many points the plan dropped as out of range. */
 int bfb_bev_pool_invalid_count(const void* plan_dev, int64_t* count, void* stream);
 
