@@ -44,12 +44,12 @@ SAMPLES_PER_GPU = 8
 C = synth.CHANNELS
 FALLBACK_HBM_GBS = 6650.0
 
-# DRAM traffic (read + write bytes) of the dominant kernels from ncu, per unit
-# of work, from the captures summarised in profiles/ (scaled by the units a
-# launch processes).  None until captured.
+# DRAM traffic (read + write bytes) of the dominant kernels per point, from the
+# ncu capture of a one-sample launch summarised in profiles/; traffic grows in
+# proportion to the points, so a launch's traffic is this times its points.
 NCU_TRAFFIC_PER_POINT = {
-    'bev_fwd_kernel': None,
-    'bev_bwd_kernel': None,
+    'bev_fwd_kernel': 349.0,  # profiles/bev_fwd_bwd_kernels_det1.md
+    'bev_bwd_kernel': 313.0,
 }
 
 
