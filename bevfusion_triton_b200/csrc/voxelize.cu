@@ -18,9 +18,10 @@
 //   vox_assign   per first point: keep / drop against max_voxels, write coors and
 //                num_points, record the voxel's table slot and member count
 //   vox_fill     bucket every kept point by voxel (slots from a scan of the counts)
-//   vox_emit     32 voxels per warp: rank each voxel's members (input order) in shared
-//                memory (repeated minimum selection for voxels above 32 points), write
-//                the [P, F] rows with zero padding, and reset each voxel's table slot
+//   vox_rank     a thread per kept point: its slot = number of smaller point indices in
+//                its voxel's bucket (input order); points below max_points write their row
+//   vox_pad      a lane per voxel: zero the unused point slots, reset the table slot;
+//                voxels above 256 points are ordered by a whole warp (repeated minimum)
 // The table therefore stays clean between calls: it is initialised once
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
@@ -35,7 +36,6 @@ constexpr uint64_t kEmptyKey = ~0ull;
 constexpr uint32_t kNoFirst = 0xffffffffu;
 constexpr int kLinBits = 40;  // cell index bits inside a key; the rest hold the sample
 constexpr int kVoxThreads = 256;
-constexpr int kEmitBlocks = 148 * 8;
 
 struct TableView {
   uint64_t* keys;
@@ -76,7 +76,8 @@ struct VoxScratch {
   uint32_t* cursor;  // [n+1] bucket offsets (scan of gcnt), advanced to bucket ends by vox_fill
   int32_t* gslot;    // [n]   table slot per voxel
   int2* vinfo;       // [n]   (sample, voxel id within the sample)
-  uint32_t* members; // [n]
+  uint32_t* members; // [n]   point index per bucket slot
+  int32_t* mvox;     // [n]   voxel id per bucket slot
   uint32_t* scan;
   uint32_t* err;     // [4]   0: table full (insert gave up)
 };
@@ -91,6 +92,7 @@ size_t carve_scratch(void* base, int64_t n, int64_t batch, VoxScratch* v) {
   v->gslot = c.take<int32_t>((size_t)n);
   v->vinfo = c.take<int2>((size_t)n);
   v->members = c.take<uint32_t>((size_t)n);
+  v->mvox = c.take<int32_t>((size_t)n);
   v->scan = c.take<uint32_t>(scan_scratch_elems(n + 1));
   v->err = c.take<uint32_t>(4);
   return c.bytes();
@@ -267,7 +269,8 @@ __global__ void vox_count_kernel(const int64_t* __restrict__ offs, int batch, co
 __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __restrict__ slot_of, int64_t n,
                                                                const int32_t* __restrict__ gvid,
                                                                uint32_t* __restrict__ cursor,
-                                                               uint32_t* __restrict__ members) {
+                                                               uint32_t* __restrict__ members,
+                                                               int32_t* __restrict__ mvox) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int lane = threadIdx.x & 31;
   int32_t g = -1;
@@ -280,99 +283,94 @@ __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __
   uint32_t base = 0;
   if (g >= 0 && lane == leader) base = atomicAdd(cursor + g, (uint32_t)__popc(peers));
   base = __shfl_sync(0xffffffffu, base, leader);
-  if (g >= 0) members[base + __popc(peers & lanemask_lt())] = (uint32_t)p;
+  if (g >= 0) {
+    const uint32_t pos = base + __popc(peers & lanemask_lt());
+    members[pos] = (uint32_t)p;
+    mvox[pos] = g;
+  }
 }
 
-constexpr int kEmitWarps = 4;
-constexpr int kFastMembers = 32;  // voxels with more points take the warp-cooperative path
+constexpr int kRankMax = 256;  // voxels with more points are ordered by a whole warp
 
-// Writes voxel rows.  A warp takes 32 consecutive voxel ids at a time, one per
-// lane: the lane ranks its voxel's members (rank = number of smaller point
-// indices, i.e. input order) in shared memory; then the warp writes the rows
-// one voxel after the other, each row with coalesced stores.  Voxels with more
-// than 32 points are done by the whole warp with repeated minimum selection.
-// Every voxel's table slot is reset on the way.
+// One thread per kept point (bucket slot): its slot within the voxel is the
+// number of smaller point indices in the voxel's bucket, i.e. its rank in
+// input order; points ranked below P write their row.
 template <class T>
-__global__ __launch_bounds__(kEmitWarps * 32) void vox_emit_kernel(
+__global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
+    const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt,
+    const uint32_t* __restrict__ cursor, const int2* __restrict__ vinfo, const uint32_t* __restrict__ members,
+    const int32_t* __restrict__ mvox, int64_t P, int64_t max_voxels, T* __restrict__ voxels) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // kept points over the batch: the bucket offset one past the last voxel
+  // (vox_fill advances only the offsets of voxels that own points)
+  if (i >= (int64_t)cursor[*total_dev]) return;
+  const int32_t g = mvox[i];
+  const uint32_t cnt = gcnt[g];
+  if (cnt > (uint32_t)kRankMax) return;
+  const uint32_t end = cursor[g], start = end - cnt;
+  const uint32_t p = members[i];
+  uint32_t r = 0;
+  for (uint32_t j = start; j < end; ++j) r += __ldg(members + j) < p;
+  if ((int64_t)r >= P) return;
+  const int2 vi = vinfo[g];
+  T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + r) * f;
+  const T* src = pts + (int64_t)p * f;
+  for (int64_t q = 0; q < f; ++q) dst[q] = src[q];
+}
+
+// One lane per voxel: reset the voxel's table slot, zero its unused point
+// slots; voxels above kRankMax points are ordered by the whole warp with
+// repeated minimum selection (input order) and written here.
+template <class T>
+__global__ __launch_bounds__(kVoxThreads) void vox_pad_kernel(
     const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, TableView tb,
     const uint32_t* __restrict__ gcnt, const uint32_t* __restrict__ cursor, const int32_t* __restrict__ gslot,
     const int2* __restrict__ vinfo, const uint32_t* __restrict__ members, int64_t P, int64_t max_voxels,
     T* __restrict__ voxels) {
-  __shared__ uint32_t s_mem[kEmitWarps][32][kFastMembers + 1];
-  __shared__ uint32_t s_sorted[kEmitWarps][32][kFastMembers + 1];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (int64_t)gridDim.x * kEmitWarps;
+  const int lane = threadIdx.x & 31;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = *total_dev;
+  if (((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >= total) return;  // whole warp out of range
   const int64_t row_len = P * f;
-  const int fi = (int)f;
-  uint32_t(*mem)[kFastMembers + 1] = s_mem[warp];
-  uint32_t(*srt)[kFastMembers + 1] = s_sorted[warp];
-  for (int64_t g0 = gw * 32; g0 < total; g0 += nwarps * 32) {
-    const int64_t g = g0 + lane;
-    uint32_t cnt = 0, end = 0;
-    int2 vi = make_int2(0, 0);
-    if (g < total) {
-      const int32_t slot = gslot[g];
-      tb.keys[slot] = kEmptyKey;  // leave the table clean for the next call
-      tb.first[slot] = kNoFirst;
-      tb.cnt[slot] = 0u;
-      cnt = gcnt[g];
-      end = cursor[g];
-      vi = vinfo[g];
+  uint32_t cnt = 0, end = 0;
+  int2 vi = make_int2(0, 0);
+  if (g < total) {
+    const int32_t slot = gslot[g];
+    tb.keys[slot] = kEmptyKey;  // leave the table clean for the next call
+    tb.first[slot] = kNoFirst;
+    tb.cnt[slot] = 0u;
+    cnt = gcnt[g];
+    end = cursor[g];
+    vi = vinfo[g];
+    if (cnt > 0 && cnt <= (uint32_t)kRankMax && (int64_t)cnt < P) {
+      T* dst = voxels + ((int64_t)vi.x * max_voxels + vi.y) * row_len;
+      for (int64_t idx = (int64_t)cnt * f; idx < row_len; ++idx) dst[idx] = from_f32<T>(0.f);
     }
-    const bool fast = cnt > 0 && cnt <= (uint32_t)kFastMembers;
-    if (fast) {
-      const uint32_t start = end - cnt;
-      for (uint32_t i = 0; i < cnt; ++i) mem[lane][i] = members[start + i];
-      for (uint32_t i = 0; i < cnt; ++i) {
-        const uint32_t mi = mem[lane][i];
-        uint32_t r = 0;
-        for (uint32_t j = 0; j < cnt; ++j) r += mem[lane][j] < mi;
-        srt[lane][r] = mi;
+  }
+  unsigned big = __ballot_sync(0xffffffffu, cnt > (uint32_t)kRankMax);
+  while (big) {
+    const int b = __ffs(big) - 1;
+    big &= big - 1;
+    const uint32_t bc = __shfl_sync(0xffffffffu, cnt, b);
+    const uint32_t be = __shfl_sync(0xffffffffu, end, b);
+    const int bx = __shfl_sync(0xffffffffu, vi.x, b);
+    const int by = __shfl_sync(0xffffffffu, vi.y, b);
+    const uint32_t bs = be - bc;
+    T* dst = voxels + ((int64_t)bx * max_voxels + by) * row_len;
+    const int64_t keep = min((int64_t)bc, P);
+    uint32_t last = 0;
+    for (int64_t j = 0; j < keep; ++j) {
+      uint32_t best = 0xffffffffu;
+      for (uint32_t i = bs + lane; i < be; i += 32) {
+        const uint32_t m = members[i];
+        if ((j == 0 || m > last) && m < best) best = m;
       }
-    }
-    __syncwarp();
-    unsigned todo = __ballot_sync(0xffffffffu, fast);
-    while (todo) {
-      const int v = __ffs(todo) - 1;
-      todo &= todo - 1;
-      const uint32_t cv = __shfl_sync(0xffffffffu, cnt, v);
-      const int sx = __shfl_sync(0xffffffffu, vi.x, v);
-      const int sy = __shfl_sync(0xffffffffu, vi.y, v);
-      T* dst = voxels + ((int64_t)sx * max_voxels + sy) * row_len;
-      const int keep = (int)min((int64_t)cv, P);
-      for (int idx = lane; idx < (int)row_len; idx += 32) {
-        const int j = idx / fi, q = idx - j * fi;
-        dst[idx] = j < keep ? pts[(int64_t)srt[v][j] * f + q] : from_f32<T>(0.f);
-      }
-    }
-    __syncwarp();
-    unsigned big = __ballot_sync(0xffffffffu, cnt > (uint32_t)kFastMembers);
-    while (big) {
-      const int b = __ffs(big) - 1;
-      big &= big - 1;
-      const uint32_t bc = __shfl_sync(0xffffffffu, cnt, b);
-      const uint32_t be = __shfl_sync(0xffffffffu, end, b);
-      const int bx = __shfl_sync(0xffffffffu, vi.x, b);
-      const int by = __shfl_sync(0xffffffffu, vi.y, b);
-      const uint32_t bs = be - bc;
-      T* dst = voxels + ((int64_t)bx * max_voxels + by) * row_len;
-      const int64_t keep = min((int64_t)bc, P);
-      uint32_t last = 0;
-      for (int64_t j = 0; j < keep; ++j) {
-        uint32_t best = 0xffffffffu;
-        for (uint32_t i = bs + lane; i < be; i += 32) {
-          const uint32_t m = members[i];
-          if ((j == 0 || m > last) && m < best) best = m;
-        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
-        last = best;
-        for (int64_t q = lane; q < f; q += 32) dst[j * f + q] = pts[(int64_t)best * f + q];
-      }
-      for (int64_t idx = keep * f + lane; idx < row_len; idx += 32) dst[idx] = from_f32<T>(0.f);
+      for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+      last = best;
+      for (int64_t q = lane; q < f; q += 32) dst[j * f + q] = pts[(int64_t)best * f + q];
     }
+    for (int64_t idx = keep * f + lane; idx < row_len; idx += 32) dst[idx] = from_f32<T>(0.f);
   }
 }
 
@@ -428,12 +426,14 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
   BFB_CHECK_LAUNCH();
   if (n > 0) {
     // bucket offsets over voxel ids; entries past the voxel count are never read
-    BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n, sv.scan, nullptr, st));
-    vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members);
+    BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n + 1, sv.scan, nullptr, st));
+    vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members, sv.mvox);
     BFB_CHECK_LAUNCH();
-    vox_emit_kernel<T><<<kEmitBlocks, kEmitWarps * 32, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor,
-                                                                sv.gslot, sv.vinfo, sv.members, P, MV,
-                                                                static_cast<T*>(voxels));
+    vox_rank_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo, sv.members,
+                                                   sv.mvox, P, MV, static_cast<T*>(voxels));
+    BFB_CHECK_LAUNCH();
+    vox_pad_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot, sv.vinfo,
+                                                  sv.members, P, MV, static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
   }
   if (zero_tail) {
