@@ -358,27 +358,28 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
   }
 }
 
-// One thread per output element of the kept voxel rows: point slot j of
-// voxel g copies feature q of its j-th point, or 0 past the voxel's points.
-// Voxel ids of a sample are consecutive rows, so stores are coalesced.
+// One warp per kept voxel row: point slot j copies its j-th point's
+// features, slots past the voxel's points get 0.  Voxel ids of a sample are
+// consecutive rows, so consecutive warps store consecutive memory.
 template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_rows_kernel(
     const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt,
     const uint32_t* __restrict__ cursor, const int2* __restrict__ vinfo, const uint32_t* __restrict__ order,
     int64_t P, int64_t max_voxels, T* __restrict__ voxels) {
-  const int64_t row_len = P * f;
-  const int64_t total = (int64_t)*total_dev * row_len;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-    const int64_t g = e / row_len;
+  const int lane = threadIdx.x & 31;
+  const int row_len = (int)(P * f), fi = (int)f;
+  const int64_t total = *total_dev;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < total; g += warps) {
     const uint32_t cnt = gcnt[g];
     if (cnt == 0) continue;  // voxel beyond max_voxels
-    const int64_t rem = e - g * row_len;
-    const int64_t j = rem / f, q = rem - j * f;
     const int2 vi = vinfo[g];
-    T v = from_f32<T>(0.f);
-    if (j < (int64_t)cnt) v = pts[(int64_t)order[cursor[g] - cnt + j] * f + q];
-    voxels[((int64_t)vi.x * max_voxels + vi.y) * row_len + rem] = v;
+    const uint32_t* ord = order + (cursor[g] - cnt);
+    T* dst = voxels + ((int64_t)vi.x * max_voxels + vi.y) * row_len;
+    for (int idx = lane; idx < row_len; idx += 32) {
+      const int j = idx / fi, q = idx - j * fi;
+      dst[idx] = (uint32_t)j < cnt ? pts[(int64_t)ord[j] * f + q] : from_f32<T>(0.f);
+    }
   }
 }
 
@@ -526,6 +527,7 @@ extern "C" int bfb_hard_voxelize_batch(const void* points, int dtype, const int6
   for (int i = 0; i < 3; ++i)
     if (gr.g[i] <= 0) return BFB_ERR_INVALID_ARG;
   if (gr.g[0] > (1LL << kLinBits) / gr.g[1] / gr.g[2]) return BFB_ERR_TOO_LARGE;
+  if ((max_points < 0 ? n : max_points) * f > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;  // one voxel row
   const uint64_t cap = table_cap_for_bytes(table_bytes);
   VoxScratch sv;
   if (!table || !scratch || cap < (uint64_t)(2 * n) || carve_scratch(nullptr, n, batch, &sv) > scratch_bytes)
