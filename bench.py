@@ -36,7 +36,7 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from bevfusion_triton_b200 import synth  # noqa: E402
+from bevfusion_triton_b200 import shard, synth  # noqa: E402
 
 METRIC = 'bev_pool fwd+bwd & voxelize ms/sample and GB/s (% of B200 HBM peak), 1/2/4/8 GPU'
 UNIT = 'ms/sample'
@@ -88,21 +88,11 @@ def barrier(ws):
 
 
 def max_over_ranks(x: float, ws: int) -> float:
-    if ws == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device='cuda' if torch.cuda.is_available() else 'cpu')
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return shard.max_over_ranks(x, 'cuda' if torch.cuda.is_available() else 'cpu')
 
 
 def sum_over_ranks(x: float, ws: int) -> float:
-    if ws == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device='cuda' if torch.cuda.is_available() else 'cpu')
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return shard.sum_over_ranks(x, 'cuda' if torch.cuda.is_available() else 'cpu')
 
 
 # ------------------------------------------------------------------ clocks
@@ -174,9 +164,11 @@ class ClockSampler:
 class Workload:
     """The rank's shard: det bev_pool batch + LiDAR batch, resident on the GPU."""
 
-    def __init__(self, rank: int, samples: int, device):
+    def __init__(self, rank: int, samples: int, device, world: int = 1):
         self.S = samples
-        case = synth.det_bev_pool_case(samples, device=device, sample_offset=rank * samples)
+        first, count = shard.shard_samples(samples * world, world, rank)
+        assert count == samples
+        case = synth.det_bev_pool_case(samples, device=device, sample_offset=first)
         self.feats, self.coords = case.feats, case.coords
         self.shape = (case.B, case.D, case.H, case.W)
         self.n = self.feats.size(0)
@@ -186,7 +178,7 @@ class Workload:
         dhw = case.D * case.H * case.W
         r = (self.coords[:, 3] * dhw + (self.coords[:, 2] * case.H + self.coords[:, 0]) * case.W + self.coords[:, 1])
         self.nonempty = int(torch.unique(r).numel())
-        clouds = [synth.lidar_sweeps(rank * samples + i) for i in range(samples)]
+        clouds = [synth.lidar_sweeps(first + i) for i in range(samples)]
         self.offs = [0]
         for c in clouds:
             self.offs.append(self.offs[-1] + c.size(0))
@@ -221,7 +213,7 @@ def run_ours(args, ws, rank, local):
     cdll.bfb_kernel_launches.restype = ctypes.c_uint64
     O = ops()
     dev = torch.device('cuda', local)
-    wl = Workload(rank, args.samples_per_gpu, dev)
+    wl = Workload(rank, args.samples_per_gpu, dev, ws)
     B, D, H, W = wl.shape
     stream = torch.cuda.current_stream()
 
