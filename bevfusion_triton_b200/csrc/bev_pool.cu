@@ -16,7 +16,8 @@
 //   5. scan + bev_emit_kernel one work descriptor per piece
 //   6. bev_fwd_kernel         one CTA per piece; each non-empty cell is summed by ONE
 //                             warp in ascending point order with fp32 adds (16-byte
-//                             row loads), largest cells first, into a shared
+//                             row loads, the next rows' loads in flight while the
+//                             current ones are added), largest cells first, into a shared
 //                             [cell][channel] tile; then every channel-plane segment
 //                             of the piece is written coalesced, zeros included (no
 //                             memset, no permute).  fp32 results equal index_add_'s
@@ -38,7 +39,6 @@ constexpr int kTileCells = 32;
 constexpr int kPiecePoints = 2048;
 constexpr int kPoolWarps = 4;
 constexpr int kPoolThreads = kPoolWarps * 32;
-constexpr int kUnroll = 8;
 
 struct PlanHeader {
   uint32_t n_valid;
@@ -381,10 +381,45 @@ struct PermStream {
   }
 };
 
+// Sum of one cell's rows in ascending point order, software-pipelined: the
+// loads of the next U rows are in flight while the current U are added.
+template <class T, int VE, int U>
+__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, int cnt, const T* fbase,
+                                                   int64_t C, bool active, float (&acc)[VE]) {
+  float va[U][VE], vb[U][VE];
+  auto load = [&](int k, float (&v)[U][VE]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (k + u < cnt && active) {
+        VecIO<T, VE>::load(fbase + (int64_t)pids[k + u] * C, v[u]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
+      }
+    }
+  };
+  auto add = [&](int k, const float (&v)[U][VE]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (k + u < cnt) {
+#pragma unroll
+        for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
+      }
+  };
+  load(0, va);
+  for (int k = 0; k < cnt; k += 2 * U) {
+    if (k + U < cnt) load(k + U, vb);
+    add(k, va);
+    if (k + U >= cnt) break;
+    if (k + 2 * U < cnt) load(k + 2 * U, va);
+    add(k + U, vb);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // 6. forward: one CTA per (piece, channel slice of 32 vectors)
 // ---------------------------------------------------------------------------
-template <class T, int VE>
+template <class T, int VE, int PU>
 __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
     const T* __restrict__ feats, int64_t C, int nvec, int64_t dhw, int64_t tpb,
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
@@ -429,34 +464,38 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
     i = __shfl_sync(0xffffffffu, i, 0);
     if (i >= m) break;
     const int cell = s_cell[i], beg = s_beg[i], cnt = s_cnt[i];
-    PermStream ps;
-    if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
     float acc[VE];
 #pragma unroll
     for (int q = 0; q < VE; ++q) acc[q] = 0.f;
-    for (int k = 0; k < cnt; k += kUnroll) {
-      float v[kUnroll][VE];
+    if (staged) {
+      sum_cell_pipelined<T, VE, PU>(s_perm + beg, cnt, fbase, C, active, acc);
+    } else {
+      PermStream ps;
+      if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
+      for (int k = 0; k < cnt; k += PU) {
+        float v[PU][VE];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        uint32_t pid = 0;
-        if (staged) {
-          if (k + u < cnt) pid = s_perm[beg + k + u];
-        } else {
-          pid = ps.at(pa + beg + k + u, lane);
+        for (int u = 0; u < PU; ++u) {
+          uint32_t pid = 0;
+          if (staged) {
+            if (k + u < cnt) pid = s_perm[beg + k + u];
+          } else {
+            pid = ps.at(pa + beg + k + u, lane);
+          }
+          if (k + u < cnt && active) {
+            VecIO<T, VE>::load(fbase + (int64_t)pid * C, v[u]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
+          }
         }
-        if (k + u < cnt && active) {
-          VecIO<T, VE>::load(fbase + (int64_t)pid * C, v[u]);
-        } else {
+        // ascending point order, one fp32 add per element per point
 #pragma unroll
-          for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
-        }
-      }
-      // ascending point order, one fp32 add per element per point
+        for (int u = 0; u < PU; ++u) {
+          if (k + u < cnt) {
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (k + u < cnt) {
-#pragma unroll
-          for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
+            for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
+          }
         }
       }
     }
@@ -609,21 +648,29 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <class T, int VE>
-int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out,
+template <class T, int VE, int PU>
+int launch_fwd_v(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out,
                cudaStream_t st) {
   const int nvec = (int)(C / VE);
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
   const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4) + kPiecePoints * sizeof(uint32_t);
   if (smem > 48 * 1024)
-    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
-  bev_fwd_kernel<T, VE><<<grid, kPoolThreads, smem, st>>>(
+  bev_fwd_kernel<T, VE, PU><<<grid, kPoolThreads, smem, st>>>(
       static_cast<const T*>(feats), C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
       static_cast<T*>(out));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
+}
+
+// Pipeline depth of the forward gather: 8 rows for 4-byte features (96
+// registers), 4 for 16-bit features (8 elements per lane already).
+template <class T, int VE>
+int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out, cudaStream_t st) {
+  constexpr int kDepth = (sizeof(T) == 4 || VE == 1) ? 8 : 4;
+  return launch_fwd_v<T, VE, kDepth>(feats, C, g, pv, out, st);
 }
 
 template <class T, int VE>
