@@ -19,10 +19,10 @@
 //                num_points, record the voxel's table slot and member count
 //   vox_fill     bucket every kept point by voxel (slots from a scan of the counts)
 //   vox_rank     a thread per kept point: its slot = number of smaller point indices in
-//                its voxel's bucket (input order), recorded when below max_points
-//   vox_order    a lane per voxel: reset the table slot; voxels above 256 points are
-//                ordered by a whole warp (repeated minimum)
-//   vox_rows     a thread per output element of the kept rows (copy or zero padding)
+//                its voxel's bucket (input order); slots below max_points get its row
+//   vox_pad      a thread per (voxel, slot): zero the slots past the voxel's points
+//   vox_order    a lane per voxel: reset the table slot; voxels above 4096 points are
+//                ordered and written by a whole warp (repeated minimum)
 // The table therefore stays clean between calls: it is initialised once
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
@@ -79,7 +79,6 @@ struct VoxScratch {
   int2* vinfo;       // [n]   (sample, voxel id within the sample)
   uint32_t* members; // [n]   point index per bucket slot
   int32_t* mvox;     // [n]   voxel id per bucket slot
-  uint32_t* order;   // [n]   per bucket: its first P points in input order
   uint32_t* scan;
   uint32_t* err;     // [4]   0: table full (insert gave up)
 };
@@ -95,7 +94,6 @@ size_t carve_scratch(void* base, int64_t n, int64_t batch, VoxScratch* v) {
   v->vinfo = c.take<int2>((size_t)n);
   v->members = c.take<uint32_t>((size_t)n);
   v->mvox = c.take<int32_t>((size_t)n);
-  v->order = c.take<uint32_t>((size_t)n);
   v->scan = c.take<uint32_t>(scan_scratch_elems(n + 1));
   v->err = c.take<uint32_t>(4);
   return c.bytes();
@@ -293,14 +291,16 @@ __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __
   }
 }
 
-constexpr int kRankMax = 256;  // voxels with more points are ordered by a whole warp
+constexpr int kRankMax = 4096;  // voxels with more points are ordered by a whole warp
 
 // One thread per kept point (bucket slot): its slot within the voxel is the
 // number of smaller point indices in the voxel's bucket, i.e. its rank in
-// input order; ranks below P are recorded in `order` (bucket-local).
+// input order; points ranked below P copy their features into that slot.
+template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
-    const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt, const uint32_t* __restrict__ cursor,
-    const uint32_t* __restrict__ members, const int32_t* __restrict__ mvox, int64_t P, uint32_t* __restrict__ order) {
+    const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt,
+    const uint32_t* __restrict__ cursor, const int2* __restrict__ vinfo, const uint32_t* __restrict__ members,
+    const int32_t* __restrict__ mvox, int64_t P, int64_t max_voxels, T* __restrict__ voxels) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   // kept points over the batch: the bucket offset one past the last voxel
   // (vox_fill advances only the offsets of voxels that own points)
@@ -312,21 +312,47 @@ __global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
   const uint32_t p = members[i];
   uint32_t r = 0;
   for (uint32_t j = start; j < end; ++j) r += __ldg(members + j) < p;
-  if ((int64_t)r < P) order[start + r] = p;
+  if ((int64_t)r >= P) return;
+  const int2 vi = vinfo[g];
+  T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + r) * f;
+  const T* src = pts + (int64_t)p * f;
+  for (int64_t q = 0; q < f; ++q) dst[q] = src[q];
+}
+
+// One thread per (voxel, point slot): slots past a voxel's points get 0.
+template <class T>
+__global__ __launch_bounds__(kVoxThreads) void vox_pad_kernel(const uint32_t* __restrict__ total_dev,
+                                                              const uint32_t* __restrict__ gcnt,
+                                                              const int2* __restrict__ vinfo, int64_t f, int64_t P,
+                                                              int64_t max_voxels, T* __restrict__ voxels) {
+  const int64_t total = (int64_t)*total_dev * P;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    const int64_t g = t / P, j = t - g * P;
+    const uint32_t cnt = gcnt[g];
+    if (cnt == 0 || cnt > (uint32_t)kRankMax || j < (int64_t)cnt) continue;
+    const int2 vi = vinfo[g];
+    T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + j) * f;
+    for (int64_t q = 0; q < f; ++q) dst[q] = from_f32<T>(0.f);
+  }
 }
 
 // One lane per voxel: reset the voxel's table slot; voxels above kRankMax
-// points get their first P points (input order) into `order` from the whole
-// warp by repeated minimum selection.
+// points are written by the whole warp: first P points by repeated minimum
+// selection (input order), zero padding.
+template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
-    const uint32_t* __restrict__ total_dev, TableView tb, const uint32_t* __restrict__ gcnt,
-    const uint32_t* __restrict__ cursor, const int32_t* __restrict__ gslot, const uint32_t* __restrict__ members,
-    int64_t P, uint32_t* __restrict__ order) {
+    const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, TableView tb,
+    const uint32_t* __restrict__ gcnt, const uint32_t* __restrict__ cursor, const int32_t* __restrict__ gslot,
+    const int2* __restrict__ vinfo, const uint32_t* __restrict__ members, int64_t P, int64_t max_voxels,
+    T* __restrict__ voxels) {
   const int lane = threadIdx.x & 31;
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = *total_dev;
   if (((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >= total) return;  // whole warp out of range
+  const int64_t row_len = P * f;
   uint32_t cnt = 0, end = 0;
+  int2 vi = make_int2(0, 0);
   if (g < total) {
     const int32_t slot = gslot[g];
     tb.keys[slot] = kEmptyKey;  // leave the table clean for the next call
@@ -334,6 +360,7 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
     tb.cnt[slot] = 0u;
     cnt = gcnt[g];
     end = cursor[g];
+    vi = vinfo[g];
   }
   unsigned big = __ballot_sync(0xffffffffu, cnt > (uint32_t)kRankMax);
   while (big) {
@@ -341,7 +368,10 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
     big &= big - 1;
     const uint32_t bc = __shfl_sync(0xffffffffu, cnt, b);
     const uint32_t be = __shfl_sync(0xffffffffu, end, b);
+    const int bx = __shfl_sync(0xffffffffu, vi.x, b);
+    const int by = __shfl_sync(0xffffffffu, vi.y, b);
     const uint32_t bs = be - bc;
+    T* dst = voxels + ((int64_t)bx * max_voxels + by) * row_len;
     const int64_t keep = min((int64_t)bc, P);
     uint32_t last = 0;
     for (int64_t j = 0; j < keep; ++j) {
@@ -353,33 +383,9 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
       last = best;
-      if (lane == 0) order[bs + j] = best;
+      for (int64_t q = lane; q < f; q += 32) dst[j * f + q] = pts[(int64_t)best * f + q];
     }
-  }
-}
-
-// One warp per kept voxel row: point slot j copies its j-th point's
-// features, slots past the voxel's points get 0.  Voxel ids of a sample are
-// consecutive rows, so consecutive warps store consecutive memory.
-template <class T>
-__global__ __launch_bounds__(kVoxThreads) void vox_rows_kernel(
-    const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt,
-    const uint32_t* __restrict__ cursor, const int2* __restrict__ vinfo, const uint32_t* __restrict__ order,
-    int64_t P, int64_t max_voxels, T* __restrict__ voxels) {
-  const int lane = threadIdx.x & 31;
-  const int row_len = (int)(P * f), fi = (int)f;
-  const int64_t total = *total_dev;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < total; g += warps) {
-    const uint32_t cnt = gcnt[g];
-    if (cnt == 0) continue;  // voxel beyond max_voxels
-    const int2 vi = vinfo[g];
-    const uint32_t* ord = order + (cursor[g] - cnt);
-    T* dst = voxels + ((int64_t)vi.x * max_voxels + vi.y) * row_len;
-    for (int idx = lane; idx < row_len; idx += 32) {
-      const int j = idx / fi, q = idx - j * fi;
-      dst[idx] = (uint32_t)j < cnt ? pts[(int64_t)ord[j] * f + q] : from_f32<T>(0.f);
-    }
+    for (int64_t idx = keep * f + lane; idx < row_len; idx += 32) dst[idx] = from_f32<T>(0.f);
   }
 }
 
@@ -438,14 +444,14 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
     BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n + 1, sv.scan, nullptr, st));
     vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members, sv.mvox);
     BFB_CHECK_LAUNCH();
-    vox_rank_kernel<<<nb, kVoxThreads, 0, st>>>(sv.excl + n, sv.gcnt, sv.cursor, sv.members, sv.mvox, P,
-                                                sv.order);
+    vox_rank_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo, sv.members,
+                                                   sv.mvox, P, MV, static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
-    vox_order_kernel<<<nb, kVoxThreads, 0, st>>>(sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot, sv.members, P,
-                                                 sv.order);
+    vox_pad_kernel<T><<<148 * 16, kVoxThreads, 0, st>>>(sv.excl + n, sv.gcnt, sv.vinfo, f, P, MV,
+                                                        static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
-    vox_rows_kernel<T><<<148 * 16, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo,
-                                                         sv.order, P, MV, static_cast<T*>(voxels));
+    vox_order_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot, sv.vinfo,
+                                                    sv.members, P, MV, static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
   }
   if (zero_tail) {
