@@ -171,3 +171,39 @@ def test_cabi_direct_call(cuda):
                                 ctypes.c_void_p(plan.data_ptr()), ctypes.c_size_t(plan_b.value - 1),
                                 ctypes.c_void_p(scr.data_ptr()), scr_b, stream)
     assert rc == -3
+
+
+def test_seg_batch4_fwd_bwd_vs_oracle(cuda):
+    """Config 4: segmentation grid 256 x 256, batch 4, fp32, forward + backward."""
+    case = synth.seg_bev_pool_case(4, device='cuda')
+    shape = (case.B, case.D, case.H, case.W)
+    assert shape == (4, 1, 256, 256)
+    x = case.feats.clone().requires_grad_(True)
+    out = bev_pool(x, case.coords, *shape)
+    g = torch.Generator(device='cuda').manual_seed(3)
+    up = torch.randn(out.shape, generator=g, device='cuda')
+    out.backward(up)
+    ref, bad = oracle.bev_pool(case.feats.cpu().numpy(), case.coords.cpu().numpy(), *shape)
+    assert bad == 0
+    np.testing.assert_array_equal(out.detach().cpu().numpy(), ref)
+    rg = oracle.bev_pool_backward(up.cpu().numpy(), case.coords.cpu().numpy(), *shape)
+    np.testing.assert_array_equal(x.grad.cpu().numpy(), rg)
+
+
+def test_det_batch8_fp16_features(cuda):
+    """Config 2's fp16-feature variant: the fp16 output equals the fp32 sum of
+    the same fp16 inputs rounded once (the stated bar is 1e-2)."""
+    case = synth.det_bev_pool_case(8, device='cuda', dtype=torch.float16)
+    shape = (case.B, case.D, case.H, case.W)
+    x = case.feats.clone().requires_grad_(True)
+    out = bev_pool(x, case.coords, *shape)
+    assert out.dtype == torch.float16
+    ref, _ = oracle.bev_pool(case.feats.float().cpu().numpy(), case.coords.cpu().numpy(), *shape)
+    np.testing.assert_allclose(out.detach().float().cpu().numpy(), ref, rtol=1e-2, atol=1e-2)
+    assert torch.equal(out.detach().cpu(), torch.from_numpy(ref).half())
+    up = torch.randn(out.shape, device='cuda').half()
+    out.backward(up)
+    idx = case.coords.cpu()
+    s = ((idx[:, 2] * case.H + idx[:, 0]) * case.W + idx[:, 1]).cuda()
+    want = up.reshape(case.B, up.size(1), -1).permute(0, 2, 1)[idx[:, 3].cuda(), s]
+    assert torch.equal(x.grad, want)
