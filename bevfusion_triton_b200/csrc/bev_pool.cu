@@ -381,17 +381,49 @@ struct PermStream {
   }
 };
 
+// Row sources of the forward gather.  DenseRows reads feats[pid, slice];
+// DepthContextRows forms depth[pid] * context[pixel(pid), slice] on the fly
+// (product rounded to fp32 exactly as a materialised feature tensor would be),
+// reading the context from its transposed [pixel, C] copy.
+template <class T, int VE>
+struct DenseRows {
+  const T* feats;
+  int64_t C;
+  const T* base;
+  __device__ __forceinline__ void bind(int v0, int lane) { base = feats + (int64_t)(v0 + lane) * VE; }
+  __device__ __forceinline__ void load(uint32_t pid, float (&v)[VE]) const {
+    VecIO<T, VE>::load(base + (int64_t)pid * C, v);
+  }
+};
+
+struct DepthContextRows {
+  const float* depth;   // [n]   one value per frustum point
+  const float* ctx_t;   // [pixels, C]
+  int64_t C;
+  uint32_t dhw;         // depth bins x feature-map pixels of one camera
+  uint32_t hw;          // feature-map pixels of one camera
+  const float* base;
+  __device__ __forceinline__ void bind(int v0, int lane) { base = ctx_t + (int64_t)(v0 + lane) * 4; }
+  __device__ __forceinline__ void load(uint32_t pid, float (&v)[4]) const {
+    const uint32_t cam = pid / dhw, pix = cam * hw + (pid - cam * dhw) % hw;
+    VecIO<float, 4>::load(base + (int64_t)pix * C, v);
+    const float d = __ldg(depth + pid);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(d, v[q]);
+  }
+};
+
 // Sum of one cell's rows in ascending point order, software-pipelined: the
 // loads of the next U rows are in flight while the current U are added.
-template <class T, int VE, int U>
-__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, int cnt, const T* fbase,
-                                                   int64_t C, bool active, float (&acc)[VE]) {
+template <int VE, int U, class Src>
+__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, int cnt, const Src& src,
+                                                   bool active, float (&acc)[VE]) {
   float va[U][VE], vb[U][VE];
   auto load = [&](int k, float (&v)[U][VE]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (k + u < cnt && active) {
-        VecIO<T, VE>::load(fbase + (int64_t)pids[k + u] * C, v[u]);
+        src.load(pids[k + u], v[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
@@ -403,7 +435,7 @@ __device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ 
     for (int u = 0; u < U; ++u)
       if (k + u < cnt) {
 #pragma unroll
-        for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
+        for (int q = 0; q < VE; ++q) acc[q] = __fadd_rn(acc[q], v[u][q]);
       }
   };
   load(0, va);
@@ -419,9 +451,9 @@ __device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ 
 // ---------------------------------------------------------------------------
 // 6. forward: one CTA per (piece, channel slice of 32 vectors)
 // ---------------------------------------------------------------------------
-template <class T, int VE, int PU>
+template <class T, int VE, int PU, class Src>
 __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
-    const T* __restrict__ feats, int64_t C, int nvec, int64_t dhw, int64_t tpb,
+    Src src, int64_t C, int nvec, int64_t dhw, int64_t tpb,
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
     const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -456,7 +488,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
   __syncthreads();
 
   const bool active = lane < nvs;
-  const T* fbase = feats + (int64_t)(v0 + lane) * VE;
+  src.bind(v0, lane);
   const int m = s_m;
   for (;;) {
     int i = 0;
@@ -468,7 +500,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
 #pragma unroll
     for (int q = 0; q < VE; ++q) acc[q] = 0.f;
     if (staged) {
-      sum_cell_pipelined<T, VE, PU>(s_perm + beg, cnt, fbase, C, active, acc);
+      sum_cell_pipelined<VE, PU>(s_perm + beg, cnt, src, active, acc);
     } else {
       PermStream ps;
       if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
@@ -483,7 +515,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
             pid = ps.at(pa + beg + k + u, lane);
           }
           if (k + u < cnt && active) {
-            VecIO<T, VE>::load(fbase + (int64_t)pid * C, v[u]);
+            src.load(pid, v[u]);
           } else {
 #pragma unroll
             for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
@@ -494,7 +526,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
         for (int u = 0; u < PU; ++u) {
           if (k + u < cnt) {
 #pragma unroll
-            for (int q = 0; q < VE; ++q) acc[q] += v[u][q];
+            for (int q = 0; q < VE; ++q) acc[q] = __fadd_rn(acc[q], v[u][q]);
           }
         }
       }
@@ -648,18 +680,18 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <class T, int VE, int PU>
-int launch_fwd_v(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out,
+template <class T, int VE, int PU, class Src>
+int launch_fwd_v(const Src& src, int64_t C, const Geometry& g, const PlanView& pv, void* out,
                cudaStream_t st) {
   const int nvec = (int)(C / VE);
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
   const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4) + kPiecePoints * sizeof(uint32_t);
   if (smem > 48 * 1024)
-    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
-  bev_fwd_kernel<T, VE, PU><<<grid, kPoolThreads, smem, st>>>(
-      static_cast<const T*>(feats), C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
+  bev_fwd_kernel<T, VE, PU, Src><<<grid, kPoolThreads, smem, st>>>(
+      src, C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
       static_cast<T*>(out));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
@@ -670,7 +702,8 @@ int launch_fwd_v(const void* feats, int64_t C, const Geometry& g, const PlanView
 template <class T, int VE>
 int launch_fwd(const void* feats, int64_t C, const Geometry& g, const PlanView& pv, void* out, cudaStream_t st) {
   constexpr int kDepth = (sizeof(T) == 4 || VE == 1) ? 8 : 4;
-  return launch_fwd_v<T, VE, kDepth>(feats, C, g, pv, out, st);
+  DenseRows<T, VE> src{static_cast<const T*>(feats), C, nullptr};
+  return launch_fwd_v<T, VE, kDepth>(src, C, g, pv, out, st);
 }
 
 template <class T, int VE>
@@ -896,3 +929,213 @@ extern "C" int bfb_bev_pool_forward_noalloc(const void* feats, int dtype, const 
 }
 
 extern "C" size_t bfb_bev_pool_noalloc_capacity(void) { return kNoAllocBytes; }
+
+// ===========================================================================
+// Fused depth x context pooling (the LSS camera branch without a feature
+// tensor): feats[n, c] = depth[n] * context[cam(n), c, h(n), w(n)] is formed
+// on the fly inside the gather.  Forward equals bev_pool on the materialised
+// product bit for bit (product and sums rounded as there).
+// ===========================================================================
+namespace bfb {
+namespace {
+
+// out[m][p][r] = in[m][r][p] (fp32), 32 x 32 tiles through shared memory.
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t R, int64_t P) {
+  __shared__ float tile[32][33];
+  const int64_t m = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, p0 = (int64_t)blockIdx.x * 32;
+  const float* src = in + m * R * P;
+  float* dst = out + m * R * P;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t r = r0 + i, p = p0 + threadIdx.x;
+    if (r < R && p < P) tile[i][threadIdx.x] = src[r * P + p];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t p = p0 + i, r = r0 + threadIdx.x;
+    if (r < R && p < P) dst[p * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+int launch_transpose(const float* in, float* out, int64_t M, int64_t R, int64_t P, cudaStream_t st) {
+  if (M == 0 || R == 0 || P == 0) return BFB_OK;
+  if (M > 65535 || ceil_div(R, 32) > 65535) return BFB_ERR_TOO_LARGE;
+  dim3 grid((unsigned)ceil_div(P, 32), (unsigned)ceil_div(R, 32), (unsigned)M);
+  transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(in, out, R, P);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+struct DcDims {
+  int64_t cams, nd, hw, c;  // cameras over the batch, depth bins, feature-map pixels, channels
+  __host__ __device__ int64_t n() const { return cams * nd * hw; }
+};
+
+// Per frustum point, in pixel-major order [cam][hw][nd]: its cell (or -1 when
+// outside the grid) and its depth value.
+template <class IT>
+__global__ void dc_point_table_kernel(const IT* __restrict__ coords, const float* __restrict__ depth, DcDims dm,
+                                      int64_t B, int64_t D, int64_t H, int64_t W, int32_t* __restrict__ key_t,
+                                      float* __restrict__ depth_t) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= dm.n()) return;
+  int64_t x, y, z, b;
+  load_coord<IT>(coords, n, x, y, z, b);
+  const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W && (uint64_t)z < (uint64_t)D &&
+                  (uint64_t)b < (uint64_t)B;
+  const int64_t cam = n / (dm.nd * dm.hw), rem = n - cam * dm.nd * dm.hw;
+  const int64_t d = rem / dm.hw, p = rem - d * dm.hw;
+  const int64_t t = (cam * dm.hw + p) * dm.nd + d;
+  key_t[t] = ok ? (int32_t)(((b * D + z) * H + x) * W + y) : -1;
+  depth_t[t] = depth[n];
+}
+
+// A warp per camera pixel walks its depth bins in order:
+//   grad_depth[n]     = sum_c grad[cell(n), c] * context[pixel, c]
+//   grad_context[pixel, c] = sum_n depth[n] * grad[cell(n), c]   (ascending n)
+// g_t is grad_out transposed to [cell, C]; lanes hold 4 channels each.
+__global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restrict__ g_t, const float* __restrict__ ctx_t,
+                                                         const int32_t* __restrict__ key_t,
+                                                         const float* __restrict__ depth_t, DcDims dm,
+                                                         float* __restrict__ gdepth_t, float* __restrict__ gctx_t) {
+  constexpr int U = 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t pix = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (pix >= dm.cams * dm.hw) return;  // warp-uniform
+  const int nv = (int)(dm.c / 4);
+  const bool active = lane < nv;
+  float cx[4] = {0.f, 0.f, 0.f, 0.f}, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (active) VecIO<float, 4>::load(ctx_t + pix * dm.c + lane * 4, cx);
+  const int32_t* keys = key_t + pix * dm.nd;
+  const float* deps = depth_t + pix * dm.nd;
+  float* gdep = gdepth_t + pix * dm.nd;
+  for (int64_t base = 0; base < dm.nd; base += 32) {
+    const int cnt = (int)min((int64_t)32, dm.nd - base);
+    const int32_t myk = lane < cnt ? __ldg(keys + base + lane) : -1;
+    const float myd = lane < cnt ? __ldg(deps + base + lane) : 0.f;
+    float mydot = 0.f;
+    for (int k0 = 0; k0 < cnt; k0 += U) {
+      float v[U][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int32_t key = __shfl_sync(0xffffffffu, myk, (k0 + u) & 31);
+        if (k0 + u < cnt && key >= 0 && active) {
+          VecIO<float, 4>::load(g_t + (int64_t)key * dm.c + lane * 4, v[u]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[u][q] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float dep = __shfl_sync(0xffffffffu, myd, (k0 + u) & 31);
+        float dot = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          dot = __fadd_rn(dot, __fmul_rn(v[u][q], cx[q]));
+          acc[q] = __fadd_rn(acc[q], __fmul_rn(dep, v[u][q]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (lane == ((k0 + u) & 31)) mydot = dot;
+      }
+    }
+    if (lane < cnt) gdep[base + lane] = mydot;
+  }
+  if (active) {
+    float* dst = gctx_t + pix * dm.c + lane * 4;
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+}
+
+int dc_check(const DcDims& dm, const Geometry& g) {
+  if (dm.cams <= 0 || dm.nd <= 0 || dm.hw <= 0 || dm.c <= 0) return BFB_ERR_INVALID_ARG;
+  if (dm.c % 4 != 0 || dm.c > 128) return BFB_ERR_INVALID_ARG;  // a warp holds a 4-channel vector per lane
+  if (dm.n() != g.n) return BFB_ERR_INVALID_ARG;
+  return BFB_OK;
+}
+
+}  // namespace
+}  // namespace bfb
+
+extern "C" int bfb_bev_pool_dc_workspace_sizes(int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c,
+                                               int64_t B, int64_t D, int64_t H, int64_t W, size_t* plan_bytes,
+                                               size_t* scratch_bytes, size_t* aux_bytes, size_t* bwd_bytes) {
+  const DcDims dm{cams, nd, fh * fw, c};
+  Geometry g;
+  BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
+  BFB_TRY(dc_check(dm, g));
+  BFB_TRY(bfb_bev_pool_workspace_sizes(dm.n(), c, B, D, H, W, plan_bytes, scratch_bytes));
+  if (aux_bytes) *aux_bytes = align_up(sizeof(float) * (size_t)(cams * dm.hw * c));
+  if (bwd_bytes) {
+    Carver cv(nullptr);
+    cv.take<float>((size_t)(g.cells * c));        // grad table [cell, C]
+    cv.take<int32_t>((size_t)dm.n());             // cell per point, pixel-major
+    cv.take<float>((size_t)dm.n());               // depth, pixel-major
+    cv.take<float>((size_t)dm.n());               // grad depth, pixel-major
+    cv.take<float>((size_t)(cams * dm.hw * c));   // grad context [pixel, C]
+    *bwd_bytes = cv.bytes();
+  }
+  return BFB_OK;
+}
+
+extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context, const void* coords, int itype,
+                                       int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
+                                       int64_t D, int64_t H, int64_t W, float* out, void* plan, size_t plan_bytes,
+                                       void* scratch, size_t scratch_bytes, void* aux, size_t aux_bytes,
+                                       void* stream) {
+  const DcDims dm{cams, nd, fh * fw, c};
+  Geometry g;
+  BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
+  BFB_TRY(dc_check(dm, g));
+  if (!depth || !context || !out) return BFB_ERR_INVALID_ARG;
+  if (!aux || aux_bytes < sizeof(float) * (size_t)(cams * dm.hw * c)) return BFB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(aux) & 15) || (reinterpret_cast<uintptr_t>(out) & 3)) return BFB_ERR_INVALID_ARG;
+  cudaStream_t st = as_stream(stream);
+  float* ctx_t = static_cast<float*>(aux);
+  BFB_TRY(launch_transpose(context, ctx_t, cams, c, dm.hw, st));  // [cam][C][hw] -> [cam][hw][C]
+  BFB_TRY(bfb_bev_pool_plan(coords, itype, dm.n(), B, D, H, W, plan, plan_bytes, scratch, scratch_bytes, stream));
+  PlanView pv;
+  carve_plan(plan, g, &pv);
+  DepthContextRows src{depth, ctx_t, c, (uint32_t)(nd * dm.hw), (uint32_t)dm.hw, nullptr};
+  return launch_fwd_v<float, 4, 8>(src, c, g, pv, out, st);
+}
+
+extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* depth, const void* coords, int itype,
+                                        int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
+                                        int64_t D, int64_t H, int64_t W, const void* aux, size_t aux_bytes,
+                                        void* ws, size_t ws_bytes, float* grad_depth, float* grad_context,
+                                        void* stream) {
+  const DcDims dm{cams, nd, fh * fw, c};
+  Geometry g;
+  BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
+  BFB_TRY(dc_check(dm, g));
+  if (!grad_out || !depth || !coords || !grad_depth || !grad_context) return BFB_ERR_INVALID_ARG;
+  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!aux || aux_bytes < sizeof(float) * (size_t)(cams * dm.hw * c)) return BFB_ERR_WORKSPACE;
+  size_t need = 0;
+  BFB_TRY(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, nullptr, nullptr, nullptr, &need));
+  if (!ws || ws_bytes < need) return BFB_ERR_WORKSPACE;
+  Carver cv(ws);
+  float* g_t = cv.take<float>((size_t)(g.cells * c));
+  int32_t* key_t = cv.take<int32_t>((size_t)dm.n());
+  float* depth_t = cv.take<float>((size_t)dm.n());
+  float* gdepth_t = cv.take<float>((size_t)dm.n());
+  float* gctx_t = cv.take<float>((size_t)(cams * dm.hw * c));
+  cudaStream_t st = as_stream(stream);
+  BFB_TRY(launch_transpose(grad_out, g_t, B, c, g.dhw, st));  // [B][C][DHW] -> [B][DHW][C]
+  const unsigned nb = (unsigned)ceil_div(dm.n(), 256);
+  if (itype == BFB_I32)
+    dc_point_table_kernel<int32_t><<<nb, 256, 0, st>>>(static_cast<const int32_t*>(coords), depth, dm, B, D, H, W,
+                                                       key_t, depth_t);
+  else
+    dc_point_table_kernel<int64_t><<<nb, 256, 0, st>>>(static_cast<const int64_t*>(coords), depth, dm, B, D, H, W,
+                                                       key_t, depth_t);
+  BFB_CHECK_LAUNCH();
+  dc_backward_kernel<<<(unsigned)ceil_div(cams * dm.hw * 32, 256), 256, 0, st>>>(
+      g_t, static_cast<const float*>(aux), key_t, depth_t, dm, gdepth_t, gctx_t);
+  BFB_CHECK_LAUNCH();
+  BFB_TRY(launch_transpose(gdepth_t, grad_depth, cams, dm.hw, nd, st));   // [cam][hw][nd] -> [cam][nd][hw]
+  BFB_TRY(launch_transpose(gctx_t, grad_context, cams, dm.hw, c, st));    // [cam][hw][C] -> [cam][C][hw]
+  return BFB_OK;
+}

@@ -121,6 +121,63 @@ int64_t bev_pool_invalid_count(const at::Tensor& plan) {
   return v;
 }
 
+// ------------------------------------------------- fused depth x context pooling
+std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward(const at::Tensor& depth_in, const at::Tensor& ctx_in,
+                                                       const at::Tensor& coords_in, int64_t B, int64_t D, int64_t H,
+                                                       int64_t W) {
+  require_cuda(depth_in, "depth");
+  require_cuda(ctx_in, "context");
+  require_cuda(coords_in, "coords");
+  c10::cuda::CUDAGuard guard(depth_in.device());
+  TORCH_CHECK_TYPE(depth_in.scalar_type() == at::kFloat && ctx_in.scalar_type() == at::kFloat,
+                   "depth and context must be float32");
+  TORCH_CHECK_VALUE(depth_in.dim() == 4 && ctx_in.dim() == 4, "depth [cams, D, fH, fW] and context [cams, C, fH, fW]");
+  auto depth = depth_in.contiguous();
+  auto ctx = ctx_in.contiguous();
+  auto coords = coords_in.contiguous();
+  const int64_t cams = depth.size(0), nd = depth.size(1), fh = depth.size(2), fw = depth.size(3), c = ctx.size(1);
+  TORCH_CHECK_VALUE(ctx.size(0) == cams && ctx.size(2) == fh && ctx.size(3) == fw, "context does not match depth");
+  TORCH_CHECK_VALUE(coords.dim() == 2 && coords.size(0) == cams * nd * fh * fw && coords.size(1) == 4,
+                    "coords must hold one (x, y, z, b) row per frustum point");
+  const int itype = coords.scalar_type() == at::kLong ? BFB_I64 : BFB_I32;
+  size_t plan_b = 0, scr_b = 0, aux_b = 0, bwd_b = 0;
+  check(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, &plan_b, &scr_b, &aux_b, &bwd_b),
+        "bev_pool_dc workspace query");
+  auto opts = depth.options().dtype(at::kByte);
+  auto plan = at::empty({(int64_t)plan_b}, opts);
+  auto scratch = at::empty({(int64_t)scr_b}, opts);
+  auto aux = at::empty({(int64_t)aux_b}, opts);
+  auto out = at::empty({B, c, D, H, W}, depth.options());
+  check(bfb_bev_pool_dc_forward(depth.data_ptr<float>(), ctx.data_ptr<float>(), coords.data_ptr(), itype, cams, nd, fh,
+                                fw, c, B, D, H, W, out.data_ptr<float>(), plan.data_ptr(), plan_b, scratch.data_ptr(),
+                                scr_b, aux.data_ptr(), aux_b, stream_of(depth)),
+        "bev_pool_dc forward");
+  return {out, aux};
+}
+
+std::tuple<at::Tensor, at::Tensor> bev_pool_dc_backward(const at::Tensor& grad_in, const at::Tensor& depth_in,
+                                                        const at::Tensor& coords_in, const at::Tensor& aux,
+                                                        int64_t c, int64_t B, int64_t D, int64_t H, int64_t W) {
+  require_cuda(grad_in, "grad_out");
+  c10::cuda::CUDAGuard guard(grad_in.device());
+  auto grad = grad_in.contiguous().to(at::kFloat);
+  auto depth = depth_in.contiguous();
+  auto coords = coords_in.contiguous();
+  const int64_t cams = depth.size(0), nd = depth.size(1), fh = depth.size(2), fw = depth.size(3);
+  const int itype = coords.scalar_type() == at::kLong ? BFB_I64 : BFB_I32;
+  size_t bwd_b = 0;
+  check(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, nullptr, nullptr, nullptr, &bwd_b),
+        "bev_pool_dc workspace query");
+  auto ws = at::empty({(int64_t)bwd_b}, depth.options().dtype(at::kByte));
+  auto gdepth = at::empty_like(depth);
+  auto gctx = at::empty({cams, c, fh, fw}, depth.options());
+  check(bfb_bev_pool_dc_backward(grad.data_ptr<float>(), depth.data_ptr<float>(), coords.data_ptr(), itype, cams, nd,
+                                 fh, fw, c, B, D, H, W, aux.data_ptr(), (size_t)aux.numel(), ws.data_ptr(), bwd_b,
+                                 gdepth.data_ptr<float>(), gctx.data_ptr<float>(), stream_of(grad)),
+        "bev_pool_dc backward");
+  return {gdepth, gctx};
+}
+
 // ------------------------------------------------------------ voxelisation
 std::vector<float> as_floats(const c10::ArrayRef<double>& v, size_t n, const char* what) {
   TORCH_CHECK_VALUE(v.size() == n, what, " must have length ", n);
@@ -300,6 +357,10 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward_planned(Tensor feats, Tensor plan, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_backward(Tensor grad_out, Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_invalid_count(Tensor plan) -> int");
+  m.def("bev_pool_dc_forward(Tensor depth, Tensor context, Tensor coords, int B, int D, int H, int W) -> (Tensor, Tensor)");
+  m.def(
+      "bev_pool_dc_backward(Tensor grad_out, Tensor depth, Tensor coords, Tensor aux, int C, int B, int D, int H, "
+      "int W) -> (Tensor, Tensor)");
   m.def("dynamic_voxelize(Tensor points, Tensor(a!) coors, float[] voxel_size, float[] coors_range) -> ()");
   m.def(
       "hard_voxelize(Tensor points, Tensor(a!) voxels, Tensor(b!) coors, Tensor(c!) num_points, "
@@ -320,6 +381,8 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("bev_pool_forward_planned", &bev_pool_forward_planned);
   m.impl("bev_pool_backward", &bev_pool_backward);
   m.impl("bev_pool_invalid_count", &bev_pool_invalid_count);
+  m.impl("bev_pool_dc_forward", &bev_pool_dc_forward);
+  m.impl("bev_pool_dc_backward", &bev_pool_dc_backward);
   m.impl("dynamic_voxelize", &dynamic_voxelize);
   m.impl("hard_voxelize", &hard_voxelize);
   m.impl("hard_voxelize_batch", &hard_voxelize_batch);

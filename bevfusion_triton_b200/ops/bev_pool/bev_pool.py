@@ -109,3 +109,50 @@ def bev_pool_planned(feats: torch.Tensor, plan: torch.Tensor, B: int, D: int, H:
 def invalid_count(plan: torch.Tensor) -> int:
     """Points a plan dropped as out of range (synchronises the stream)."""
     return int(ops().bev_pool_invalid_count(plan))
+
+
+class _BevPoolDepthContextFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, depth, context, coords, B, D, H, W):
+        out, aux = ops().bev_pool_dc_forward(depth, context, coords, B, D, H, W)
+        ctx.save_for_backward(depth, coords, aux)
+        ctx.shape = (context.size(1), B, D, H, W)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        depth, coords, aux = ctx.saved_tensors
+        C, B, D, H, W = ctx.shape
+        gdepth, gctx = ops().bev_pool_dc_backward(grad_out, depth, coords, aux, C, B, D, H, W)
+        return gdepth, gctx, None, None, None, None, None
+
+
+def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: torch.Tensor,
+                           B: int, D: int, H: int, W: int) -> torch.Tensor:
+    """The LSS camera branch's pooling without a feature tensor.
+
+    Equals ``bev_pool(feats[kept], coords[kept], B, D, H, W)`` with
+    ``feats = rearrange(depth.unsqueeze(2) * context.unsqueeze(3), 'b n c d h w -> (b n d h w) c')``
+    (models/vtransforms/depth_lss.py:91-94, base.py:136-160), forward bit for
+    bit.  ``depth`` [B, N, D_bins, fH, fW] (softmaxed) or [cams, D_bins, fH,
+    fW]; ``context`` [B, N, C, fH, fW] or [cams, C, fH, fW], fp32;
+    ``coords`` one (x, y, z, b) row per frustum point in (b, n, d, h, w)
+    order, unfiltered (points outside the grid are dropped).  Differentiable
+    w.r.t. depth and context.  C must be a multiple of 4, at most 128.
+    """
+    if depth.dim() == 5:
+        depth = depth.flatten(0, 1)
+    if context.dim() == 5:
+        context = context.flatten(0, 1)
+    if depth.dim() != 4 or context.dim() != 4:
+        raise ValueError('depth and context must be 4-D or 5-D tensors.')
+    if coords.dim() != 2 or coords.size(-1) != 4:
+        raise ValueError('coords must have shape [N, 4].')
+    if coords.dtype not in (torch.int32, torch.int64):
+        raise TypeError('coords must have dtype torch.int32 or torch.int64.')
+    if depth.dtype != torch.float32 or context.dtype != torch.float32:
+        raise TypeError('depth and context must have dtype torch.float32.')
+    if min(B, D, H, W) <= 0:
+        raise ValueError('B, D, H, W must be positive integers.')
+    _require_cuda(depth, context, coords)
+    return _BevPoolDepthContextFunction.apply(depth, context, coords, int(B), int(D), int(H), int(W))

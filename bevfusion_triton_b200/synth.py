@@ -235,3 +235,37 @@ def lidar_sweeps(sample: int = 0, seed: int = 0, device='cpu') -> torch.Tensor:
         dt = torch.full((xyz.size(0), 1), 0.05 * s, dtype=torch.float64)
         sweeps.append(torch.cat((xyz, inten, dt), 1))
     return torch.cat(sweeps, 0).float().contiguous().to(device)
+
+
+@dataclass
+class DepthContextCase:
+    depth: torch.Tensor    # [B, 6, D_bins, fH, fW] softmax over depth bins
+    context: torch.Tensor  # [B, 6, C, fH, fW]
+    coords: torch.Tensor   # [B*6*D_bins*fH*fW, 4] int64 (x, y, z, b), unfiltered
+    kept: torch.Tensor     # [B*6*D_bins*fH*fW] bool, the caller's in-grid filter
+    B: int
+    D: int
+    H: int
+    W: int
+
+
+def depth_context_case(batch: int, grid: dict, *, seed: int = 0, device='cpu', sample_offset: int = 0):
+    """Inputs of the fused camera-branch pooling: the depth distribution and
+    context of depth_lss.py:91-92 before their product, and one cell per
+    frustum point (out-of-grid points kept, with their out-of-range cells)."""
+    geom = frustum_geometry()
+    g, kept, nx = quantize_geometry(geom, **grid)
+    ncam = len(CAM_YAWS_DEG)
+    d = int(round((DBOUND[1] - DBOUND[0]) / DBOUND[2]))
+    fh, fw = FEATURE_SIZE
+    deps, ctxs, coords, keeps = [], [], [], []
+    for i in range(batch):
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed * 1_000_003 + sample_offset + i)
+        logits = torch.randn((ncam, d, fh, fw), generator=gen, device=device, dtype=torch.float32)
+        deps.append(logits.softmax(dim=1))
+        ctxs.append(torch.randn((ncam, CHANNELS, fh, fw), generator=gen, device=device, dtype=torch.float32))
+        coords.append(torch.cat((g, torch.full((g.size(0), 1), i, dtype=torch.int64)), 1))
+        keeps.append(kept)
+    return DepthContextCase(torch.stack(deps), torch.stack(ctxs), torch.cat(coords).to(device),
+                            torch.cat(keeps).to(device), batch, nx[2], nx[0], nx[1])

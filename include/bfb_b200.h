@@ -108,6 +108,35 @@ int bfb_bev_pool_backward(const void* grad_out_dev, int dtype, int64_t n, int64_
                           int64_t D, int64_t H, int64_t W, const void* plan_dev,
                           size_t plan_bytes, void* grad_feats_dev, void* stream);
 
+/* Fused camera branch: bev_pool of feats[n, c] = depth[n] * context[cam, c, h, w]
+ * without materialising feats.  Replaces models/vtransforms/depth_lss.py:91-94
+ * (softmax(depth) (x) context) followed by models/vtransforms/base.py:136-160
+ * (flatten, filter, ops.bev_pool).  depth [cams, nd, fh, fw] fp32 (already
+ * softmaxed), context [cams, c, fh, fw] fp32, coords [cams*nd*fh*fw, 4] for
+ * EVERY frustum point in (cam, d, h, w) order (points outside the grid are
+ * dropped, which is the caller's filter), c % 4 == 0 and c <= 128.  The
+ * forward equals bfb_bev_pool_forward on the materialised product bit for bit.
+ * `aux` (cams*fh*fw*c floats, from *_sizes) is written by the forward and read
+ * by the backward; `bwd` is the backward's scratch.  grad_depth has the
+ * layout of depth, grad_context that of context. */
+int bfb_bev_pool_dc_workspace_sizes(int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c,
+                                    int64_t B, int64_t D, int64_t H, int64_t W, size_t* plan_bytes,
+                                    size_t* scratch_bytes, size_t* aux_bytes, size_t* bwd_bytes);
+
+int bfb_bev_pool_dc_forward(const float* depth_dev, const float* context_dev,
+                            const void* coords_dev, int coords_itype, int64_t cams, int64_t nd,
+                            int64_t fh, int64_t fw, int64_t c, int64_t B, int64_t D, int64_t H,
+                            int64_t W, float* out_dev, void* plan_dev, size_t plan_bytes,
+                            void* scratch_dev, size_t scratch_bytes, void* aux_dev,
+                            size_t aux_bytes, void* stream);
+
+int bfb_bev_pool_dc_backward(const float* grad_out_dev, const float* depth_dev,
+                             const void* coords_dev, int coords_itype, int64_t cams, int64_t nd,
+                             int64_t fh, int64_t fw, int64_t c, int64_t B, int64_t D, int64_t H,
+                             int64_t W, const void* aux_dev, size_t aux_bytes, void* bwd_dev,
+                             size_t bwd_bytes, float* grad_depth_dev, float* grad_context_dev,
+                             void* stream);
+
 /* bev_pool forward that allocates nothing and takes no workspace.  It has no
  * counterpart in the reference.  It is for callers that cannot allocate GPU
  * memory at call time -- code in a real-time loop where cudaMalloc would
