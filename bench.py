@@ -301,6 +301,10 @@ def run_ours(args, ws, rank, local):
     }
     if not args.no_e2e:
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
+    if not args.no_fused:
+        del wl
+        torch.cuda.empty_cache()
+        line['fused_camera_branch'] = run_fused(args, rank, ws)
     if not args.no_cpu_baseline and ws == 1 and rank == 0:
         line['cpu_baseline'] = cpu_baseline(args)
     if rank == 0:
@@ -398,6 +402,51 @@ def run_e2e(args, wl, ws, samples_total):
             'pipeline': 'per sample over 3 streams (H2D / compute / D2H)', 'voxel_counts_match_device_step': ok}
 
 
+def run_fused(args, rank, ws):
+    """The camera branch from depth distribution and context to BEV (fwd+bwd)
+    over the rank's det samples: unfused (depth x context product, flatten,
+    in-grid filter, bev_pool, as models/vtransforms/depth_lss.py + base.py do)
+    vs the fused op that never materialises the feature tensor."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool, bev_pool_depth_context
+    S = args.samples_per_gpu
+    first, _ = shard.shard_samples(S * ws, ws, rank)
+    case = synth.depth_context_case(S, synth.DET_GRID, device='cuda', sample_offset=first)
+    shape = (case.B, case.D, case.H, case.W)
+    up = torch.randn((case.B, C, case.D, case.H, case.W), device='cuda')
+    kidx = torch.nonzero(case.kept).squeeze(1)
+    kcoords = case.coords[kidx]
+
+    def unfused():
+        d = case.depth.detach().requires_grad_(True)
+        c = case.context.detach().requires_grad_(True)
+        x = (d.unsqueeze(2) * c.unsqueeze(3)).permute(0, 1, 3, 4, 5, 2).reshape(-1, C)
+        bev_pool(x[kidx], kcoords, *shape).backward(up)
+
+    def fused():
+        d = case.depth.detach().requires_grad_(True)
+        c = case.context.detach().requires_grad_(True)
+        bev_pool_depth_context(d, c, case.coords, *shape).backward(up)
+
+    res = {}
+    for name, fn in (('unfused', unfused), ('fused', fused)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(ws)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k = max(3, min(args.steps, 10))
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        res[name + '_ms_per_sample'] = round(max_over_ranks(s0.elapsed_time(s1), ws) / k / S, 4)
+    res['speedup'] = round(res['unfused_ms_per_sample'] / res['fused_ms_per_sample'], 2)
+    res['note'] = 'det geometry, softmax depth (118 bins) x context (C=80), fp32, forward + backward'
+    return res
+
+
 # ------------------------------------------------------------------ CPU
 def cpu_reference_sample(threads: int, det=None, clouds=None):
     """One bounded sample of the reference's CPU algorithms: det bev_pool
@@ -475,6 +524,7 @@ def main():
     ap.add_argument('--ref-steps', type=int, default=3)
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-fused', action='store_true')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3  # timing rule: at least 3 warm-up steps

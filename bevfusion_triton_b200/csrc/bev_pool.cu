@@ -391,39 +391,59 @@ struct DenseRows {
   int64_t C;
   const T* base;
   __device__ __forceinline__ void bind(int v0, int lane) { base = feats + (int64_t)(v0 + lane) * VE; }
-  __device__ __forceinline__ void load(uint32_t pid, float (&v)[VE]) const {
+  __device__ __forceinline__ void load(uint32_t pid, uint32_t /*pos*/, float (&v)[VE]) const {
     VecIO<T, VE>::load(base + (int64_t)pid * C, v);
   }
 };
 
+// Unsigned 32-bit division by a runtime constant with a multiply-high and
+// shifts (round-up magic number, d >= 1).
+struct FastDiv {
+  uint32_t d, magic, shift;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div), magic(0), shift(0) {
+    if (div > 1) {
+      uint32_t s = 0;
+      while ((1ull << s) < div) ++s;
+      shift = s;
+      magic = (uint32_t)((((1ull << 32) * ((1ull << s) - div)) / div) + 1);
+    }
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    if (d == 1) return n;
+    const uint32_t t = __umulhi(n, magic);
+    return (((n - t) >> 1) + t) >> (shift - 1);
+  }
+};
+
+// The permutation handed to this source holds the PIXEL of each sorted point
+// and `depth` is in sorted order too (both written by dc_stream_kernel), so a
+// row is one context vector times one scalar with no index arithmetic.
 struct DepthContextRows {
-  const float* depth;   // [n]   one value per frustum point
+  const float* depth;   // [n] depth of the sorted points
   const float* ctx_t;   // [pixels, C]
   int64_t C;
-  uint32_t dhw;         // depth bins x feature-map pixels of one camera
-  uint32_t hw;          // feature-map pixels of one camera
   const float* base;
   __device__ __forceinline__ void bind(int v0, int lane) { base = ctx_t + (int64_t)(v0 + lane) * 4; }
-  __device__ __forceinline__ void load(uint32_t pid, float (&v)[4]) const {
-    const uint32_t cam = pid / dhw, pix = cam * hw + (pid - cam * dhw) % hw;
-    VecIO<float, 4>::load(base + (int64_t)pix * C, v);
-    const float d = __ldg(depth + pid);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(d, v[q]);
+  __device__ __forceinline__ void load(uint32_t pix, uint32_t pos, float (&v)[4]) const {
+    // context rows are shared by a pixel's depth bins: keep them in L1
+    const float4 q = __ldg(reinterpret_cast<const float4*>(base + (int64_t)pix * C));
+    const float d = __ldg(depth + pos);
+    v[0] = __fmul_rn(d, q.x); v[1] = __fmul_rn(d, q.y); v[2] = __fmul_rn(d, q.z); v[3] = __fmul_rn(d, q.w);
   }
 };
 
 // Sum of one cell's rows in ascending point order, software-pipelined: the
 // loads of the next U rows are in flight while the current U are added.
 template <int VE, int U, class Src>
-__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, int cnt, const Src& src,
-                                                   bool active, float (&acc)[VE]) {
+__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, uint32_t pos0, int cnt,
+                                                   const Src& src, bool active, float (&acc)[VE]) {
   float va[U][VE], vb[U][VE];
   auto load = [&](int k, float (&v)[U][VE]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (k + u < cnt && active) {
-        src.load(pids[k + u], v[u]);
+        src.load(pids[k + u], pos0 + k + u, v[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
@@ -500,7 +520,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
 #pragma unroll
     for (int q = 0; q < VE; ++q) acc[q] = 0.f;
     if (staged) {
-      sum_cell_pipelined<VE, PU>(s_perm + beg, cnt, src, active, acc);
+      sum_cell_pipelined<VE, PU>(s_perm + beg, (uint32_t)(pa + beg), cnt, src, active, acc);
     } else {
       PermStream ps;
       if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
@@ -515,7 +535,7 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
             pid = ps.at(pa + beg + k + u, lane);
           }
           if (k + u < cnt && active) {
-            src.load(pid, v[u]);
+            src.load(pid, (uint32_t)(pa + beg + k + u), v[u]);
           } else {
 #pragma unroll
             for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
@@ -971,81 +991,115 @@ struct DcDims {
   __host__ __device__ int64_t n() const { return cams * nd * hw; }
 };
 
-// Per frustum point, in pixel-major order [cam][hw][nd]: its cell (or -1 when
-// outside the grid) and its depth value.
+// Cell of every frustum point in input order, or -1 outside the grid.
 template <class IT>
-__global__ void dc_point_table_kernel(const IT* __restrict__ coords, const float* __restrict__ depth, DcDims dm,
-                                      int64_t B, int64_t D, int64_t H, int64_t W, int32_t* __restrict__ key_t,
-                                      float* __restrict__ depth_t) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= dm.n()) return;
+__global__ void dc_keys_kernel(const IT* __restrict__ coords, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
+                               int32_t* __restrict__ keys) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
   int64_t x, y, z, b;
-  load_coord<IT>(coords, n, x, y, z, b);
+  load_coord<IT>(coords, p, x, y, z, b);
   const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W && (uint64_t)z < (uint64_t)D &&
                   (uint64_t)b < (uint64_t)B;
-  const int64_t cam = n / (dm.nd * dm.hw), rem = n - cam * dm.nd * dm.hw;
-  const int64_t d = rem / dm.hw, p = rem - d * dm.hw;
-  const int64_t t = (cam * dm.hw + p) * dm.nd + d;
-  key_t[t] = ok ? (int32_t)(((b * D + z) * H + x) * W + y) : -1;
-  depth_t[t] = depth[n];
+  keys[p] = ok ? (int32_t)(((b * D + z) * H + x) * W + y) : -1;
+}
+
+// Sorted-order stream of the fused forward: pixel and depth of every sorted point.
+__global__ void dc_stream_kernel(const uint32_t* __restrict__ perm, int64_t n, const float* __restrict__ depth,
+                                 FastDiv dhw, FastDiv hw, uint32_t* __restrict__ pix, float* __restrict__ dep) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const uint32_t pid = perm[p];
+  const uint32_t cam = dhw.div(pid);
+  const uint32_t r = pid - cam * dhw.d;
+  pix[p] = cam * hw.d + (r - hw.div(r) * hw.d);
+  dep[p] = __ldg(depth + pid);
 }
 
 // A warp per camera pixel walks its depth bins in order:
-//   grad_depth[n]     = sum_c grad[cell(n), c] * context[pixel, c]
+//   grad_depth[n]          = sum_c grad[cell(n), c] * context[pixel, c]
 //   grad_context[pixel, c] = sum_n depth[n] * grad[cell(n), c]   (ascending n)
-// g_t is grad_out transposed to [cell, C]; lanes hold 4 channels each.
+// g_t is grad_out transposed to [cell, C]; lanes hold 4 channels each.  The
+// 16 dot products of a chunk of 16 depth bins are finished together by a
+// reduce-scatter across the lanes (16 shuffles), lane j ending with bin j.
 __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restrict__ g_t, const float* __restrict__ ctx_t,
-                                                         const int32_t* __restrict__ key_t,
-                                                         const float* __restrict__ depth_t, DcDims dm,
-                                                         float* __restrict__ gdepth_t, float* __restrict__ gctx_t) {
+                                                         const int32_t* __restrict__ keys,
+                                                         const float* __restrict__ depth, DcDims dm,
+                                                         float* __restrict__ gdepth, float* __restrict__ gctx_t) {
   constexpr int U = 8;
   const int lane = threadIdx.x & 31;
   const int64_t pix = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (pix >= dm.cams * dm.hw) return;  // warp-uniform
+  const int64_t cam = pix / dm.hw, p = pix - cam * dm.hw;
   const int nv = (int)(dm.c / 4);
   const bool active = lane < nv;
   float cx[4] = {0.f, 0.f, 0.f, 0.f}, acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (active) VecIO<float, 4>::load(ctx_t + pix * dm.c + lane * 4, cx);
-  const int32_t* keys = key_t + pix * dm.nd;
-  const float* deps = depth_t + pix * dm.nd;
-  float* gdep = gdepth_t + pix * dm.nd;
+  // point of bin d: (cam * nd + d) * hw + p
+  const int64_t n0 = cam * dm.nd * dm.hw + p;
   for (int64_t base = 0; base < dm.nd; base += 32) {
     const int cnt = (int)min((int64_t)32, dm.nd - base);
-    const int32_t myk = lane < cnt ? __ldg(keys + base + lane) : -1;
-    const float myd = lane < cnt ? __ldg(deps + base + lane) : 0.f;
-    float mydot = 0.f;
-    for (int k0 = 0; k0 < cnt; k0 += U) {
-      float v[U][4];
+    const int64_t mine = n0 + (base + lane) * dm.hw;
+    const int32_t myk = lane < cnt ? __ldg(keys + mine) : -1;
+    const float myd = lane < cnt ? __ldg(depth + mine) : 0.f;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int32_t key = __shfl_sync(0xffffffffu, myk, (k0 + u) & 31);
-        if (k0 + u < cnt && key >= 0 && active) {
-          VecIO<float, 4>::load(g_t + (int64_t)key * dm.c + lane * 4, v[u]);
-        } else {
+    for (int h = 0; h < 2; ++h) {
+      float part[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[u][q] = 0.f;
-        }
-      }
+      for (int k0 = 0; k0 < 16; k0 += U) {
+        float v[U][4];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float dep = __shfl_sync(0xffffffffu, myd, (k0 + u) & 31);
-        float dot = 0.f;
+        for (int u = 0; u < U; ++u) {
+          const int32_t key = __shfl_sync(0xffffffffu, myk, 16 * h + k0 + u);
+          if (key >= 0 && active) {
+            VecIO<float, 4>::load(g_t + (int64_t)key * dm.c + lane * 4, v[u]);
+          } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          dot = __fadd_rn(dot, __fmul_rn(v[u][q], cx[q]));
-          acc[q] = __fadd_rn(acc[q], __fmul_rn(dep, v[u][q]));
+            for (int q = 0; q < 4; ++q) v[u][q] = 0.f;
+          }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (lane == ((k0 + u) & 31)) mydot = dot;
+        for (int u = 0; u < U; ++u) {
+          const float dep = __shfl_sync(0xffffffffu, myd, 16 * h + k0 + u);
+          float dot = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            dot = __fadd_rn(dot, __fmul_rn(v[u][q], cx[q]));
+            acc[q] = __fadd_rn(acc[q], __fmul_rn(dep, v[u][q]));
+          }
+          part[k0 + u] = dot;
+        }
       }
+      // reduce-scatter within each half-warp (lane bits 3..0), then across halves
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1) {
+        const bool upper = (lane & w) != 0;
+#pragma unroll
+        for (int i = 0; i < w; ++i) {
+          const float send = upper ? part[i] : part[i + w];
+          const float keep = upper ? part[i + w] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+        }
+      }
+      part[0] += __shfl_xor_sync(0xffffffffu, part[0], 16);
+      const int bin = 16 * h + (lane & 15);
+      if (lane < 16 && bin < cnt) gdepth[n0 + (base + bin) * dm.hw] = part[0];
     }
-    if (lane < cnt) gdep[base + lane] = mydot;
   }
+
   if (active) {
     float* dst = gctx_t + pix * dm.c + lane * 4;
     *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
+}
+
+// Forward -> backward buffer: context transposed to [pixel, C], then the cell
+// of every frustum point.
+size_t dc_aux_bytes(const DcDims& dm) {
+  Carver cv(nullptr);
+  cv.take<float>((size_t)(dm.cams * dm.hw * dm.c));
+  cv.take<int32_t>((size_t)dm.n());
+  return cv.bytes();
 }
 
 int dc_check(const DcDims& dm, const Geometry& g) {
@@ -1066,13 +1120,10 @@ extern "C" int bfb_bev_pool_dc_workspace_sizes(int64_t cams, int64_t nd, int64_t
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
   BFB_TRY(dc_check(dm, g));
   BFB_TRY(bfb_bev_pool_workspace_sizes(dm.n(), c, B, D, H, W, plan_bytes, scratch_bytes));
-  if (aux_bytes) *aux_bytes = align_up(sizeof(float) * (size_t)(cams * dm.hw * c));
+  if (aux_bytes) *aux_bytes = dc_aux_bytes(dm);
   if (bwd_bytes) {
     Carver cv(nullptr);
     cv.take<float>((size_t)(g.cells * c));        // grad table [cell, C]
-    cv.take<int32_t>((size_t)dm.n());             // cell per point, pixel-major
-    cv.take<float>((size_t)dm.n());               // depth, pixel-major
-    cv.take<float>((size_t)dm.n());               // grad depth, pixel-major
     cv.take<float>((size_t)(cams * dm.hw * c));   // grad context [pixel, C]
     *bwd_bytes = cv.bytes();
   }
@@ -1089,16 +1140,39 @@ extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context,
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
   BFB_TRY(dc_check(dm, g));
   if (!depth || !context || !out) return BFB_ERR_INVALID_ARG;
-  if (!aux || aux_bytes < sizeof(float) * (size_t)(cams * dm.hw * c)) return BFB_ERR_WORKSPACE;
+  if (!aux || aux_bytes < dc_aux_bytes(dm)) return BFB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(aux) & 15) || (reinterpret_cast<uintptr_t>(out) & 3)) return BFB_ERR_INVALID_ARG;
+  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
   cudaStream_t st = as_stream(stream);
-  float* ctx_t = static_cast<float*>(aux);
+  Carver av(aux);
+  float* ctx_t = av.take<float>((size_t)(cams * dm.hw * c));
+  int32_t* keys = av.take<int32_t>((size_t)dm.n());
   BFB_TRY(launch_transpose(context, ctx_t, cams, c, dm.hw, st));  // [cam][C][hw] -> [cam][hw][C]
+  {
+    const unsigned nb = (unsigned)ceil_div(dm.n(), 256);
+    if (itype == BFB_I32)
+      dc_keys_kernel<int32_t><<<nb, 256, 0, st>>>(static_cast<const int32_t*>(coords), dm.n(), B, D, H, W, keys);
+    else
+      dc_keys_kernel<int64_t><<<nb, 256, 0, st>>>(static_cast<const int64_t*>(coords), dm.n(), B, D, H, W, keys);
+    BFB_CHECK_LAUNCH();
+  }
   BFB_TRY(bfb_bev_pool_plan(coords, itype, dm.n(), B, D, H, W, plan, plan_bytes, scratch, scratch_bytes, stream));
   PlanView pv;
   carve_plan(plan, g, &pv);
-  DepthContextRows src{depth, ctx_t, c, (uint32_t)(nd * dm.hw), (uint32_t)dm.hw, nullptr};
-  return launch_fwd_v<float, 4, 8>(src, c, g, pv, out, st);
+  if (nd * dm.hw > 0xffffffffLL || dm.n() > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
+  // the plan's scratch is free again: sorted pixel / depth streams
+  Carver sc(scratch);
+  uint32_t* spix = sc.take<uint32_t>((size_t)dm.n());
+  float* sdep = sc.take<float>((size_t)dm.n());
+  if (sc.bytes() > scratch_bytes) return BFB_ERR_WORKSPACE;
+  dc_stream_kernel<<<(unsigned)ceil_div(dm.n(), 256), 256, 0, st>>>(pv.perm, dm.n(), depth,
+                                                                   FastDiv((uint32_t)(nd * dm.hw)),
+                                                                   FastDiv((uint32_t)dm.hw), spix, sdep);
+  BFB_CHECK_LAUNCH();
+  PlanView sv = pv;
+  sv.perm = spix;
+  DepthContextRows src{sdep, ctx_t, c, nullptr};
+  return launch_fwd_v<float, 4, 8>(src, c, g, sv, out, st);
 }
 
 extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* depth, const void* coords, int itype,
@@ -1112,30 +1186,21 @@ extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* dept
   BFB_TRY(dc_check(dm, g));
   if (!grad_out || !depth || !coords || !grad_depth || !grad_context) return BFB_ERR_INVALID_ARG;
   if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
-  if (!aux || aux_bytes < sizeof(float) * (size_t)(cams * dm.hw * c)) return BFB_ERR_WORKSPACE;
+  if (!aux || aux_bytes < dc_aux_bytes(dm)) return BFB_ERR_WORKSPACE;
   size_t need = 0;
   BFB_TRY(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, nullptr, nullptr, nullptr, &need));
   if (!ws || ws_bytes < need) return BFB_ERR_WORKSPACE;
+  Carver av(const_cast<void*>(aux));
+  const float* ctx_t = av.take<float>((size_t)(cams * dm.hw * c));
+  const int32_t* keys = av.take<int32_t>((size_t)dm.n());
   Carver cv(ws);
   float* g_t = cv.take<float>((size_t)(g.cells * c));
-  int32_t* key_t = cv.take<int32_t>((size_t)dm.n());
-  float* depth_t = cv.take<float>((size_t)dm.n());
-  float* gdepth_t = cv.take<float>((size_t)dm.n());
   float* gctx_t = cv.take<float>((size_t)(cams * dm.hw * c));
   cudaStream_t st = as_stream(stream);
   BFB_TRY(launch_transpose(grad_out, g_t, B, c, g.dhw, st));  // [B][C][DHW] -> [B][DHW][C]
-  const unsigned nb = (unsigned)ceil_div(dm.n(), 256);
-  if (itype == BFB_I32)
-    dc_point_table_kernel<int32_t><<<nb, 256, 0, st>>>(static_cast<const int32_t*>(coords), depth, dm, B, D, H, W,
-                                                       key_t, depth_t);
-  else
-    dc_point_table_kernel<int64_t><<<nb, 256, 0, st>>>(static_cast<const int64_t*>(coords), depth, dm, B, D, H, W,
-                                                       key_t, depth_t);
+  dc_backward_kernel<<<(unsigned)ceil_div(cams * dm.hw * 32, 256), 256, 0, st>>>(g_t, ctx_t, keys, depth, dm,
+                                                                                 grad_depth, gctx_t);
   BFB_CHECK_LAUNCH();
-  dc_backward_kernel<<<(unsigned)ceil_div(cams * dm.hw * 32, 256), 256, 0, st>>>(
-      g_t, static_cast<const float*>(aux), key_t, depth_t, dm, gdepth_t, gctx_t);
-  BFB_CHECK_LAUNCH();
-  BFB_TRY(launch_transpose(gdepth_t, grad_depth, cams, dm.hw, nd, st));   // [cam][hw][nd] -> [cam][nd][hw]
   BFB_TRY(launch_transpose(gctx_t, grad_context, cams, dm.hw, c, st));    // [cam][hw][C] -> [cam][C][hw]
   return BFB_OK;
 }
