@@ -190,7 +190,9 @@ def scatter_cases(spt):
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference').resolve()
+    if len(sys.argv) < 2:
+        raise SystemExit('usage: make_golden.py <path to the bevfusion-triton checkout>')
+    ref = Path(sys.argv[1]).resolve()
     bpt, vt, spt = import_reference(ref)
     torch.set_num_threads(8)
     digests = {}
