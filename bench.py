@@ -48,8 +48,8 @@ FALLBACK_HBM_GBS = 6650.0
 # ncu capture of a one-sample launch summarised in profiles/; traffic grows in
 # proportion to the points, so a launch's traffic is this times its points.
 NCU_TRAFFIC_PER_POINT = {
-    'bev_fwd_kernel': 349.0,  # profiles/bev_fwd_bwd_kernels_det1.md
-    'bev_bwd_kernel': 313.0,
+    'bev_fwd_kernel': 340.6,  # profiles/bev_fwd_bwd_kernels_det1.md
+    'bev_bwd_kernel': 313.8,
 }
 
 
