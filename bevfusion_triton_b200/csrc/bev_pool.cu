@@ -76,6 +76,7 @@ int make_geometry(int64_t n, int64_t B, int64_t D, int64_t H, int64_t W, Geometr
 struct PlanView {
   PlanHeader* hdr;
   uint32_t* perm;
+  uint32_t* pkey;  // cell rank of every point in input order (sentinel = dropped)
   int2* cell_se;
   int4* pieces;
 };
@@ -94,6 +95,7 @@ size_t carve_plan(void* base, const Geometry& g, PlanView* v) {
   Carver c(base);
   v->hdr = c.take<PlanHeader>(1);
   v->perm = c.take<uint32_t>((size_t)g.n);
+  v->pkey = c.take<uint32_t>((size_t)g.n);
   v->cell_se = c.take<int2>((size_t)g.cells + 1);
   v->pieces = c.take<int4>((size_t)g.max_pieces);
   return c.bytes();
@@ -138,8 +140,8 @@ __device__ __forceinline__ void load_coord<int64_t>(const int64_t* coords, int64
 template <class IT>
 __global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
     const IT* __restrict__ coords, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
-    uint32_t* __restrict__ keys, int bits0, uint32_t* __restrict__ hist, int64_t ntiles,
-    PlanHeader* hdr) {
+    uint32_t* __restrict__ keys, uint32_t* __restrict__ pkey, int bits0, uint32_t* __restrict__ hist,
+    int64_t ntiles, PlanHeader* hdr) {
   extern __shared__ uint32_t s_hist[];
   const int nd = 1 << bits0;
   for (int i = threadIdx.x; i < skewed_size(nd); i += kRadixThreads) s_hist[i] = 0;
@@ -156,6 +158,7 @@ __global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
     const uint32_t k = ok ? (uint32_t)(((b * D + z) * H + x) * W + y) : sentinel;
     bad += ok ? 0u : 1u;
     keys[p] = k;
+    pkey[p] = k;
     atomicAdd(&s_hist[skew((int)(k & ((1u << bits0) - 1u)))], 1u);
   }
   // one atomic per warp for the dropped-point counter
@@ -698,6 +701,134 @@ __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// 7b. backward in gather form (needs a workspace of one row per grid cell)
+//
+// bev_rows_kernel copies grad_out[b, :, cell] of every non-empty cell into a
+// [cell][C] row buffer (a few tens of MB for a det sample, so it stays in L2);
+// bev_gather_kernel then walks the points in input order, reads each point's
+// cell rank (pkey, written by the plan) and its row from that buffer, and
+// writes grad_feats as one contiguous stream.  Same result as bev_bwd_kernel;
+// the output writes are sequential instead of 320-byte rows scattered over
+// the whole buffer.
+// ---------------------------------------------------------------------------
+template <class T, int VE>
+struct alignas(VE * sizeof(T) == 16 ? 16 : sizeof(T)) Vec {
+  T e[VE];
+};
+template <class T, int VE>
+__device__ __forceinline__ Vec<T, VE> load_vec(const Vec<T, VE>* p) {
+  if constexpr (VE * sizeof(T) == 16) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    return *reinterpret_cast<const Vec<T, VE>*>(&r);
+  } else {
+    Vec<T, VE> v;
+#pragma unroll
+    for (int i = 0; i < VE; ++i) v.e[i] = __ldg(p->e + i);
+    return v;
+  }
+}
+template <class T, int VE>
+__device__ __forceinline__ void store_vec(T* p, const Vec<T, VE>& v) {
+  if constexpr (VE * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(v.e);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VE; ++i) p[i] = v.e[i];
+  }
+}
+
+constexpr int kRowsBatch = 5;  // channel vectors loaded before the first store
+
+// One CTA per tile of 32 cells; lane = cell.  Each warp takes kRowsBatch
+// channel vectors at a time: their channel-plane segments are read coalesced
+// (32-byte sectors without a non-empty cell skipped), then each non-empty
+// cell stores the vectors into its row.
+template <class T, int VE>
+__global__ __launch_bounds__(kPoolThreads) void bev_rows_kernel(const T* __restrict__ gout, int64_t C, int nvec,
+                                                                int64_t dhw, int64_t tpb,
+                                                                const int2* __restrict__ cell_se,
+                                                                T* __restrict__ rows) {
+  const int64_t t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t r0, s0;
+  const int nc = tile_cells(t, tpb, dhw, &r0, &s0);
+  bool need = false;
+  if (lane < nc) {
+    const int2 se = __ldg(cell_se + r0 + lane);
+    need = se.y > se.x;
+  }
+  const unsigned nz = __ballot_sync(0xffffffffu, need);
+  if (nz == 0u) return;
+  const bool load = lane < nc && ((nz >> (lane & ~7)) & 0xffu);
+  const int64_t b = t / tpb;
+  const T* src = gout + b * C * dhw + s0 + lane;
+  T* dst = rows + (r0 + lane) * C;
+  for (int j0 = warp * kRowsBatch; j0 < nvec; j0 += kPoolWarps * kRowsBatch) {
+    Vec<T, VE> q[kRowsBatch];
+#pragma unroll
+    for (int u = 0; u < kRowsBatch; ++u) {
+      const int j = j0 + u;
+#pragma unroll
+      for (int i = 0; i < VE; ++i)
+        q[u].e[i] = (load && j < nvec) ? __ldg(src + (int64_t)(j * VE + i) * dhw) : from_f32<T>(0.f);
+    }
+    if (need) {
+#pragma unroll
+      for (int u = 0; u < kRowsBatch; ++u)
+        if (j0 + u < nvec) store_vec<T, VE>(dst + (j0 + u) * VE, q[u]);
+    }
+  }
+}
+
+constexpr int kGatherThreads = 256;
+constexpr int kGatherPoints = 256;  // points per CTA
+constexpr int kGatherBatch = 5;     // loads in flight per thread
+
+template <class T, int VE>
+__global__ __launch_bounds__(kGatherThreads) void bev_gather_kernel(const T* __restrict__ rows,
+                                                                    const uint32_t* __restrict__ pkey,
+                                                                    uint32_t sentinel, int64_t n, int nvec,
+                                                                    FastDiv dv, T* __restrict__ gfeat) {
+  using V = Vec<T, VE>;
+  const int64_t p0 = (int64_t)blockIdx.x * kGatherPoints;
+  const uint32_t np = (uint32_t)min((int64_t)kGatherPoints, n - p0);
+  const uint32_t total = np * (uint32_t)nvec;  // channel vectors of this CTA's points
+  const V* rv = reinterpret_cast<const V*>(rows);
+  V* out = reinterpret_cast<V*>(gfeat) + p0 * nvec;
+  __shared__ uint32_t s_key[kGatherPoints];
+  for (uint32_t i = threadIdx.x; i < np; i += kGatherThreads) s_key[i] = __ldg(pkey + p0 + i);
+  __syncthreads();
+  for (uint32_t l0 = threadIdx.x; l0 < total; l0 += kGatherThreads * kGatherBatch) {
+    V q[kGatherBatch];
+#pragma unroll
+    for (int u = 0; u < kGatherBatch; ++u) {
+      const uint32_t l = l0 + u * kGatherThreads;
+      if (l < total) {
+        const uint32_t p = dv.div(l);
+        const uint32_t ch = l - p * (uint32_t)nvec;
+        const uint32_t k = s_key[p];
+        if (k != sentinel) {
+          q[u] = load_vec<T, VE>(rv + (int64_t)k * nvec + ch);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VE; ++i) q[u].e[i] = from_f32<T>(0.f);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherBatch; ++u) {
+      const uint32_t l = l0 + u * kGatherThreads;
+      if (l < total) {
+        if constexpr (VE * sizeof(T) == 16)
+          st_stream16(out + l, *reinterpret_cast<const uint4*>(q[u].e));
+        else
+          out[l] = q[u];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 template <class T, int VE, int PU, class Src>
@@ -743,6 +874,20 @@ int launch_bwd(const void* gout, int64_t C, const Geometry& g, const PlanView& p
   return BFB_OK;
 }
 
+template <class T, int VE>
+int launch_bwd_gather(const void* gout, int64_t C, const Geometry& g, const PlanView& pv, void* rows,
+                      void* gfeat, cudaStream_t st) {
+  const int nvec = (int)(C / VE);
+  bev_rows_kernel<T, VE><<<(unsigned)g.tiles, kPoolThreads, 0, st>>>(
+      static_cast<const T*>(gout), C, nvec, g.dhw, g.tpb, pv.cell_se, static_cast<T*>(rows));
+  BFB_CHECK_LAUNCH();
+  bev_gather_kernel<T, VE><<<(unsigned)ceil_div(g.n, kGatherPoints), kGatherThreads, 0, st>>>(
+      static_cast<const T*>(rows), pv.pkey, (uint32_t)g.cells, g.n, nvec, FastDiv((uint32_t)nvec),
+      static_cast<T*>(gfeat));
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
 bool vec16_ok(const void* p, int64_t C, int esz) {
   return (C * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
@@ -776,6 +921,24 @@ int run_bwd(int dtype, const void* gout, int64_t C, const Geometry& g, const Pla
     case BFB_BF16:
       return vec16_ok(gfeat, C, 2) ? launch_bwd<__nv_bfloat16, 8>(gout, C, g, pv, gfeat, st)
                                    : launch_bwd<__nv_bfloat16, 1>(gout, C, g, pv, gfeat, st);
+    default:
+      return BFB_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int run_bwd_gather(int dtype, const void* gout, int64_t C, const Geometry& g, const PlanView& pv, void* rows,
+                   void* gfeat, cudaStream_t st) {
+  const bool v16 = vec16_ok(gfeat, C, dtype_size(dtype)) && vec16_ok(gout, 0, 1) && vec16_ok(rows, 0, 1);
+  switch (dtype) {
+    case BFB_F32:
+      return v16 ? launch_bwd_gather<float, 4>(gout, C, g, pv, rows, gfeat, st)
+                 : launch_bwd_gather<float, 1>(gout, C, g, pv, rows, gfeat, st);
+    case BFB_F16:
+      return v16 ? launch_bwd_gather<__half, 8>(gout, C, g, pv, rows, gfeat, st)
+                 : launch_bwd_gather<__half, 1>(gout, C, g, pv, rows, gfeat, st);
+    case BFB_BF16:
+      return v16 ? launch_bwd_gather<__nv_bfloat16, 8>(gout, C, g, pv, rows, gfeat, st)
+                 : launch_bwd_gather<__nv_bfloat16, 1>(gout, C, g, pv, rows, gfeat, st);
     default:
       return BFB_ERR_UNSUPPORTED_DTYPE;
   }
@@ -825,10 +988,10 @@ extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64
     const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
     if (itype == BFB_I32)
       bev_keys_kernel<int32_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
-          static_cast<const int32_t*>(coords), n, B, D, H, W, sv.keys0, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
+          static_cast<const int32_t*>(coords), n, B, D, H, W, sv.keys0, pv.pkey, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
     else
       bev_keys_kernel<int64_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
-          static_cast<const int64_t*>(coords), n, B, D, H, W, sv.keys0, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
+          static_cast<const int64_t*>(coords), n, B, D, H, W, sv.keys0, pv.pkey, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
     BFB_CHECK_LAUNCH();
     BFB_TRY(radix_sort_index(sv.keys0, sv.keys1, sv.vtmp, pv.perm, n, rp, sv.hist, sv.scan,
                              /*hist0_ready=*/true, st, &keys_sorted));
@@ -889,6 +1052,38 @@ extern "C" int bfb_bev_pool_backward(const void* gout, int dtype, int64_t n, int
   if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
   carve_plan(const_cast<void*>(plan), g, &pv);
   return run_bwd(dtype, gout, c, g, pv, gfeat, as_stream(stream));
+}
+
+extern "C" int bfb_bev_pool_backward_workspace_size(int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
+                                                   int64_t W, int dtype, size_t* bytes) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  BFB_TRY(check_channels(c));
+  const size_t esz = dtype_size(dtype);
+  if (esz == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!bytes) return BFB_ERR_INVALID_ARG;
+  *bytes = (size_t)g.cells * (size_t)c * esz;
+  return BFB_OK;
+}
+
+extern "C" int bfb_bev_pool_backward_gather(const void* gout, int dtype, int64_t n, int64_t c, int64_t B,
+                                            int64_t D, int64_t H, int64_t W, const void* plan,
+                                            size_t plan_bytes, void* gfeat, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  BFB_TRY(check_channels(c));
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (!plan) return BFB_ERR_WORKSPACE;
+  if (n == 0) return BFB_OK;
+  if (!gout || !gfeat) return BFB_ERR_INVALID_ARG;
+  size_t need = 0;
+  BFB_TRY(bfb_bev_pool_backward_workspace_size(n, c, B, D, H, W, dtype, &need));
+  if (!workspace || workspace_bytes < need) return BFB_ERR_WORKSPACE;
+  PlanView pv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
+  carve_plan(const_cast<void*>(plan), g, &pv);
+  return run_bwd_gather(dtype, gout, c, g, pv, workspace, gfeat, as_stream(stream));
 }
 
 extern "C" int bfb_bev_pool_invalid_count(const void* plan, int64_t* count, void* stream) {

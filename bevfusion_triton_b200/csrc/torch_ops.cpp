@@ -108,9 +108,22 @@ at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, 
               "grad_out must have shape [B, C, D, H, W]");
   const int64_t c = grad.size(1);
   auto gfeat = at::empty({n, c}, grad.options());
-  check(bfb_bev_pool_backward(grad.data_ptr(), dtype_code(grad), n, c, B, D, H, W, plan.data_ptr(),
-                              (size_t)plan.numel(), gfeat.data_ptr(), stream_of(grad)),
-        "bev_pool backward");
+  // Gather form when its row buffer (one row per grid cell) is no larger than
+  // grad_feats itself; the scatter form needs no buffer.
+  size_t rows_bytes = 0;
+  check(bfb_bev_pool_backward_workspace_size(n, c, B, D, H, W, dtype_code(grad), &rows_bytes),
+        "bev_pool backward workspace");
+  if (n > 0 && rows_bytes <= (size_t)gfeat.numel() * gfeat.element_size()) {
+    auto rows = at::empty({(int64_t)rows_bytes}, grad.options().dtype(at::kByte));
+    check(bfb_bev_pool_backward_gather(grad.data_ptr(), dtype_code(grad), n, c, B, D, H, W, plan.data_ptr(),
+                                       (size_t)plan.numel(), gfeat.data_ptr(), rows.data_ptr(), rows_bytes,
+                                       stream_of(grad)),
+          "bev_pool backward");
+  } else {
+    check(bfb_bev_pool_backward(grad.data_ptr(), dtype_code(grad), n, c, B, D, H, W, plan.data_ptr(),
+                                (size_t)plan.numel(), gfeat.data_ptr(), stream_of(grad)),
+          "bev_pool backward");
+  }
   return gfeat;
 }
 

@@ -108,6 +108,20 @@ int bfb_bev_pool_backward(const void* grad_out_dev, int dtype, int64_t n, int64_
                           int64_t D, int64_t H, int64_t W, const void* plan_dev,
                           size_t plan_bytes, void* grad_feats_dev, void* stream);
 
+/* The same backward in gather form: grad_out rows of the non-empty cells are
+ * first copied into `workspace_dev` (one row of c elements per grid cell,
+ * B*D*H*W*c*sizeof(dtype) bytes, from bfb_bev_pool_backward_workspace_size),
+ * then grad_feats is written in point order as one contiguous stream.  Same
+ * result as bfb_bev_pool_backward, bit for bit; faster when the row buffer is
+ * small next to grad_feats (dense point clouds such as the LSS frustum). */
+int bfb_bev_pool_backward_workspace_size(int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
+                                         int64_t W, int dtype, size_t* bytes);
+
+int bfb_bev_pool_backward_gather(const void* grad_out_dev, int dtype, int64_t n, int64_t c,
+                                 int64_t B, int64_t D, int64_t H, int64_t W, const void* plan_dev,
+                                 size_t plan_bytes, void* grad_feats_dev, void* workspace_dev,
+                                 size_t workspace_bytes, void* stream);
+
 /* Fused camera branch: bev_pool of feats[n, c] = depth[n] * context[cam, c, h, w]
  * without materialising feats.  Replaces models/vtransforms/depth_lss.py:91-94
  * (softmax(depth) (x) context) followed by models/vtransforms/base.py:136-160

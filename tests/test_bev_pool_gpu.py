@@ -207,3 +207,37 @@ def test_det_batch8_fp16_features(cuda):
     s = ((idx[:, 2] * case.H + idx[:, 0]) * case.W + idx[:, 1]).cuda()
     want = up.reshape(case.B, up.size(1), -1).permute(0, 2, 1)[idx[:, 3].cuda(), s]
     assert torch.equal(x.grad, want)
+
+
+@pytest.mark.parametrize('case', CASES[1:], ids=lambda c: f'n{c[0]}_c{c[1]}_B{c[2]}')
+@pytest.mark.parametrize('fdtype', [torch.float32, torch.float16, torch.bfloat16])
+def test_backward_gather_equals_scatter(cuda, case, fdtype):
+    """Both backward forms of the C ABI (scatter: no workspace; gather: one
+    row per grid cell) give the oracle's gradient exactly."""
+    from bevfusion_triton_b200 import load_native
+    L = load_native()
+    n, c, B, D, H, W, cdtype, hot, invalid = case
+    feats, coords = rand_bev_case(n, c, B, D, H, W, seed=n + c, cdtype=cdtype, fdtype=fdtype, hot=hot,
+                                  invalid=invalid)
+    plan = bev_pool_plan(coords.cuda(), B, D, H, W)
+    up = torch.randn((B, c, D, H, W), generator=torch.Generator().manual_seed(5)).to(fdtype).cuda()
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[fdtype]
+    i64, vp = ctypes.c_int64, ctypes.c_void_p
+    stream = vp(torch.cuda.current_stream().cuda_stream)
+    dims = [i64(v) for v in (n, c, B, D, H, W)]
+    g_scatter = torch.full((n, c), 7, dtype=fdtype, device='cuda')
+    assert L.bfb_bev_pool_backward(vp(up.data_ptr()), code, *dims, vp(plan.data_ptr()), ctypes.c_size_t(plan.numel()),
+                                   vp(g_scatter.data_ptr()), stream) == 0
+    ws_b = ctypes.c_size_t()
+    assert L.bfb_bev_pool_backward_workspace_size(*dims, code, ctypes.byref(ws_b)) == 0
+    assert ws_b.value == B * D * H * W * c * up.element_size()
+    ws = torch.empty(ws_b.value, dtype=torch.uint8, device='cuda')
+    g_gather = torch.full((n, c), 7, dtype=fdtype, device='cuda')
+    args = [vp(up.data_ptr()), code, *dims, vp(plan.data_ptr()), ctypes.c_size_t(plan.numel()),
+            vp(g_gather.data_ptr()), vp(ws.data_ptr())]
+    assert L.bfb_bev_pool_backward_gather(*args, ctypes.c_size_t(ws_b.value - 1), stream) == -3
+    assert L.bfb_bev_pool_backward_gather(*args, ws_b, stream) == 0
+    torch.cuda.synchronize()
+    rgrad = oracle.bev_pool_backward(up.float().cpu().numpy(), coords.numpy(), B, D, H, W)
+    np.testing.assert_array_equal(g_gather.float().cpu().numpy(), rgrad)
+    assert torch.equal(g_gather, g_scatter)
