@@ -49,8 +49,8 @@ FALLBACK_HBM_GBS = 6650.0
 # proportion to the points, so a launch's traffic is this times its points.
 NCU_TRAFFIC_PER_POINT = {
     'bev_fwd_kernel': 340.6,  # profiles/bev_fwd_bwd_kernels_det1.md
-    # backward: bev_rows_kernel (37.3 MB) + bev_gather_kernel (531.8 MB) of one sample
-    'bev_rows_kernel+bev_gather_kernel': 321.4,
+    # backward: bev_rows_kernel (37.3 MB) + bev_gather_kernel (533.7 MB) of one sample
+    'bev_rows_kernel+bev_gather_kernel': 322.4,
 }
 
 

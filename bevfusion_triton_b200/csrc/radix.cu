@@ -45,7 +45,7 @@ __global__ __launch_bounds__(kRadixThreads) void radix_upsweep_kernel(const uint
 // input order within a digit) into shared memory, then every digit's run is
 // written to its global slot with consecutive threads on consecutive
 // addresses, so global writes are whole sectors.
-__global__ __launch_bounds__(kRadixThreads, 1) void radix_downsweep_kernel(
+__global__ __launch_bounds__(kRadixThreads, 2) void radix_downsweep_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     int bits, const uint32_t* __restrict__ hist, int64_t ntiles) {
@@ -57,6 +57,7 @@ __global__ __launch_bounds__(kRadixThreads, 1) void radix_downsweep_kernel(
   uint32_t* s_key = s_off + kRadixWarps * row;       // [kRadixTile]
   uint32_t* s_val = s_key + kRadixTile;              // [kRadixTile]
   uint32_t* s_gbase = s_val + kRadixTile;            // [row] global digit start - local start
+  unsigned char* s_own = reinterpret_cast<unsigned char*>(s_gbase + row);  // [kRadixWarps][row] lane per digit
   __shared__ uint32_t s_ws[kRadixWarps];
   const uint32_t dmask = (uint32_t)nd - 1u;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -75,28 +76,28 @@ __global__ __launch_bounds__(kRadixThreads, 1) void radix_downsweep_kernel(
   const unsigned lt = lanemask_lt();
   __syncthreads();
 
-  // A: per-warp digit counts; one leader per distinct digit in a step
+  // A: per-warp digit counts (order does not matter here: shared atomics)
 #pragma unroll
   for (int j = 0; j < kSteps; ++j) {
     const bool valid = start + j * 32 + lane < n;
-    const uint32_t d = (k[j] >> shift) & dmask;
-    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
-    if (valid && (peers & lt) == 0) my[skew((int)d)] += __popc(peers);
-    __syncwarp();
+    if (valid) atomicAdd(&my[skew((int)((k[j] >> shift) & dmask))], 1u);
   }
   __syncthreads();
 
   // B: tile totals per digit -> tile-local digit starts (block scan over
   // digits, up to two digits per thread) and per-warp local offsets
-  const int per_thread = (nd + kRadixThreads - 1) / kRadixThreads;  // 1 or 2
-  uint32_t tot[2] = {0u, 0u};
+  constexpr int kMaxPer = ((1 << kRadixMaxBits) + kRadixThreads - 1) / kRadixThreads;
+  const int per_thread = (nd + kRadixThreads - 1) / kRadixThreads;  // <= kMaxPer
+  uint32_t tot[kMaxPer] = {};
   for (int q = 0; q < per_thread; ++q) {
     const int d = threadIdx.x * per_thread + q;
     if (d < nd)
       for (int w = 0; w < kRadixWarps; ++w) tot[q] += s_off[w * row + skew(d)];
   }
   {
-    const uint32_t mine = tot[0] + tot[1];
+    uint32_t mine = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) mine += tot[q];
     uint32_t x = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -131,21 +132,40 @@ __global__ __launch_bounds__(kRadixThreads, 1) void radix_downsweep_kernel(
   }
   __syncthreads();
 
-  // C: stable rank within the tile -> shared memory
+  // C: stable rank within the tile -> shared memory.  A step whose 32 digits
+  // are all different (over half the steps for keys in camera-frustum order)
+  // needs no ranking: each lane claims its digit's slot in a per-warp byte
+  // table and the warp checks that every lane still owns its slot.
+  // Otherwise equal digits are ranked by lane with __match_any_sync.
+  unsigned char* own = s_own + warp * row;
+  const bool full_warp = start + kRadixWarpItems <= n;
 #pragma unroll
   for (int j = 0; j < kSteps; ++j) {
     const bool valid = start + j * 32 + lane < n;
     const uint32_t d = (k[j] >> shift) & dmask;
-    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
-    const uint32_t rank = __popc(peers & lt);
     const int sd = skew((int)d);
-    if (valid) {
-      const uint32_t pos = my[sd] + rank;
+    bool clash = true;
+    if (full_warp) {
+      own[sd] = (unsigned char)lane;
+      __syncwarp();
+      clash = __any_sync(0xffffffffu, own[sd] != (unsigned char)lane);
+    }
+    if (!clash) {
+      const uint32_t pos = my[sd];
       s_key[pos] = k[j];
       s_val[pos] = v[j];
+      my[sd] = pos + 1;
+    } else {
+      const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+      const uint32_t rank = __popc(peers & lt);
+      if (valid) {
+        const uint32_t pos = my[sd] + rank;
+        s_key[pos] = k[j];
+        s_val[pos] = v[j];
+      }
+      __syncwarp();
+      if (valid && rank == 0) my[sd] += __popc(peers);
     }
-    __syncwarp();
-    if (valid && rank == 0) my[sd] += __popc(peers);
     __syncwarp();
   }
   __syncthreads();
@@ -183,7 +203,8 @@ int radix_sort_index(uint32_t* keys0, uint32_t* keys1, uint32_t* vals_tmp, uint3
     }
     BFB_TRY(exclusive_scan_u32(hist, hist, (int64_t)nd * ntiles, scan_scratch, nullptr, stream));
     const size_t smem = ((size_t)kRadixWarps * skewed_size(nd) + 2 * (size_t)kRadixTile + skewed_size(nd)) *
-                        sizeof(uint32_t);
+                            sizeof(uint32_t) +
+                        (size_t)kRadixWarps * skewed_size(nd);
     if (smem > 48 * 1024)
       BFB_CUDA(cudaFuncSetAttribute(radix_downsweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem));

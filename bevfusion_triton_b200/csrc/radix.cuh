@@ -12,10 +12,10 @@
 
 namespace bfb {
 
-constexpr int kRadixWarps = 16;
-constexpr int kRadixThreads = kRadixWarps * 32;        // 512
+constexpr int kRadixWarps = 8;
+constexpr int kRadixThreads = kRadixWarps * 32;        // 256
 constexpr int kRadixWarpItems = 1024;                  // per warp
-constexpr int kRadixTile = kRadixWarps * kRadixWarpItems;  // 16384
+constexpr int kRadixTile = kRadixWarps * kRadixWarpItems;  // 8192
 constexpr int kRadixMaxBits = 10;                      // digit width
 
 // Shared-memory slot of digit d in a per-warp / per-block counter array: one
