@@ -410,8 +410,10 @@ def run_fused(args, rank, ws):
     """The camera branch from depth distribution and context to BEV (fwd+bwd)
     over the rank's det samples: unfused (depth x context product, flatten,
     in-grid filter, bev_pool, as models/vtransforms/depth_lss.py + base.py do)
-    vs the fused op that never materialises the feature tensor."""
-    from bevfusion_triton_b200.ops.bev_pool import bev_pool, bev_pool_depth_context
+    vs the fused op that never materialises the feature tensor; and both
+    again starting from the camera parameters (geometry + quantise + filter
+    in torch, against the geometry plan)."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool, bev_pool_depth_context, bev_pool_geometry_plan
     S = args.samples_per_gpu
     first, _ = shard.shard_samples(S * ws, ws, rank)
     case = synth.depth_context_case(S, synth.DET_GRID, device='cuda', sample_offset=first)
@@ -431,8 +433,29 @@ def run_fused(args, rank, ws):
         c = case.context.detach().requires_grad_(True)
         bev_pool_depth_context(d, c, case.coords, *shape).backward(up)
 
+    # the same branch from the camera parameters: the reference geometry,
+    # quantise and filter in torch, then the unfused pooling; against the
+    # geometry plan feeding the fused pooling (no coordinate tensor at all)
+    rig = synth.camera_rig(S, augment=True, seed=first, device='cuda')
+    bounds = {k: synth.DET_GRID[k] for k in ('xbound', 'ybound', 'zbound')}
+
+    def unfused_camera():
+        coords, kept, shp = synth.lss_coords(synth.lss_geometry(**rig), **bounds)
+        kidx = torch.nonzero(kept).squeeze(1)
+        d = case.depth.detach().requires_grad_(True)
+        c = case.context.detach().requires_grad_(True)
+        x = (d.unsqueeze(2) * c.unsqueeze(3)).permute(0, 1, 3, 4, 5, 2).reshape(-1, C)
+        bev_pool(x[kidx], coords[kidx], *shp).backward(up)
+
+    def fused_camera():
+        plan, shp = bev_pool_geometry_plan(**rig, **bounds)
+        d = case.depth.detach().requires_grad_(True)
+        c = case.context.detach().requires_grad_(True)
+        bev_pool_depth_context(d, c, None, *shp, plan=plan).backward(up)
+
     res = {}
-    for name, fn in (('unfused', unfused), ('fused', fused)):
+    for name, fn in (('unfused', unfused), ('fused', fused), ('unfused_from_camera', unfused_camera),
+                     ('fused_from_camera', fused_camera)):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -447,7 +470,10 @@ def run_fused(args, rank, ws):
         barrier(ws)
         res[name + '_ms_per_sample'] = round(max_over_ranks(s0.elapsed_time(s1), ws) / k / S, 4)
     res['speedup'] = round(res['unfused_ms_per_sample'] / res['fused_ms_per_sample'], 2)
-    res['note'] = 'det geometry, softmax depth (118 bins) x context (C=80), fp32, forward + backward'
+    res['speedup_from_camera'] = round(res['unfused_from_camera_ms_per_sample'] / res['fused_from_camera_ms_per_sample'], 2)
+    res['note'] = ('det grid, softmax depth (118 bins) x context (C=80), fp32, forward + backward; *_from_camera '
+                   'also computes the frustum geometry, quantisation and filter from the camera parameters '
+                   '(augmented rig)')
     return res
 
 

@@ -117,6 +117,25 @@ size_t carve_scratch(void* base, const Geometry& g, ScratchView* v) {
   return c.bytes();
 }
 
+// Division by a fixed 32-bit divisor with a multiply-high and shifts.
+struct FastDiv {
+  uint32_t d, magic, shift;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div), magic(0), shift(0) {
+    if (div > 1) {
+      uint32_t s = 0;
+      while ((1ull << s) < div) ++s;
+      shift = s;
+      magic = (uint32_t)((((1ull << 32) * ((1ull << s) - div)) / div) + 1);
+    }
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    if (d == 1) return n;
+    const uint32_t t = __umulhi(n, magic);
+    return (((n - t) >> 1) + t) >> (shift - 1);
+  }
+};
+
 // ---------------------------------------------------------------------------
 // 1. cell ranks
 // ---------------------------------------------------------------------------
@@ -137,25 +156,109 @@ __device__ __forceinline__ void load_coord<int64_t>(const int64_t* coords, int64
   x = c0.x; y = c0.y; z = c1.x; b = c1.y;
 }
 
+// Cell of point p from its (x, y, z, b) coordinates.
 template <class IT>
+struct CoordCells {
+  const IT* coords;
+  int64_t B, D, H, W;
+  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r) const {
+    int64_t x, y, z, b;
+    load_coord<IT>(coords, p, x, y, z, b);
+    const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W && (uint64_t)z < (uint64_t)D &&
+                    (uint64_t)b < (uint64_t)B;
+    *r = (uint32_t)(((b * D + z) * H + x) * W + y);
+    return ok;
+  }
+};
+
+// Cell of frustum point p straight from the camera parameters: the LSS
+// geometry (models/vtransforms/base.py:82-126) followed by the quantisation
+// and in-grid test of its bev_pool caller (base.py:131-158), so no coordinate
+// tensor is formed.  Points are ordered (b, cam, d, h, w) as the caller
+// flattens them.  Each row of a 3x3 product is (a0*p0 fused-added to a1*p1)
+// plus a2*p2 rounded separately, the association that reproduces torch's
+// CUDA broadcast matmul of these shapes on all but a few in a million
+// values (measured on the B200); `.long()` truncates toward zero.
+struct CameraCells {
+  const float* frustum;      // [D, fH, fW, 3] (u, v, depth)
+  const float* post_rots;    // [B*N, 3, 3]
+  const float* post_trans;   // [B*N, 3]
+  const float* combine;      // [B*N, 3, 3]  camera2lidar_rot @ intrins^-1
+  const float* trans;        // [B*N, 3]     camera2lidar translation
+  const float* extra_rots;   // [B, 3, 3] or null
+  const float* extra_trans;  // [B, 3] or null
+  FastDiv frustum_pts;       // D * fH * fW
+  FastDiv ncam;              // N
+  float lower[3], dx[3];     // bx - dx / 2 and dx
+  int64_t nz, nx, ny;        // grid cells along z, x, y
+
+  // one row of a 3x3 product: fma(a1, p1, a0 * p0) + a2 * p2
+  static __device__ __forceinline__ float row3(float a0, float a1, float a2, const float (&v)[3]) {
+    return __fadd_rn(__fmaf_rn(a1, v[1], __fmul_rn(a0, v[0])), __fmul_rn(a2, v[2]));
+  }
+
+  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r) const {
+    const uint32_t bn = frustum_pts.div((uint32_t)p);
+    const uint32_t f = (uint32_t)p - bn * frustum_pts.d;
+    const uint32_t b = ncam.div(bn);
+    float t[3], u[3], v[3], q[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) t[i] = __fsub_rn(__ldg(frustum + 3 * f + i), __ldg(post_trans + 3 * bn + i));
+    const float* pr = post_rots + 9 * bn;  // post_rots^T @ t
+#pragma unroll
+    for (int i = 0; i < 3; ++i) u[i] = row3(__ldg(pr + i), __ldg(pr + 3 + i), __ldg(pr + 6 + i), t);
+    v[0] = __fmul_rn(u[0], u[2]);
+    v[1] = __fmul_rn(u[1], u[2]);
+    v[2] = u[2];
+    const float* cm = combine + 9 * bn;
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+      q[i] = __fadd_rn(row3(__ldg(cm + 3 * i), __ldg(cm + 3 * i + 1), __ldg(cm + 3 * i + 2), v),
+                       __ldg(trans + 3 * bn + i));
+    if (extra_rots) {
+      const float* er = extra_rots + 9 * b;
+      float e[3];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) e[i] = row3(__ldg(er + 3 * i), __ldg(er + 3 * i + 1), __ldg(er + 3 * i + 2), q);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) q[i] = e[i];
+    }
+    if (extra_trans) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) q[i] = __fadd_rn(q[i], __ldg(extra_trans + 3 * b + i));
+    }
+    const int64_t lim[3] = {nx, ny, nz};
+    int64_t gi[3];
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const float c = truncf(__fdiv_rn(__fsub_rn(q[i], lower[i]), dx[i]));
+      ok = ok && c >= 0.f && c < (float)lim[i];  // false for NaN
+      gi[i] = ok ? (int64_t)c : 0;
+    }
+    *r = (uint32_t)((((int64_t)b * nz + gi[2]) * nx + gi[0]) * ny + gi[1]);
+    return ok;
+  }
+};
+
+// Cell rank of every point (the sentinel B*D*H*W for points outside the
+// grid) into the sort's key buffer and the plan's per-point copy, plus the
+// sort's first-digit histogram of this tile and the dropped-point count.
+template <class Src>
 __global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
-    const IT* __restrict__ coords, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
-    uint32_t* __restrict__ keys, uint32_t* __restrict__ pkey, int bits0, uint32_t* __restrict__ hist,
-    int64_t ntiles, PlanHeader* hdr) {
+    Src src, int64_t n, uint32_t sentinel, uint32_t* __restrict__ keys, uint32_t* __restrict__ pkey, int bits0,
+    uint32_t* __restrict__ hist, int64_t ntiles, PlanHeader* hdr) {
   extern __shared__ uint32_t s_hist[];
   const int nd = 1 << bits0;
   for (int i = threadIdx.x; i < skewed_size(nd); i += kRadixThreads) s_hist[i] = 0;
   __syncthreads();
-  const uint32_t sentinel = (uint32_t)(B * D * H * W);
   const int64_t base = (int64_t)blockIdx.x * kRadixTile;
   const int64_t end = min(n, base + kRadixTile);
   uint32_t bad = 0;
   for (int64_t p = base + threadIdx.x; p < end; p += kRadixThreads) {
-    int64_t x, y, z, b;
-    load_coord<IT>(coords, p, x, y, z, b);
-    const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W &&
-                    (uint64_t)z < (uint64_t)D && (uint64_t)b < (uint64_t)B;
-    const uint32_t k = ok ? (uint32_t)(((b * D + z) * H + x) * W + y) : sentinel;
+    uint32_t k;
+    const bool ok = src.cell(p, &k);
+    if (!ok) k = sentinel;
     bad += ok ? 0u : 1u;
     keys[p] = k;
     pkey[p] = k;
@@ -401,23 +504,6 @@ struct DenseRows {
 
 // Unsigned 32-bit division by a runtime constant with a multiply-high and
 // shifts (round-up magic number, d >= 1).
-struct FastDiv {
-  uint32_t d, magic, shift;
-  FastDiv() = default;
-  explicit FastDiv(uint32_t div) : d(div), magic(0), shift(0) {
-    if (div > 1) {
-      uint32_t s = 0;
-      while ((1ull << s) < div) ++s;
-      shift = s;
-      magic = (uint32_t)((((1ull << 32) * ((1ull << s) - div)) / div) + 1);
-    }
-  }
-  __device__ __forceinline__ uint32_t div(uint32_t n) const {
-    if (d == 1) return n;
-    const uint32_t t = __umulhi(n, magic);
-    return (((n - t) >> 1) + t) >> (shift - 1);
-  }
-};
 
 // The permutation handed to this source holds the PIXEL of each sorted point
 // and `depth` is in sorted order too (both written by dc_stream_kernel), so a
@@ -944,6 +1030,29 @@ int run_bwd_gather(int dtype, const void* gout, int64_t C, const Geometry& g, co
   }
 }
 
+// Everything after the keys kernel: sort (its first histogram came with the
+// keys), per-cell bounds, tiles, work list.
+int finish_plan(const Geometry& g, const PlanView& pv, const ScratchView& sv, const RadixPlan& rp, cudaStream_t st) {
+  const int64_t n = g.n;
+  uint32_t* keys_sorted = sv.keys0;
+  if (n > 0)
+    BFB_TRY(radix_sort_index(sv.keys0, sv.keys1, sv.vtmp, pv.perm, n, rp, sv.hist, sv.scan,
+                             /*hist0_ready=*/true, st, &keys_sorted));
+  BFB_CUDA(cudaMemsetAsync(pv.cell_se, 0, sizeof(int2) * (size_t)(g.cells + 1), st));
+  if (n > 0) {
+    bev_bounds_kernel<<<(unsigned)ceil_div(ceil_div(n, 4), 256), 256, 0, st>>>(keys_sorted, n, (uint32_t)g.cells,
+                                                                              pv.cell_se, pv.hdr);
+    BFB_CHECK_LAUNCH();
+  }
+  const unsigned wblocks = (unsigned)ceil_div(g.tiles * 32, 256);
+  bev_tile_plan_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np, sv.tile_mask);
+  BFB_CHECK_LAUNCH();
+  BFB_TRY(exclusive_scan_u32(sv.tile_np, sv.tile_np, g.tiles, sv.scan, &pv.hdr->total_pieces, st));
+  bev_emit_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np, sv.tile_mask, pv.pieces);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
 int check_channels(int64_t c) { return (c <= 0 || c > (1 << 20)) ? BFB_ERR_INVALID_ARG : BFB_OK; }
 
 }  // namespace
@@ -982,34 +1091,56 @@ extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64
   const RadixPlan rp = make_radix_plan((uint32_t)g.cells);
 
   BFB_CUDA(cudaMemsetAsync(pv.hdr, 0, sizeof(PlanHeader), st));
-  uint32_t* keys_sorted = sv.keys0;
   if (n > 0) {
     const int64_t ntiles = radix_tiles(n);
     const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
+    const uint32_t sentinel = (uint32_t)g.cells;
     if (itype == BFB_I32)
-      bev_keys_kernel<int32_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
-          static_cast<const int32_t*>(coords), n, B, D, H, W, sv.keys0, pv.pkey, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
+      bev_keys_kernel<<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
+          CoordCells<int32_t>{static_cast<const int32_t*>(coords), B, D, H, W}, n, sentinel, sv.keys0, pv.pkey,
+          rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
     else
-      bev_keys_kernel<int64_t><<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
-          static_cast<const int64_t*>(coords), n, B, D, H, W, sv.keys0, pv.pkey, rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
-    BFB_CHECK_LAUNCH();
-    BFB_TRY(radix_sort_index(sv.keys0, sv.keys1, sv.vtmp, pv.perm, n, rp, sv.hist, sv.scan,
-                             /*hist0_ready=*/true, st, &keys_sorted));
-  }
-  BFB_CUDA(cudaMemsetAsync(pv.cell_se, 0, sizeof(int2) * (size_t)(g.cells + 1), st));
-  if (n > 0) {
-    bev_bounds_kernel<<<(unsigned)ceil_div(ceil_div(n, 4), 256), 256, 0, st>>>(keys_sorted, n, (uint32_t)g.cells,
-                                                                  pv.cell_se, pv.hdr);
+      bev_keys_kernel<<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(
+          CoordCells<int64_t>{static_cast<const int64_t*>(coords), B, D, H, W}, n, sentinel, sv.keys0, pv.pkey,
+          rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
     BFB_CHECK_LAUNCH();
   }
-  const unsigned wblocks = (unsigned)ceil_div(g.tiles * 32, 256);
-  bev_tile_plan_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np, sv.tile_mask);
+  return finish_plan(g, pv, sv, rp, st);
+}
+
+extern "C" int bfb_bev_pool_geometry_plan(const float* frustum, int64_t nd, int64_t fh, int64_t fw,
+                                          const float* post_rots, const float* post_trans, const float* combine,
+                                          const float* trans, const float* extra_rots, const float* extra_trans,
+                                          int64_t B, int64_t ncam, const float* lower, const float* dx, int64_t D,
+                                          int64_t H, int64_t W, void* plan, size_t plan_bytes, void* scratch,
+                                          size_t scratch_bytes, void* stream) {
+  if (nd <= 0 || fh <= 0 || fw <= 0 || ncam <= 0 || B <= 0) return BFB_ERR_INVALID_ARG;
+  if (nd > 0x7fffffffLL / fh / fw || B > 0x7fffffffLL / ncam) return BFB_ERR_TOO_LARGE;
+  const int64_t fpts = nd * fh * fw;
+  if (B * ncam > 0x7fffffffLL / fpts) return BFB_ERR_TOO_LARGE;
+  const int64_t n = B * ncam * fpts;
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  if (!frustum || !post_rots || !post_trans || !combine || !trans || !lower || !dx) return BFB_ERR_INVALID_ARG;
+  if (!plan || !scratch) return BFB_ERR_WORKSPACE;
+  PlanView pv;
+  ScratchView sv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes || carve_scratch(nullptr, g, &sv) > scratch_bytes)
+    return BFB_ERR_WORKSPACE;
+  carve_plan(plan, g, &pv);
+  carve_scratch(scratch, g, &sv);
+  cudaStream_t st = as_stream(stream);
+  const RadixPlan rp = make_radix_plan((uint32_t)g.cells);
+  CameraCells cc{frustum, post_rots, post_trans, combine, trans, extra_rots, extra_trans,
+                 FastDiv((uint32_t)fpts), FastDiv((uint32_t)ncam), {lower[0], lower[1], lower[2]},
+                 {dx[0], dx[1], dx[2]}, D, H, W};
+  BFB_CUDA(cudaMemsetAsync(pv.hdr, 0, sizeof(PlanHeader), st));
+  const int64_t ntiles = radix_tiles(n);
+  const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
+  bev_keys_kernel<<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(cc, n, (uint32_t)g.cells, sv.keys0, pv.pkey,
+                                                                rp.digit_bits[0], sv.hist, ntiles, pv.hdr);
   BFB_CHECK_LAUNCH();
-  BFB_TRY(exclusive_scan_u32(sv.tile_np, sv.tile_np, g.tiles, sv.scan, &pv.hdr->total_pieces, st));
-  bev_emit_kernel<<<wblocks, 256, 0, st>>>(pv.cell_se, g.tiles, g.tpb, g.dhw, sv.tile_np,
-                                           sv.tile_mask, pv.pieces);
-  BFB_CHECK_LAUNCH();
-  return BFB_OK;
+  return finish_plan(g, pv, sv, rp, st);
 }
 
 extern "C" int bfb_bev_pool_forward_planned(const void* feats, int dtype, int64_t n, int64_t c,
@@ -1084,6 +1215,30 @@ extern "C" int bfb_bev_pool_backward_gather(const void* gout, int dtype, int64_t
   if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
   carve_plan(const_cast<void*>(plan), g, &pv);
   return run_bwd_gather(dtype, gout, c, g, pv, workspace, gfeat, as_stream(stream));
+}
+
+// cells[p] = cell rank of point p in the plan, -1 when it was dropped
+__global__ void plan_cells_kernel(const uint32_t* __restrict__ pkey, int64_t n, uint32_t sentinel,
+                                  int64_t* __restrict__ cells) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const uint32_t k = pkey[p];
+  cells[p] = k == sentinel ? -1 : (int64_t)k;
+}
+
+extern "C" int bfb_bev_pool_plan_cells(const void* plan, size_t plan_bytes, int64_t n, int64_t B, int64_t D,
+                                       int64_t H, int64_t W, int64_t* cells, void* stream) {
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  if (!plan) return BFB_ERR_WORKSPACE;
+  if (n > 0 && !cells) return BFB_ERR_INVALID_ARG;
+  PlanView pv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
+  carve_plan(const_cast<void*>(plan), g, &pv);
+  if (n == 0) return BFB_OK;
+  plan_cells_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, as_stream(stream)>>>(pv.pkey, n, (uint32_t)g.cells, cells);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
 }
 
 extern "C" int bfb_bev_pool_invalid_count(const void* plan, int64_t* count, void* stream) {
@@ -1186,19 +1341,6 @@ struct DcDims {
   __host__ __device__ int64_t n() const { return cams * nd * hw; }
 };
 
-// Cell of every frustum point in input order, or -1 outside the grid.
-template <class IT>
-__global__ void dc_keys_kernel(const IT* __restrict__ coords, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
-                               int32_t* __restrict__ keys) {
-  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= n) return;
-  int64_t x, y, z, b;
-  load_coord<IT>(coords, p, x, y, z, b);
-  const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W && (uint64_t)z < (uint64_t)D &&
-                  (uint64_t)b < (uint64_t)B;
-  keys[p] = ok ? (int32_t)(((b * D + z) * H + x) * W + y) : -1;
-}
-
 // Sorted-order stream of the fused forward: pixel and depth of every sorted point.
 __global__ void dc_stream_kernel(const uint32_t* __restrict__ perm, int64_t n, const float* __restrict__ depth,
                                  FastDiv dhw, FastDiv hw, uint32_t* __restrict__ pix, float* __restrict__ dep) {
@@ -1218,7 +1360,7 @@ __global__ void dc_stream_kernel(const uint32_t* __restrict__ perm, int64_t n, c
 // 16 dot products of a chunk of 16 depth bins are finished together by a
 // reduce-scatter across the lanes (16 shuffles), lane j ending with bin j.
 __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restrict__ g_t, const float* __restrict__ ctx_t,
-                                                         const int32_t* __restrict__ keys,
+                                                         const uint32_t* __restrict__ keys, uint32_t cells,
                                                          const float* __restrict__ depth, DcDims dm,
                                                          float* __restrict__ gdepth, float* __restrict__ gctx_t) {
   constexpr int U = 8;
@@ -1235,7 +1377,7 @@ __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restric
   for (int64_t base = 0; base < dm.nd; base += 32) {
     const int cnt = (int)min((int64_t)32, dm.nd - base);
     const int64_t mine = n0 + (base + lane) * dm.hw;
-    const int32_t myk = lane < cnt ? __ldg(keys + mine) : -1;
+    const uint32_t myk = lane < cnt ? __ldg(keys + mine) : cells;
     const float myd = lane < cnt ? __ldg(depth + mine) : 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -1245,8 +1387,8 @@ __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restric
         float v[U][4];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int32_t key = __shfl_sync(0xffffffffu, myk, 16 * h + k0 + u);
-          if (key >= 0 && active) {
+          const uint32_t key = __shfl_sync(0xffffffffu, myk, 16 * h + k0 + u);
+          if (key < cells && active) {
             VecIO<float, 4>::load(g_t + (int64_t)key * dm.c + lane * 4, v[u]);
           } else {
 #pragma unroll
@@ -1289,11 +1431,11 @@ __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restric
 }
 
 // Forward -> backward buffer: context transposed to [pixel, C], then the cell
-// of every frustum point.
+// of every frustum point (B*D*H*W outside the grid).
 size_t dc_aux_bytes(const DcDims& dm) {
   Carver cv(nullptr);
   cv.take<float>((size_t)(dm.cams * dm.hw * dm.c));
-  cv.take<int32_t>((size_t)dm.n());
+  cv.take<uint32_t>((size_t)dm.n());
   return cv.bytes();
 }
 
@@ -1325,37 +1467,30 @@ extern "C" int bfb_bev_pool_dc_workspace_sizes(int64_t cams, int64_t nd, int64_t
   return BFB_OK;
 }
 
-extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context, const void* coords, int itype,
-                                       int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
-                                       int64_t D, int64_t H, int64_t W, float* out, void* plan, size_t plan_bytes,
-                                       void* scratch, size_t scratch_bytes, void* aux, size_t aux_bytes,
-                                       void* stream) {
+extern "C" int bfb_bev_pool_dc_forward_planned(const float* depth, const float* context, int64_t cams, int64_t nd,
+                                               int64_t fh, int64_t fw, int64_t c, int64_t B, int64_t D, int64_t H,
+                                               int64_t W, const void* plan, size_t plan_bytes, float* out,
+                                               void* scratch, size_t scratch_bytes, void* aux, size_t aux_bytes,
+                                               void* stream) {
   const DcDims dm{cams, nd, fh * fw, c};
   Geometry g;
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
   BFB_TRY(dc_check(dm, g));
   if (!depth || !context || !out) return BFB_ERR_INVALID_ARG;
+  if (!plan || !scratch) return BFB_ERR_WORKSPACE;
   if (!aux || aux_bytes < dc_aux_bytes(dm)) return BFB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(aux) & 15) || (reinterpret_cast<uintptr_t>(out) & 3)) return BFB_ERR_INVALID_ARG;
-  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (nd * dm.hw > 0xffffffffLL || dm.n() > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
+  PlanView pv;
+  if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
+  carve_plan(const_cast<void*>(plan), g, &pv);
   cudaStream_t st = as_stream(stream);
   Carver av(aux);
   float* ctx_t = av.take<float>((size_t)(cams * dm.hw * c));
-  int32_t* keys = av.take<int32_t>((size_t)dm.n());
+  uint32_t* keys = av.take<uint32_t>((size_t)dm.n());
   BFB_TRY(launch_transpose(context, ctx_t, cams, c, dm.hw, st));  // [cam][C][hw] -> [cam][hw][C]
-  {
-    const unsigned nb = (unsigned)ceil_div(dm.n(), 256);
-    if (itype == BFB_I32)
-      dc_keys_kernel<int32_t><<<nb, 256, 0, st>>>(static_cast<const int32_t*>(coords), dm.n(), B, D, H, W, keys);
-    else
-      dc_keys_kernel<int64_t><<<nb, 256, 0, st>>>(static_cast<const int64_t*>(coords), dm.n(), B, D, H, W, keys);
-    BFB_CHECK_LAUNCH();
-  }
-  BFB_TRY(bfb_bev_pool_plan(coords, itype, dm.n(), B, D, H, W, plan, plan_bytes, scratch, scratch_bytes, stream));
-  PlanView pv;
-  carve_plan(plan, g, &pv);
-  if (nd * dm.hw > 0xffffffffLL || dm.n() > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
-  // the plan's scratch is free again: sorted pixel / depth streams
+  BFB_CUDA(cudaMemcpyAsync(keys, pv.pkey, sizeof(uint32_t) * (size_t)dm.n(), cudaMemcpyDeviceToDevice, st));
+  // sorted pixel / depth streams in the scratch
   Carver sc(scratch);
   uint32_t* spix = sc.take<uint32_t>((size_t)dm.n());
   float* sdep = sc.take<float>((size_t)dm.n());
@@ -1370,6 +1505,22 @@ extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context,
   return launch_fwd_v<float, 4, 8>(src, c, g, sv, out, st);
 }
 
+extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context, const void* coords, int itype,
+                                       int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
+                                       int64_t D, int64_t H, int64_t W, float* out, void* plan, size_t plan_bytes,
+                                       void* scratch, size_t scratch_bytes, void* aux, size_t aux_bytes,
+                                       void* stream) {
+  const DcDims dm{cams, nd, fh * fw, c};
+  Geometry g;
+  BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
+  BFB_TRY(dc_check(dm, g));
+  if (!depth || !context || !out) return BFB_ERR_INVALID_ARG;
+  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
+  BFB_TRY(bfb_bev_pool_plan(coords, itype, dm.n(), B, D, H, W, plan, plan_bytes, scratch, scratch_bytes, stream));
+  return bfb_bev_pool_dc_forward_planned(depth, context, cams, nd, fh, fw, c, B, D, H, W, plan, plan_bytes, out,
+                                         scratch, scratch_bytes, aux, aux_bytes, stream);
+}
+
 extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* depth, const void* coords, int itype,
                                         int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
                                         int64_t D, int64_t H, int64_t W, const void* aux, size_t aux_bytes,
@@ -1379,21 +1530,22 @@ extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* dept
   Geometry g;
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
   BFB_TRY(dc_check(dm, g));
-  if (!grad_out || !depth || !coords || !grad_depth || !grad_context) return BFB_ERR_INVALID_ARG;
-  if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
+  (void)coords;  // the cells come from aux
+  (void)itype;
+  if (!grad_out || !depth || !grad_depth || !grad_context) return BFB_ERR_INVALID_ARG;
   if (!aux || aux_bytes < dc_aux_bytes(dm)) return BFB_ERR_WORKSPACE;
   size_t need = 0;
   BFB_TRY(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, nullptr, nullptr, nullptr, &need));
   if (!ws || ws_bytes < need) return BFB_ERR_WORKSPACE;
   Carver av(const_cast<void*>(aux));
   const float* ctx_t = av.take<float>((size_t)(cams * dm.hw * c));
-  const int32_t* keys = av.take<int32_t>((size_t)dm.n());
+  const uint32_t* keys = av.take<uint32_t>((size_t)dm.n());
   Carver cv(ws);
   float* g_t = cv.take<float>((size_t)(g.cells * c));
   float* gctx_t = cv.take<float>((size_t)(cams * dm.hw * c));
   cudaStream_t st = as_stream(stream);
   BFB_TRY(launch_transpose(grad_out, g_t, B, c, g.dhw, st));  // [B][C][DHW] -> [B][DHW][C]
-  dc_backward_kernel<<<(unsigned)ceil_div(cams * dm.hw * 32, 256), 256, 0, st>>>(g_t, ctx_t, keys, depth, dm,
+  dc_backward_kernel<<<(unsigned)ceil_div(cams * dm.hw * 32, 256), 256, 0, st>>>(g_t, ctx_t, keys, (uint32_t)g.cells, depth, dm,
                                                                                  grad_depth, gctx_t);
   BFB_CHECK_LAUNCH();
   BFB_TRY(launch_transpose(gctx_t, grad_context, cams, dm.hw, c, st));    // [cam][hw][C] -> [cam][C][hw]

@@ -127,6 +127,16 @@ at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, 
   return gfeat;
 }
 
+at::Tensor bev_pool_plan_cells(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
+  require_cuda(plan, "plan");
+  c10::cuda::CUDAGuard guard(plan.device());
+  auto cells = at::empty({n}, plan.options().dtype(at::kLong));
+  check(bfb_bev_pool_plan_cells(plan.data_ptr(), (size_t)plan.numel(), n, B, D, H, W, cells.data_ptr<int64_t>(),
+                                stream_of(plan)),
+        "bev_pool plan cells");
+  return cells;
+}
+
 int64_t bev_pool_invalid_count(const at::Tensor& plan) {
   c10::cuda::CUDAGuard guard(plan.device());
   int64_t v = 0;
@@ -166,6 +176,82 @@ std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward(const at::Tensor& depth_i
                                 scr_b, aux.data_ptr(), aux_b, stream_of(depth)),
         "bev_pool_dc forward");
   return {out, aux};
+}
+
+std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward_planned(const at::Tensor& depth_in, const at::Tensor& ctx_in,
+                                                               const at::Tensor& plan, int64_t B, int64_t D, int64_t H,
+                                                               int64_t W) {
+  require_cuda(depth_in, "depth");
+  require_cuda(ctx_in, "context");
+  require_cuda(plan, "plan");
+  c10::cuda::CUDAGuard guard(depth_in.device());
+  TORCH_CHECK_TYPE(depth_in.scalar_type() == at::kFloat && ctx_in.scalar_type() == at::kFloat,
+                   "depth and context must be float32");
+  TORCH_CHECK_VALUE(depth_in.dim() == 4 && ctx_in.dim() == 4, "depth [cams, D, fH, fW] and context [cams, C, fH, fW]");
+  auto depth = depth_in.contiguous();
+  auto ctx = ctx_in.contiguous();
+  const int64_t cams = depth.size(0), nd = depth.size(1), fh = depth.size(2), fw = depth.size(3), c = ctx.size(1);
+  TORCH_CHECK_VALUE(ctx.size(0) == cams && ctx.size(2) == fh && ctx.size(3) == fw, "context does not match depth");
+  size_t plan_b = 0, scr_b = 0, aux_b = 0;
+  check(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, &plan_b, &scr_b, &aux_b, nullptr),
+        "bev_pool_dc workspace query");
+  auto opts = depth.options().dtype(at::kByte);
+  auto scratch = at::empty({(int64_t)scr_b}, opts);
+  auto aux = at::empty({(int64_t)aux_b}, opts);
+  auto out = at::empty({B, c, D, H, W}, depth.options());
+  check(bfb_bev_pool_dc_forward_planned(depth.data_ptr<float>(), ctx.data_ptr<float>(), cams, nd, fh, fw, c, B, D, H,
+                                        W, plan.data_ptr(), (size_t)plan.numel(), out.data_ptr<float>(),
+                                        scratch.data_ptr(), scr_b, aux.data_ptr(), aux_b, stream_of(depth)),
+        "bev_pool_dc forward");
+  return {out, aux};
+}
+
+at::Tensor bev_pool_geometry_plan(const at::Tensor& frustum_in, const at::Tensor& post_rots_in,
+                                  const at::Tensor& post_trans_in, const at::Tensor& combine_in,
+                                  const at::Tensor& trans_in, const std::optional<at::Tensor>& extra_rots_in,
+                                  const std::optional<at::Tensor>& extra_trans_in, at::ArrayRef<double> lower,
+                                  at::ArrayRef<double> dx, int64_t D, int64_t H, int64_t W) {
+  require_cuda(frustum_in, "frustum");
+  c10::cuda::CUDAGuard guard(frustum_in.device());
+  auto f32 = [](const at::Tensor& t) { return t.contiguous().to(at::kFloat); };
+  auto frustum = f32(frustum_in);
+  auto post_rots = f32(post_rots_in), post_trans = f32(post_trans_in);
+  auto combine = f32(combine_in), trans = f32(trans_in);
+  TORCH_CHECK_VALUE(frustum.dim() == 4 && frustum.size(3) == 3, "frustum must be [D, fH, fW, 3]");
+  TORCH_CHECK_VALUE(post_rots.dim() == 4 && post_rots.size(2) == 3 && post_rots.size(3) == 3,
+                    "post_rots must be [B, N, 3, 3]");
+  const int64_t B = post_rots.size(0), ncam = post_rots.size(1);
+  TORCH_CHECK_VALUE(combine.sizes() == post_rots.sizes(), "combine must be [B, N, 3, 3]");
+  TORCH_CHECK_VALUE(post_trans.dim() == 3 && post_trans.size(0) == B && post_trans.size(1) == ncam &&
+                        post_trans.size(2) == 3 && trans.sizes() == post_trans.sizes(),
+                    "post_trans and camera2lidar_trans must be [B, N, 3]");
+  TORCH_CHECK_VALUE(lower.size() == 3 && dx.size() == 3, "lower and dx need 3 values");
+  at::Tensor er, et;
+  if (extra_rots_in.has_value()) {
+    er = f32(*extra_rots_in);
+    TORCH_CHECK_VALUE(er.dim() == 3 && er.size(0) == B && er.size(1) == 3 && er.size(2) == 3,
+                      "extra_rots must be [B, 3, 3]");
+  }
+  if (extra_trans_in.has_value()) {
+    et = f32(*extra_trans_in);
+    TORCH_CHECK_VALUE(et.dim() == 2 && et.size(0) == B && et.size(1) == 3, "extra_trans must be [B, 3]");
+  }
+  const int64_t nd = frustum.size(0), fh = frustum.size(1), fw = frustum.size(2);
+  const int64_t n = B * ncam * nd * fh * fw;
+  size_t plan_b = 0, scratch_b = 0;
+  check(bfb_bev_pool_workspace_sizes(n, 1, B, D, H, W, &plan_b, &scratch_b), "bev_pool workspace query");
+  auto opts = frustum.options().dtype(at::kByte);
+  auto plan = at::empty({(int64_t)plan_b}, opts);
+  auto scratch = at::empty({(int64_t)scratch_b}, opts);
+  const float lo[3] = {(float)lower[0], (float)lower[1], (float)lower[2]};
+  const float d3[3] = {(float)dx[0], (float)dx[1], (float)dx[2]};
+  check(bfb_bev_pool_geometry_plan(frustum.data_ptr<float>(), nd, fh, fw, post_rots.data_ptr<float>(),
+                                   post_trans.data_ptr<float>(), combine.data_ptr<float>(), trans.data_ptr<float>(),
+                                   er.defined() ? er.data_ptr<float>() : nullptr,
+                                   et.defined() ? et.data_ptr<float>() : nullptr, B, ncam, lo, d3, D, H, W,
+                                   plan.data_ptr(), plan_b, scratch.data_ptr(), scratch_b, stream_of(frustum)),
+        "bev_pool geometry plan");
+  return plan;
 }
 
 std::tuple<at::Tensor, at::Tensor> bev_pool_dc_backward(const at::Tensor& grad_in, const at::Tensor& depth_in,
@@ -370,7 +456,12 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward_planned(Tensor feats, Tensor plan, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_backward(Tensor grad_out, Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_invalid_count(Tensor plan) -> int");
+  m.def("bev_pool_plan_cells(Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_dc_forward(Tensor depth, Tensor context, Tensor coords, int B, int D, int H, int W) -> (Tensor, Tensor)");
+  m.def("bev_pool_dc_forward_planned(Tensor depth, Tensor context, Tensor plan, int B, int D, int H, int W) -> (Tensor, Tensor)");
+  m.def(
+      "bev_pool_geometry_plan(Tensor frustum, Tensor post_rots, Tensor post_trans, Tensor combine, Tensor trans, "
+      "Tensor? extra_rots, Tensor? extra_trans, float[] lower, float[] dx, int D, int H, int W) -> Tensor");
   m.def(
       "bev_pool_dc_backward(Tensor grad_out, Tensor depth, Tensor coords, Tensor aux, int C, int B, int D, int H, "
       "int W) -> (Tensor, Tensor)");
@@ -394,7 +485,10 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("bev_pool_forward_planned", &bev_pool_forward_planned);
   m.impl("bev_pool_backward", &bev_pool_backward);
   m.impl("bev_pool_invalid_count", &bev_pool_invalid_count);
+  m.impl("bev_pool_plan_cells", &bev_pool_plan_cells);
   m.impl("bev_pool_dc_forward", &bev_pool_dc_forward);
+  m.impl("bev_pool_dc_forward_planned", &bev_pool_dc_forward_planned);
+  m.impl("bev_pool_geometry_plan", &bev_pool_geometry_plan);
   m.impl("bev_pool_dc_backward", &bev_pool_dc_backward);
   m.impl("dynamic_voxelize", &dynamic_voxelize);
   m.impl("hard_voxelize", &hard_voxelize);

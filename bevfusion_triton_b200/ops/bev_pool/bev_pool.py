@@ -106,6 +106,12 @@ def bev_pool_planned(feats: torch.Tensor, plan: torch.Tensor, B: int, D: int, H:
     return _BevPoolPlannedFunction.apply(feats, plan, int(B), int(D), int(H), int(W))
 
 
+def plan_cells(plan: torch.Tensor, n: int, B: int, D: int, H: int, W: int) -> torch.Tensor:
+    """[n] int64: the cell rank ((b*D + z)*H + x)*W + y a plan gave every
+    point (input order), -1 for points it dropped."""
+    return ops().bev_pool_plan_cells(plan, int(n), int(B), int(D), int(H), int(W))
+
+
 def invalid_count(plan: torch.Tensor) -> int:
     """Points a plan dropped as out of range (synchronises the stream)."""
     return int(ops().bev_pool_invalid_count(plan))
@@ -113,22 +119,26 @@ def invalid_count(plan: torch.Tensor) -> int:
 
 class _BevPoolDepthContextFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, depth, context, coords, B, D, H, W):
-        out, aux = ops().bev_pool_dc_forward(depth, context, coords, B, D, H, W)
-        ctx.save_for_backward(depth, coords, aux)
+    def forward(ctx, depth, context, coords, plan, B, D, H, W):
+        if plan is None:
+            out, aux = ops().bev_pool_dc_forward(depth, context, coords, B, D, H, W)
+        else:
+            out, aux = ops().bev_pool_dc_forward_planned(depth, context, plan, B, D, H, W)
+        ctx.save_for_backward(depth, aux)
         ctx.shape = (context.size(1), B, D, H, W)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        depth, coords, aux = ctx.saved_tensors
+        depth, aux = ctx.saved_tensors
         C, B, D, H, W = ctx.shape
-        gdepth, gctx = ops().bev_pool_dc_backward(grad_out, depth, coords, aux, C, B, D, H, W)
-        return gdepth, gctx, None, None, None, None, None
+        none = depth.new_empty(0, dtype=torch.int64)  # the cells come from aux
+        gdepth, gctx = ops().bev_pool_dc_backward(grad_out, depth, none, aux, C, B, D, H, W)
+        return gdepth, gctx, None, None, None, None, None, None
 
 
-def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: torch.Tensor,
-                           B: int, D: int, H: int, W: int) -> torch.Tensor:
+def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: torch.Tensor | None,
+                           B: int, D: int, H: int, W: int, plan: torch.Tensor | None = None) -> torch.Tensor:
     """The LSS camera branch's pooling without a feature tensor.
 
     Equals ``bev_pool(feats[kept], coords[kept], B, D, H, W)`` with
@@ -137,8 +147,10 @@ def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: t
     bit.  ``depth`` [B, N, D_bins, fH, fW] (softmaxed) or [cams, D_bins, fH,
     fW]; ``context`` [B, N, C, fH, fW] or [cams, C, fH, fW], fp32;
     ``coords`` one (x, y, z, b) row per frustum point in (b, n, d, h, w)
-    order, unfiltered (points outside the grid are dropped).  Differentiable
-    w.r.t. depth and context.  C must be a multiple of 4, at most 128.
+    order, unfiltered (points outside the grid are dropped).  With ``plan``
+    (from ``bev_pool_geometry_plan`` or ``bev_pool_plan`` over those frustum
+    points) ``coords`` is not needed and may be None.  Differentiable w.r.t.
+    depth and context.  C must be a multiple of 4, at most 128.
     """
     if depth.dim() == 5:
         depth = depth.flatten(0, 1)
@@ -146,13 +158,67 @@ def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: t
         context = context.flatten(0, 1)
     if depth.dim() != 4 or context.dim() != 4:
         raise ValueError('depth and context must be 4-D or 5-D tensors.')
-    if coords.dim() != 2 or coords.size(-1) != 4:
-        raise ValueError('coords must have shape [N, 4].')
-    if coords.dtype not in (torch.int32, torch.int64):
-        raise TypeError('coords must have dtype torch.int32 or torch.int64.')
+    if plan is None:
+        if coords is None or coords.dim() != 2 or coords.size(-1) != 4:
+            raise ValueError('coords must have shape [N, 4].')
+        if coords.dtype not in (torch.int32, torch.int64):
+            raise TypeError('coords must have dtype torch.int32 or torch.int64.')
     if depth.dtype != torch.float32 or context.dtype != torch.float32:
         raise TypeError('depth and context must have dtype torch.float32.')
     if min(B, D, H, W) <= 0:
         raise ValueError('B, D, H, W must be positive integers.')
-    _require_cuda(depth, context, coords)
-    return _BevPoolDepthContextFunction.apply(depth, context, coords, int(B), int(D), int(H), int(W))
+    _require_cuda(depth, context, *((coords,) if plan is None else (plan,)))
+    return _BevPoolDepthContextFunction.apply(depth, context, coords, plan, int(B), int(D), int(H), int(W))
+
+
+def bev_grid(xbound, ybound, zbound):
+    """Lower grid edge ``bx - dx / 2``, cell size ``dx`` (fp32 values, as the
+    reference forms them) and cell counts ``nx`` (x, y, z); gen_dx_bx
+    (models/vtransforms/base.py:19-23) and the offset of base.py:138."""
+    rows = [xbound, ybound, zbound]
+    dx = torch.tensor([r[2] for r in rows], dtype=torch.float32)
+    bx = torch.tensor([r[0] + r[2] / 2.0 for r in rows], dtype=torch.float32)
+    lower = bx - dx / 2.0
+    nx = [int((r[1] - r[0]) / r[2]) for r in rows]
+    return lower.tolist(), dx.tolist(), nx
+
+
+def bev_pool_geometry_plan(frustum: torch.Tensor, camera2lidar_rots: torch.Tensor, camera2lidar_trans: torch.Tensor,
+                           intrins: torch.Tensor, post_rots: torch.Tensor, post_trans: torch.Tensor,
+                           xbound, ybound, zbound, extra_rots: torch.Tensor | None = None,
+                           extra_trans: torch.Tensor | None = None):
+    """bev_pool plan straight from the camera parameters (no coords tensor).
+
+    Fuses ``BaseTransform.get_geometry`` (models/vtransforms/base.py:82-126)
+    with the quantise + in-grid filter of ``BaseTransform.bev_pool``
+    (base.py:131-158): ``frustum`` [D_bins, fH, fW, 3] (``create_frustum``),
+    ``camera2lidar_rots``, ``intrins``, ``post_rots`` [B, N, 3, 3],
+    ``camera2lidar_trans``, ``post_trans`` [B, N, 3], optional
+    ``extra_rots`` [B, 3, 3] / ``extra_trans`` [B, 3] (lidar augmentation).
+    ``camera2lidar_rots @ intrins^-1`` is formed with ``torch.linalg.solve`` as
+    the reference does; the per-point 3x3 products run in the keys kernel
+    with the association of torch's CUDA matmul for these shapes (equal on
+    all but a few values in a million), so a point within rounding of a cell
+    edge may still land in the neighbouring cell.
+
+    Returns ``(plan, (B, D, H, W))``: the plan covers every frustum point in
+    (b, n, d, h, w) order and drops the ones outside the grid, so
+    ``bev_pool_planned(x.flatten(0, 4), plan, B, D, H, W)`` pools the
+    UNFILTERED features ``x`` [B, N, D_bins, fH, fW, C] (no boolean-mask
+    gather) and ``bev_pool_depth_context(depth, context, None, B, D, H, W,
+    plan=plan)`` pools depth x context.
+    """
+    for name, t in (('camera2lidar_rots', camera2lidar_rots), ('intrins', intrins), ('post_rots', post_rots)):
+        if t.dim() != 4 or t.shape[-2:] != (3, 3):
+            raise ValueError(f'{name} must have shape [B, N, 3, 3].')
+    if frustum.dim() != 4 or frustum.size(-1) != 3:
+        raise ValueError('frustum must have shape [D, fH, fW, 3].')
+    _require_cuda(frustum, camera2lidar_rots, camera2lidar_trans, intrins, post_rots, post_trans)
+    combine = torch.linalg.solve(intrins.float().transpose(-1, -2),
+                                 camera2lidar_rots.float().transpose(-1, -2)).transpose(-1, -2)
+    lower, dx, nx = bev_grid(xbound, ybound, zbound)
+    B = camera2lidar_rots.size(0)
+    D, H, W = nx[2], nx[0], nx[1]
+    plan = ops().bev_pool_geometry_plan(frustum, post_rots, post_trans, combine, camera2lidar_trans,
+                                        extra_rots, extra_trans, lower, dx, D, H, W)
+    return plan, (B, D, H, W)

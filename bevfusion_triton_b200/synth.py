@@ -99,6 +99,102 @@ def frustum_geometry() -> torch.Tensor:
     return torch.stack(outs).contiguous()
 
 
+def camera_rig(batch: int, *, augment: bool = False, seed: int = 0, device='cpu') -> dict:
+    """Inputs of ``BaseTransform.get_geometry`` (models/vtransforms/base.py:82-126)
+    for ``batch`` samples of the six-camera ring: ``frustum`` [D, fH, fW, 3]
+    and per camera ``camera2lidar_rots`` / ``intrins`` / ``post_rots``
+    [B, 6, 3, 3], ``camera2lidar_trans`` / ``post_trans`` [B, 6, 3], all fp32.
+
+    ``augment`` draws, per sample and seeded, the training-time perturbations
+    the reference pipeline applies: image resize 0.9-1.1 and rotation
+    +-5.4 degrees with a crop shift (post_rots / post_trans), a few pixels of
+    intrinsics jitter, +-2 degrees of camera yaw, and a lidar augmentation
+    (``extra_rots`` yaw +-22.5 degrees with scale 0.95-1.05, ``extra_trans``
+    +-0.5 m), returned as two more entries.
+    """
+    g = torch.Generator().manual_seed(seed * 1_000_003 + 17)
+    ncam = len(CAM_YAWS_DEG)
+    rots64, trans = _cam_to_lidar()
+    k = torch.tensor([[FX, 0.0, CX], [0.0, FY, CY], [0.0, 0.0, 1.0]], dtype=torch.float64)
+    rots = rots64.unsqueeze(0).repeat(batch, 1, 1, 1)
+    intr = k.view(1, 1, 3, 3).repeat(batch, ncam, 1, 1)
+    prots = torch.eye(3, dtype=torch.float64).view(1, 1, 3, 3).repeat(batch, ncam, 1, 1)
+    ptrans = torch.zeros((batch, ncam, 3), dtype=torch.float64)
+    out = {}
+    if augment:
+        def u(lo, hi, *shape):
+            return lo + (hi - lo) * torch.rand(shape, generator=g, dtype=torch.float64)
+
+        yaw = torch.deg2rad(u(-2.0, 2.0, batch, ncam))
+        rz = torch.zeros((batch, ncam, 3, 3), dtype=torch.float64)
+        rz[..., 0, 0], rz[..., 0, 1], rz[..., 1, 0], rz[..., 1, 1] = yaw.cos(), -yaw.sin(), yaw.sin(), yaw.cos()
+        rz[..., 2, 2] = 1.0
+        rots = rz @ rots
+        intr = intr.clone()
+        intr[..., 0, 0] += u(-5.0, 5.0, batch, ncam)
+        intr[..., 1, 1] = intr[..., 0, 0]
+        intr[..., 0, 2] += u(-4.0, 4.0, batch, ncam)
+        intr[..., 1, 2] += u(-4.0, 4.0, batch, ncam)
+        sc = u(0.9, 1.1, batch, ncam)
+        th = torch.deg2rad(u(-5.4, 5.4, batch, ncam))
+        prots = prots.clone()
+        prots[..., 0, 0], prots[..., 0, 1] = sc * th.cos(), -sc * th.sin()
+        prots[..., 1, 0], prots[..., 1, 1] = sc * th.sin(), sc * th.cos()
+        ptrans[..., 0] = u(-30.0, 30.0, batch, ncam)
+        ptrans[..., 1] = u(-30.0, 30.0, batch, ncam)
+        ey = torch.deg2rad(u(-22.5, 22.5, batch))
+        es = u(0.95, 1.05, batch)
+        er = torch.zeros((batch, 3, 3), dtype=torch.float64)
+        er[:, 0, 0], er[:, 0, 1], er[:, 1, 0], er[:, 1, 1] = es * ey.cos(), -es * ey.sin(), es * ey.sin(), es * ey.cos()
+        er[:, 2, 2] = es
+        out['extra_rots'] = er.float().to(device)
+        out['extra_trans'] = u(-0.5, 0.5, batch, 3).float().to(device)
+    out.update(
+        frustum=_frustum().to(device),
+        camera2lidar_rots=rots.float().to(device),
+        camera2lidar_trans=trans.view(1, ncam, 3).repeat(batch, 1, 1).to(device),
+        intrins=intr.float().to(device),
+        post_rots=prots.float().to(device),
+        post_trans=ptrans.float().to(device),
+    )
+    return out
+
+
+def lss_geometry(frustum, camera2lidar_rots, camera2lidar_trans, intrins, post_rots, post_trans, extra_rots=None,
+                 extra_trans=None):
+    """``BaseTransform.get_geometry`` (models/vtransforms/base.py:82-126) as
+    the reference computes it, in torch: [B, N, D, fH, fW, 3] LiDAR-frame
+    points of every frustum point."""
+    B, N, _ = camera2lidar_trans.shape
+    points = frustum - post_trans.view(B, N, 1, 1, 1, 3)
+    points = post_rots.transpose(-1, -2).reshape(B, N, 1, 1, 1, 3, 3).matmul(points.unsqueeze(-1))
+    points = torch.cat((points[:, :, :, :, :, :2] * points[:, :, :, :, :, 2:3], points[:, :, :, :, :, 2:3]), 5)
+    combine = torch.linalg.solve(intrins.transpose(-1, -2), camera2lidar_rots.transpose(-1, -2)).transpose(-1, -2)
+    points = combine.reshape(B, N, 1, 1, 1, 3, 3).matmul(points).squeeze(-1)
+    points = points + camera2lidar_trans.view(B, N, 1, 1, 1, 3)
+    if extra_rots is not None:
+        points = extra_rots.view(B, 1, 1, 1, 1, 3, 3).expand(B, N, 1, 1, 1, 3, 3).matmul(
+            points.unsqueeze(-1)).squeeze(-1)
+    if extra_trans is not None:
+        points = points + extra_trans.view(B, 1, 1, 1, 1, 3)
+    return points
+
+
+def lss_coords(geom, xbound, ybound, zbound):
+    """Quantise + in-grid filter of ``BaseTransform.bev_pool``
+    (models/vtransforms/base.py:138-158): (x, y, z, b) int64 coords of every
+    frustum point, the kept mask and the grid (B, D, H, W)."""
+    B = geom.size(0)
+    dx, bx, nx = grid_params(xbound, ybound, zbound)
+    dx, bx = dx.to(geom.device), bx.to(geom.device)
+    g = ((geom - (bx - dx / 2.0)) / dx).long().reshape(-1, 3)
+    b = torch.arange(B, device=geom.device).repeat_interleave(geom[0].numel() // 3).view(-1, 1)
+    g = torch.cat((g, b), 1)
+    kept = ((g[:, 0] >= 0) & (g[:, 0] < nx[0]) & (g[:, 1] >= 0) & (g[:, 1] < nx[1]) & (g[:, 2] >= 0)
+            & (g[:, 2] < nx[2]))
+    return g, kept, (B, nx[2], nx[0], nx[1])
+
+
 def grid_params(xbound, ybound, zbound):
     """dx, lower edge and cell counts; gen_dx_bx (base.py:19-23)."""
     rows = [xbound, ybound, zbound]

@@ -130,9 +130,10 @@ int bfb_bev_pool_backward_gather(const void* grad_out_dev, int dtype, int64_t n,
  * EVERY frustum point in (cam, d, h, w) order (points outside the grid are
  * dropped, which is the caller's filter), c % 4 == 0 and c <= 128.  The
  * forward equals bfb_bev_pool_forward on the materialised product bit for bit.
- * `aux` (cams*fh*fw*c floats, from *_sizes) is written by the forward and read
- * by the backward; `bwd` is the backward's scratch.  grad_depth has the
- * layout of depth, grad_context that of context. */
+ * `aux` (cams*fh*fw*c floats + one cell per frustum point, from *_sizes) is
+ * written by the forward and read by the backward; `bwd` is the backward's
+ * scratch.  grad_depth has the layout of depth, grad_context that of
+ * context. */
 int bfb_bev_pool_dc_workspace_sizes(int64_t cams, int64_t nd, int64_t fh, int64_t fw, int64_t c,
                                     int64_t B, int64_t D, int64_t H, int64_t W, size_t* plan_bytes,
                                     size_t* scratch_bytes, size_t* aux_bytes, size_t* bwd_bytes);
@@ -144,12 +145,54 @@ int bfb_bev_pool_dc_forward(const float* depth_dev, const float* context_dev,
                             void* scratch_dev, size_t scratch_bytes, void* aux_dev,
                             size_t aux_bytes, void* stream);
 
+/* The fused forward on a plan made beforehand (bfb_bev_pool_plan over the
+ * frustum points' coords, or bfb_bev_pool_geometry_plan); bfb_bev_pool_dc_forward
+ * is bfb_bev_pool_plan followed by this call. */
+int bfb_bev_pool_dc_forward_planned(const float* depth_dev, const float* context_dev, int64_t cams,
+                                    int64_t nd, int64_t fh, int64_t fw, int64_t c, int64_t B,
+                                    int64_t D, int64_t H, int64_t W, const void* plan_dev,
+                                    size_t plan_bytes, float* out_dev, void* scratch_dev,
+                                    size_t scratch_bytes, void* aux_dev, size_t aux_bytes,
+                                    void* stream);
+
+/* coords_dev / coords_itype are not read (the forward left every point's cell
+ * in aux) and may be NULL / 0. */
 int bfb_bev_pool_dc_backward(const float* grad_out_dev, const float* depth_dev,
                              const void* coords_dev, int coords_itype, int64_t cams, int64_t nd,
                              int64_t fh, int64_t fw, int64_t c, int64_t B, int64_t D, int64_t H,
                              int64_t W, const void* aux_dev, size_t aux_bytes, void* bwd_dev,
                              size_t bwd_bytes, float* grad_depth_dev, float* grad_context_dev,
                              void* stream);
+
+/* bev_pool plan straight from the camera parameters: the frustum geometry of
+ * models/vtransforms/base.py:82-126 (get_geometry) and the quantise + in-grid
+ * filter of base.py:131-158 (BaseTransform.bev_pool) for every frustum point,
+ * without a coordinate tensor.  The plan covers all B*ncam*nd*fh*fw frustum
+ * points in (b, cam, d, h, w) order; points outside the grid are dropped, so
+ * bfb_bev_pool_forward_planned takes the UNFILTERED [B*ncam*nd*fh*fw, c]
+ * features (no boolean-mask gather) and bfb_bev_pool_dc_forward_planned takes
+ * depth / context directly.  frustum [nd, fh, fw, 3] (u, v, depth);
+ * post_rots, combine [B*ncam, 3, 3]; post_trans, trans [B*ncam, 3]; combine =
+ * camera2lidar_rots @ intrins^-1 as the reference forms it (linalg.solve);
+ * extra_rots [B, 3, 3] and extra_trans [B, 3] may be NULL.  lower[3] = bx -
+ * dx / 2 and dx[3] are HOST arrays (x, y, z); the grid is D = nz, H = nx,
+ * W = ny cells.  Each row of a 3x3 product is fma(a1, p1, a0*p0) + a2*p2,
+ * which matches torch's CUDA matmul of these shapes on all but a few values
+ * in a million; a point lying within rounding of a cell edge can therefore
+ * still quantise into the neighbouring cell.
+ * Workspace sizes: bfb_bev_pool_workspace_sizes(B*ncam*nd*fh*fw, c, B, D, H, W). */
+/* The cell rank ((b*D + z)*H + x)*W + y the plan gave every point, in input
+ * order, or -1 for a dropped point: cells [n] int64. */
+int bfb_bev_pool_plan_cells(const void* plan_dev, size_t plan_bytes, int64_t n, int64_t B, int64_t D,
+                            int64_t H, int64_t W, int64_t* cells_dev, void* stream);
+
+int bfb_bev_pool_geometry_plan(const float* frustum_dev, int64_t nd, int64_t fh, int64_t fw,
+                               const float* post_rots_dev, const float* post_trans_dev,
+                               const float* combine_dev, const float* trans_dev,
+                               const float* extra_rots_dev, const float* extra_trans_dev,
+                               int64_t B, int64_t ncam, const float* lower, const float* dx,
+                               int64_t D, int64_t H, int64_t W, void* plan_dev, size_t plan_bytes,
+                               void* scratch_dev, size_t scratch_bytes, void* stream);
 
 /* bev_pool forward that allocates nothing and takes no workspace.  It has no
  * counterpart in the reference.  It is for callers that cannot allocate GPU
