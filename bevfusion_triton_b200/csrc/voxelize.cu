@@ -38,20 +38,25 @@ constexpr uint32_t kNoFirst = 0xffffffffu;
 constexpr int kLinBits = 40;  // cell index bits inside a key; the rest hold the sample
 constexpr int kVoxThreads = 256;
 
+// One voxel per slot, one 32-byte sector per slot: a probe, the first-point
+// minimum, the count and the id of a voxel all touch the same sector.
+struct __align__(32) VoxSlot {
+  unsigned long long key;  // kEmptyKey when free
+  uint32_t first;          // smallest point index (kNoFirst when free)
+  uint32_t cnt;            // points
+  int32_t gvid;            // voxel id over the batch, -1 when dropped by max_voxels
+  uint32_t pad[3];
+};
+static_assert(sizeof(VoxSlot) == 32, "one sector per slot");
+
 struct TableView {
-  uint64_t* keys;
-  uint32_t* first;
-  uint32_t* cnt;
-  int32_t* gvid;
+  VoxSlot* slots;
   uint64_t cap;  // power of two
 };
 
 size_t carve_table(void* base, uint64_t cap, TableView* t) {
   Carver c(base);
-  t->keys = c.take<uint64_t>(cap);
-  t->first = c.take<uint32_t>(cap);
-  t->cnt = c.take<uint32_t>(cap);
-  t->gvid = c.take<int32_t>(cap);
+  t->slots = c.take<VoxSlot>(cap);
   t->cap = cap;
   return c.bytes();
 }
@@ -199,8 +204,8 @@ __global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __rest
     const uint64_t mask = tb.cap - 1;
     uint64_t h = mix64(key) & mask;
     for (uint64_t probe = 0; probe < tb.cap; ++probe) {
-      uint64_t k = tb.keys[h];
-      if (k == kEmptyKey) k = atomicCAS(reinterpret_cast<unsigned long long*>(tb.keys + h), kEmptyKey, key);
+      uint64_t k = tb.slots[h].key;
+      if (k == kEmptyKey) k = atomicCAS(&tb.slots[h].key, kEmptyKey, (unsigned long long)key);
       if (k == kEmptyKey || k == key) {
         slot = (int64_t)h;
         break;
@@ -208,8 +213,8 @@ __global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __rest
       h = (h + 1) & mask;
     }
     if (slot >= 0) {
-      atomicMin(tb.first + slot, (uint32_t)p);
-      atomicAdd(tb.cnt + slot, (uint32_t)__popc(peers));
+      atomicMin(&tb.slots[slot].first, (uint32_t)p);
+      atomicAdd(&tb.slots[slot].cnt, (uint32_t)__popc(peers));
     } else {
       atomicAdd(err, 1u);  // table full: cannot happen when cap >= n
     }
@@ -218,12 +223,12 @@ __global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __rest
   if (p < n) slot_of[p] = valid ? (int32_t)slot : -1;
 }
 
-__global__ void vox_flags_kernel(const int32_t* __restrict__ slot_of, int64_t n, const uint32_t* __restrict__ first,
+__global__ void vox_flags_kernel(const int32_t* __restrict__ slot_of, int64_t n, const VoxSlot* __restrict__ slots,
                                  uint32_t* __restrict__ flags) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= n) return;
   const int32_t s = slot_of[p];
-  flags[p] = (s >= 0 && first[s] == (uint32_t)p) ? 1u : 0u;
+  flags[p] = (s >= 0 && slots[s].first == (uint32_t)p) ? 1u : 0u;
 }
 
 template <class T>
@@ -236,16 +241,16 @@ __global__ void vox_assign_kernel(const T* __restrict__ pts, int64_t n, int64_t 
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= n) return;
   const int32_t slot = slot_of[p];
-  if (slot < 0 || tb.first[slot] != (uint32_t)p) return;
+  if (slot < 0 || tb.slots[slot].first != (uint32_t)p) return;
   const uint32_t g = excl[p];
   const int s = batch > 1 ? sample_of(offs, batch, p) : 0;
   const int64_t local = (int64_t)g - (int64_t)excl[offs[s]];
-  const uint32_t c = tb.cnt[slot];
+  const uint32_t c = tb.slots[slot].cnt;
   const bool kept = max_voxels < 0 || local < max_voxels;
   gslot[g] = slot;
   gcnt[g] = kept ? c : 0u;
   vinfo[g] = make_int2(s, (int)local);
-  tb.gvid[slot] = kept ? (int32_t)g : -1;
+  tb.slots[slot].gvid = kept ? (int32_t)g : -1;
   if (kept) {
     float xyz[3];
     load_xyz<T>(pts, p, f, xyz);
@@ -268,7 +273,7 @@ __global__ void vox_count_kernel(const int64_t* __restrict__ offs, int batch, co
 }
 
 __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __restrict__ slot_of, int64_t n,
-                                                               const int32_t* __restrict__ gvid,
+                                                               const VoxSlot* __restrict__ slots,
                                                                uint32_t* __restrict__ cursor,
                                                                uint32_t* __restrict__ members,
                                                                int32_t* __restrict__ mvox) {
@@ -277,7 +282,7 @@ __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __
   int32_t g = -1;
   if (p < n) {
     const int32_t s = slot_of[p];
-    if (s >= 0) g = gvid[s];
+    if (s >= 0) g = slots[s].gvid;
   }
   const unsigned peers = __match_any_sync(0xffffffffu, g);
   const int leader = __ffs(peers) - 1;
@@ -355,9 +360,9 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
   int2 vi = make_int2(0, 0);
   if (g < total) {
     const int32_t slot = gslot[g];
-    tb.keys[slot] = kEmptyKey;  // leave the table clean for the next call
-    tb.first[slot] = kNoFirst;
-    tb.cnt[slot] = 0u;
+    tb.slots[slot].key = kEmptyKey;  // leave the table clean for the next call
+    tb.slots[slot].first = kNoFirst;
+    tb.slots[slot].cnt = 0u;
     cnt = gcnt[g];
     end = cursor[g];
     vi = vinfo[g];
@@ -411,6 +416,20 @@ __global__ void vox_zero_tail_kernel(const int32_t* __restrict__ voxel_num, int6
   }
 }
 
+// every slot free: key empty, no first point, count 0
+__global__ void vox_table_init_kernel(TableView tb) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tb.cap; i += stride) {
+    VoxSlot s;
+    s.key = kEmptyKey;
+    s.first = kNoFirst;
+    s.cnt = 0u;
+    s.gvid = -1;
+    s.pad[0] = s.pad[1] = s.pad[2] = 0u;
+    tb.slots[i] = s;
+  }
+}
+
 template <class T>
 int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr, const int64_t* offs_host,
                        int64_t batch, int64_t max_points, int64_t max_voxels, void* voxels, int32_t* coors,
@@ -425,7 +444,7 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
   if (n > 0) {
     vox_insert_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, n, f, gr, sv.offs, (int)batch, tb, sv.slot_of, sv.err);
     BFB_CHECK_LAUNCH();
-    vox_flags_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.first, sv.excl);
+    vox_flags_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.slots, sv.excl);
     BFB_CHECK_LAUNCH();
   }
   // excl[n] = number of distinct voxels over the batch
@@ -442,7 +461,7 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
   if (n > 0) {
     // bucket offsets over voxel ids; entries past the voxel count are never read
     BFB_TRY(exclusive_scan_u32(sv.gcnt, sv.cursor, n + 1, sv.scan, nullptr, st));
-    vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.gvid, sv.cursor, sv.members, sv.mvox);
+    vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.slots, sv.cursor, sv.members, sv.mvox);
     BFB_CHECK_LAUNCH();
     vox_rank_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo, sv.members,
                                                    sv.mvox, P, MV, static_cast<T*>(voxels));
@@ -508,10 +527,8 @@ extern "C" int bfb_hard_voxelize_table_init(void* table, size_t table_bytes, voi
   if (!table || cap == 0) return BFB_ERR_WORKSPACE;
   TableView tv;
   carve_table(table, cap, &tv);
-  cudaStream_t st = as_stream(stream);
-  BFB_CUDA(cudaMemsetAsync(tv.keys, 0xff, sizeof(uint64_t) * cap, st));
-  BFB_CUDA(cudaMemsetAsync(tv.first, 0xff, sizeof(uint32_t) * cap, st));
-  BFB_CUDA(cudaMemsetAsync(tv.cnt, 0, sizeof(uint32_t) * cap, st));
+  vox_table_init_kernel<<<(unsigned)std::min<uint64_t>((cap + 255) / 256, 148 * 64), 256, 0, as_stream(stream)>>>(tv);
+  BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
 

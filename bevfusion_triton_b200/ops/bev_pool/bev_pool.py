@@ -214,8 +214,10 @@ def bev_pool_geometry_plan(frustum: torch.Tensor, camera2lidar_rots: torch.Tenso
     if frustum.dim() != 4 or frustum.size(-1) != 3:
         raise ValueError('frustum must have shape [D, fH, fW, 3].')
     _require_cuda(frustum, camera2lidar_rots, camera2lidar_trans, intrins, post_rots, post_trans)
-    combine = torch.linalg.solve(intrins.float().transpose(-1, -2),
-                                 camera2lidar_rots.float().transpose(-1, -2)).transpose(-1, -2)
+    # the reference's torch.linalg.solve without its host-synchronising error
+    # check (same factorisation and result)
+    combine = torch.linalg.solve_ex(intrins.float().transpose(-1, -2),
+                                    camera2lidar_rots.float().transpose(-1, -2))[0].transpose(-1, -2)
     lower, dx, nx = bev_grid(xbound, ybound, zbound)
     B = camera2lidar_rots.size(0)
     D, H, W = nx[2], nx[0], nx[1]
