@@ -196,9 +196,14 @@ __global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __rest
       key = (s << kLinBits) | lin;
     }
   }
-  // lanes holding the same voxel insert once; the lowest lane holds the first point
-  const unsigned peers = __match_any_sync(0xffffffffu, key);
-  const int leader = __ffs(peers) - 1;
+  // a run of neighbouring lanes on the same voxel (points in scan order)
+  // inserts once; its first lane holds the run's smallest point index.  The
+  // same voxel in two runs inserts twice, which the atomics make harmless.
+  const uint64_t prev = __shfl_up_sync(0xffffffffu, key, 1);
+  const unsigned heads = __ballot_sync(0xffffffffu, lane == 0 || prev != key);
+  const int leader = 31 - __clz(heads & (lanemask_lt() | (1u << lane)));
+  const unsigned later = lane < 31 ? heads >> (lane + 1) : 0u;
+  const uint32_t run = later ? (uint32_t)__ffs(later) : (uint32_t)(32 - lane);
   int64_t slot = -1;
   if (valid && lane == leader) {
     const uint64_t mask = tb.cap - 1;
@@ -214,7 +219,7 @@ __global__ __launch_bounds__(kVoxThreads) void vox_insert_kernel(const T* __rest
     }
     if (slot >= 0) {
       atomicMin(&tb.slots[slot].first, (uint32_t)p);
-      atomicAdd(&tb.slots[slot].cnt, (uint32_t)__popc(peers));
+      atomicAdd(&tb.slots[slot].cnt, run);
     } else {
       atomicAdd(err, 1u);  // table full: cannot happen when cap >= n
     }
@@ -284,13 +289,18 @@ __global__ __launch_bounds__(kVoxThreads) void vox_fill_kernel(const int32_t* __
     const int32_t s = slot_of[p];
     if (s >= 0) g = slots[s].gvid;
   }
-  const unsigned peers = __match_any_sync(0xffffffffu, g);
-  const int leader = __ffs(peers) - 1;
+  // one cursor advance per run of neighbouring lanes in the same voxel (the
+  // order inside a bucket does not matter: vox_rank orders by point index)
+  const int32_t prev = __shfl_up_sync(0xffffffffu, g, 1);
+  const unsigned heads = __ballot_sync(0xffffffffu, lane == 0 || prev != g);
+  const int leader = 31 - __clz(heads & (lanemask_lt() | (1u << lane)));
+  const unsigned later = lane < 31 ? heads >> (lane + 1) : 0u;
+  const uint32_t run = later ? (uint32_t)__ffs(later) : (uint32_t)(32 - lane);
   uint32_t base = 0;
-  if (g >= 0 && lane == leader) base = atomicAdd(cursor + g, (uint32_t)__popc(peers));
+  if (g >= 0 && lane == leader) base = atomicAdd(cursor + g, run);
   base = __shfl_sync(0xffffffffu, base, leader);
   if (g >= 0) {
-    const uint32_t pos = base + __popc(peers & lanemask_lt());
+    const uint32_t pos = base + (uint32_t)(lane - leader);
     members[pos] = (uint32_t)p;
     mvox[pos] = g;
   }
