@@ -117,24 +117,6 @@ size_t carve_scratch(void* base, const Geometry& g, ScratchView* v) {
   return c.bytes();
 }
 
-// Division by a fixed 32-bit divisor with a multiply-high and shifts.
-struct FastDiv {
-  uint32_t d, magic, shift;
-  FastDiv() = default;
-  explicit FastDiv(uint32_t div) : d(div), magic(0), shift(0) {
-    if (div > 1) {
-      uint32_t s = 0;
-      while ((1ull << s) < div) ++s;
-      shift = s;
-      magic = (uint32_t)((((1ull << 32) * ((1ull << s) - div)) / div) + 1);
-    }
-  }
-  __device__ __forceinline__ uint32_t div(uint32_t n) const {
-    if (d == 1) return n;
-    const uint32_t t = __umulhi(n, magic);
-    return (((n - t) >> 1) + t) >> (shift - 1);
-  }
-};
 
 // ---------------------------------------------------------------------------
 // 1. cell ranks

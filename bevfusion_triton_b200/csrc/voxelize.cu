@@ -335,20 +335,37 @@ __global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
 }
 
 // One thread per (voxel, point slot): slots past a voxel's points get 0.
+// 32-bit index arithmetic while the slots fit (always, at the configured
+// sizes), 64-bit division otherwise.
+template <class T>
+__device__ __forceinline__ void pad_slot(uint64_t g, uint64_t j, const uint32_t* __restrict__ gcnt,
+                                         const int2* __restrict__ vinfo, int64_t f, int64_t P, int64_t max_voxels,
+                                         T* __restrict__ voxels) {
+  const uint32_t cnt = __ldg(gcnt + g);
+  if (cnt == 0 || cnt > (uint32_t)kRankMax || j < cnt) return;
+  const int2 vi = __ldg(vinfo + g);
+  T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + (int64_t)j) * f;
+  for (int64_t q = 0; q < f; ++q) dst[q] = from_f32<T>(0.f);
+}
+
 template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_pad_kernel(const uint32_t* __restrict__ total_dev,
                                                               const uint32_t* __restrict__ gcnt,
-                                                              const int2* __restrict__ vinfo, int64_t f, int64_t P,
+                                                              const int2* __restrict__ vinfo, int64_t f, FastDiv P,
                                                               int64_t max_voxels, T* __restrict__ voxels) {
-  const int64_t total = (int64_t)*total_dev * P;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
-    const int64_t g = t / P, j = t - g * P;
-    const uint32_t cnt = gcnt[g];
-    if (cnt == 0 || cnt > (uint32_t)kRankMax || j < (int64_t)cnt) continue;
-    const int2 vi = vinfo[g];
-    T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + j) * f;
-    for (int64_t q = 0; q < f; ++q) dst[q] = from_f32<T>(0.f);
+  const uint64_t total = (uint64_t)*total_dev * P.d;
+  if (total < (1ull << 32)) {
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < (uint32_t)total; t += stride) {
+      const uint32_t g = P.div(t);
+      pad_slot<T>(g, t - g * P.d, gcnt, vinfo, f, P.d, max_voxels, voxels);
+    }
+  } else {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+      const uint64_t g = t / P.d;
+      pad_slot<T>(g, t - g * P.d, gcnt, vinfo, f, P.d, max_voxels, voxels);
+    }
   }
 }
 
@@ -476,7 +493,7 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
     vox_rank_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo, sv.members,
                                                    sv.mvox, P, MV, static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
-    vox_pad_kernel<T><<<148 * 16, kVoxThreads, 0, st>>>(sv.excl + n, sv.gcnt, sv.vinfo, f, P, MV,
+    vox_pad_kernel<T><<<148 * 16, kVoxThreads, 0, st>>>(sv.excl + n, sv.gcnt, sv.vinfo, f, FastDiv((uint32_t)P), MV,
                                                         static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
     vox_order_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, tb, sv.gcnt, sv.cursor, sv.gslot, sv.vinfo,
