@@ -143,7 +143,8 @@ template <class IT>
 struct CoordCells {
   const IT* coords;
   int64_t B, D, H, W;
-  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r) const {
+  struct Cache {};
+  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r, Cache&) const {
     int64_t x, y, z, b;
     load_coord<IT>(coords, p, x, y, z, b);
     const bool ok = (uint64_t)x < (uint64_t)H && (uint64_t)y < (uint64_t)W && (uint64_t)z < (uint64_t)D &&
@@ -174,51 +175,70 @@ struct CameraCells {
   float lower[3], dx[3];     // bx - dx / 2 and dx
   int64_t nz, nx, ny;        // grid cells along z, x, y
 
+  // The parameters of the camera a thread is on, reloaded only when its next
+  // point belongs to another camera (a keys tile spans one or two cameras).
+  struct Cache {
+    uint32_t bn = 0xffffffffu, b = 0;
+    float pt[3], pr[9], cm[9], tr[3], er[9], et[3];
+  };
+
   // one row of a 3x3 product: fma(a1, p1, a0 * p0) + a2 * p2
   static __device__ __forceinline__ float row3(float a0, float a1, float a2, const float (&v)[3]) {
     return __fadd_rn(__fmaf_rn(a1, v[1], __fmul_rn(a0, v[0])), __fmul_rn(a2, v[2]));
   }
 
-  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r) const {
+  __device__ __forceinline__ void load(uint32_t bn, Cache& c) const {
+    c.bn = bn;
+    c.b = ncam.div(bn);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      c.pt[i] = __ldg(post_trans + 3 * bn + i);
+      c.tr[i] = __ldg(trans + 3 * bn + i);
+      c.et[i] = extra_trans ? __ldg(extra_trans + 3 * c.b + i) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+      c.pr[i] = __ldg(post_rots + 9 * bn + i);
+      c.cm[i] = __ldg(combine + 9 * bn + i);
+      c.er[i] = extra_rots ? __ldg(extra_rots + 9 * c.b + i) : 0.f;
+    }
+  }
+
+  __device__ __forceinline__ bool cell(int64_t p, uint32_t* r, Cache& c) const {
     const uint32_t bn = frustum_pts.div((uint32_t)p);
     const uint32_t f = (uint32_t)p - bn * frustum_pts.d;
-    const uint32_t b = ncam.div(bn);
+    if (bn != c.bn) load(bn, c);
     float t[3], u[3], v[3], q[3];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) t[i] = __fsub_rn(__ldg(frustum + 3 * f + i), __ldg(post_trans + 3 * bn + i));
-    const float* pr = post_rots + 9 * bn;  // post_rots^T @ t
+    for (int i = 0; i < 3; ++i) t[i] = __fsub_rn(__ldg(frustum + 3 * f + i), c.pt[i]);
 #pragma unroll
-    for (int i = 0; i < 3; ++i) u[i] = row3(__ldg(pr + i), __ldg(pr + 3 + i), __ldg(pr + 6 + i), t);
+    for (int i = 0; i < 3; ++i) u[i] = row3(c.pr[i], c.pr[3 + i], c.pr[6 + i], t);  // post_rots^T @ t
     v[0] = __fmul_rn(u[0], u[2]);
     v[1] = __fmul_rn(u[1], u[2]);
     v[2] = u[2];
-    const float* cm = combine + 9 * bn;
 #pragma unroll
-    for (int i = 0; i < 3; ++i)
-      q[i] = __fadd_rn(row3(__ldg(cm + 3 * i), __ldg(cm + 3 * i + 1), __ldg(cm + 3 * i + 2), v),
-                       __ldg(trans + 3 * bn + i));
+    for (int i = 0; i < 3; ++i) q[i] = __fadd_rn(row3(c.cm[3 * i], c.cm[3 * i + 1], c.cm[3 * i + 2], v), c.tr[i]);
     if (extra_rots) {
-      const float* er = extra_rots + 9 * b;
       float e[3];
 #pragma unroll
-      for (int i = 0; i < 3; ++i) e[i] = row3(__ldg(er + 3 * i), __ldg(er + 3 * i + 1), __ldg(er + 3 * i + 2), q);
+      for (int i = 0; i < 3; ++i) e[i] = row3(c.er[3 * i], c.er[3 * i + 1], c.er[3 * i + 2], q);
 #pragma unroll
       for (int i = 0; i < 3; ++i) q[i] = e[i];
     }
     if (extra_trans) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i) q[i] = __fadd_rn(q[i], __ldg(extra_trans + 3 * b + i));
+      for (int i = 0; i < 3; ++i) q[i] = __fadd_rn(q[i], c.et[i]);
     }
     const int64_t lim[3] = {nx, ny, nz};
     int64_t gi[3];
     bool ok = true;
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      const float c = truncf(__fdiv_rn(__fsub_rn(q[i], lower[i]), dx[i]));
-      ok = ok && c >= 0.f && c < (float)lim[i];  // false for NaN
-      gi[i] = ok ? (int64_t)c : 0;
+      const float g = truncf(__fdiv_rn(__fsub_rn(q[i], lower[i]), dx[i]));
+      ok = ok && g >= 0.f && g < (float)lim[i];  // false for NaN
+      gi[i] = ok ? (int64_t)g : 0;
     }
-    *r = (uint32_t)((((int64_t)b * nz + gi[2]) * nx + gi[0]) * ny + gi[1]);
+    *r = (uint32_t)((((int64_t)c.b * nz + gi[2]) * nx + gi[0]) * ny + gi[1]);
     return ok;
   }
 };
@@ -237,9 +257,10 @@ __global__ __launch_bounds__(kRadixThreads) void bev_keys_kernel(
   const int64_t base = (int64_t)blockIdx.x * kRadixTile;
   const int64_t end = min(n, base + kRadixTile);
   uint32_t bad = 0;
+  typename Src::Cache cache;
   for (int64_t p = base + threadIdx.x; p < end; p += kRadixThreads) {
     uint32_t k;
-    const bool ok = src.cell(p, &k);
+    const bool ok = src.cell(p, &k, cache);
     if (!ok) k = sentinel;
     bad += ok ? 0u : 1u;
     keys[p] = k;
