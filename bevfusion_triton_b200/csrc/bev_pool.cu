@@ -1505,7 +1505,9 @@ extern "C" int bfb_bev_pool_dc_forward_planned(const float* depth, const float* 
   PlanView sv = pv;
   sv.perm = spix;
   DepthContextRows src{sdep, ctx_t, c, nullptr};
-  return launch_fwd_v<float, 4, 8>(src, c, g, sv, out, st);
+  // the context rows come from L2 (a few MB per sample), so 4 rows in flight
+  // per warp suffice; the smaller register file lets more warps in
+  return launch_fwd_v<float, 4, 4>(src, c, g, sv, out, st);
 }
 
 extern "C" int bfb_bev_pool_dc_forward(const float* depth, const float* context, const void* coords, int itype,
