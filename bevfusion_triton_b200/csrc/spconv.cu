@@ -1,0 +1,361 @@
+// Sparse-convolution rulebook (indice pairs) for sm_100a.
+//
+// Reference semantics: ops/spconv/src/spconv_triton.py
+//   :655-749  _get_indice_pairs_impl (the sequential algorithm; its
+//             cuda_ordering=True branch is what the Triton path returns)
+//   :792-915  get_indice_pairs_triton: candidates (input j, kernel offset k)
+//             in j-major order, output sites = the distinct candidate cells in
+//             ascending flat order (regular / transposed conv) or the inputs
+//             themselves (submanifold), rule k's pairs in ascending j
+//   :90-198   candidate cell of (j, k):
+//               regular:    out = (in + pad - k*dil) / stride, exact division
+//               transposed: out = in*stride - pad + k*dil
+//             kept when every coordinate lies in the output shape
+//   :298-318  output shape (host side)
+//
+// Pipeline (flat cell = b * volume + row-major spatial index, < 2^32):
+//   spc_candidates  thread per (j, k): the candidate's cell, valid flag in the
+//                   rule-major flag array flags[k * n + j]
+//   submanifold:  spc_insert_inputs (hash: cell -> largest j holding it, as
+//                 the sequential loop's last write wins), spc_lookup
+//                 (candidate -> output j, or dropped)
+//   regular:      spc_mark (one bit per grid cell), spc_popc + scan (output
+//                 ids are the ranks of the set bits, i.e. the distinct cells in
+//                 ascending order), spc_rank (candidate -> output id)
+//   scan of flags -> rule k's pairs at [base_k, base_k + count_k) in ascending j;
+//   spc_pack writes indice_pairs[k, 0/1, slot] and spc_counts indice_num.
+//   spc_outids (regular only, second call once the caller knows the count)
+//   decodes the set bits into [b, c0, .., c{ndim-1}] rows.
+#include "scan.cuh"
+
+namespace bfb {
+namespace {
+
+constexpr uint32_t kSpEmpty = 0xffffffffu;
+constexpr int kSpMaxDims = 4;
+constexpr int kSpThreads = 256;
+
+struct SpGeom {
+  int ndim;
+  int64_t ks[kSpMaxDims], st[kSpMaxDims], pad[kSpMaxDims], dil[kSpMaxDims], out[kSpMaxDims];
+  int64_t volume;  // product of out[]
+  int64_t K;       // product of ks[]
+  bool transpose;
+};
+
+struct SpSlot {
+  uint32_t key;  // kSpEmpty when free
+  int32_t val;
+};
+
+uint64_t sp_table_cap(int64_t inserts) {
+  uint64_t cap = 1024;
+  while (cap < (uint64_t)(2 * inserts)) cap *= 2;
+  return cap;
+}
+
+__device__ __forceinline__ uint32_t sp_hash(uint32_t k) {
+  k ^= k >> 16; k *= 0x7feb352du; k ^= k >> 15; k *= 0x846ca68bu; k ^= k >> 16;
+  return k;
+}
+
+// Slot of `key`, inserting it if absent; -1 only if the table is full
+// (cannot happen: the capacity is at least twice the insertions).
+__device__ __forceinline__ int64_t sp_insert(SpSlot* tb, uint64_t cap, uint32_t key) {
+  const uint64_t mask = cap - 1;
+  uint64_t h = sp_hash(key) & mask;
+  for (uint64_t probe = 0; probe < cap; ++probe) {
+    uint32_t k = tb[h].key;
+    if (k == kSpEmpty) k = atomicCAS(&tb[h].key, kSpEmpty, key);
+    if (k == kSpEmpty || k == key) return (int64_t)h;
+    h = (h + 1) & mask;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ int64_t sp_find(const SpSlot* tb, uint64_t cap, uint32_t key) {
+  const uint64_t mask = cap - 1;
+  uint64_t h = sp_hash(key) & mask;
+  for (uint64_t probe = 0; probe < cap; ++probe) {
+    const uint32_t k = tb[h].key;
+    if (k == key) return (int64_t)h;
+    if (k == kSpEmpty) return -1;
+    h = (h + 1) & mask;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ uint32_t flat_of(const int32_t* row, const SpGeom& g) {
+  uint64_t f = 0;
+  for (int d = 0; d < g.ndim; ++d) f = f * (uint64_t)g.out[d] + (uint64_t)row[1 + d];
+  return (uint32_t)((uint64_t)row[0] * (uint64_t)g.volume + f);
+}
+
+__global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n, SpGeom g,
+                                      uint32_t* __restrict__ cell, uint32_t* __restrict__ flags) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * g.K) return;
+  const int64_t j = t / g.K;
+  int64_t rem = t - j * g.K;
+  const int32_t* row = idx + j * (g.ndim + 1);
+  int64_t kd[kSpMaxDims];
+  for (int d = g.ndim - 1; d >= 0; --d) {  // last dimension fastest
+    kd[d] = rem % g.ks[d];
+    rem /= g.ks[d];
+  }
+  bool ok = true;
+  uint64_t f = 0;
+  for (int d = 0; d < g.ndim; ++d) {
+    const int64_t in = row[1 + d];
+    int64_t o;
+    if (g.transpose) {
+      o = in * g.st[d] - g.pad[d] + kd[d] * g.dil[d];
+    } else {
+      const int64_t num = in + g.pad[d] - kd[d] * g.dil[d];
+      ok = ok && num % g.st[d] == 0;
+      o = num / g.st[d];
+    }
+    ok = ok && o >= 0 && o < g.out[d];
+    f = f * (uint64_t)g.out[d] + (uint64_t)(ok ? o : 0);
+  }
+  const int64_t k = t - j * g.K;
+  cell[t] = (uint32_t)((uint64_t)row[0] * (uint64_t)g.volume + f);
+  flags[k * n + j] = ok ? 1u : 0u;
+}
+
+// submanifold: cell of every input -> the largest input index holding it
+__global__ void spc_insert_inputs_kernel(const int32_t* __restrict__ idx, int64_t n, SpGeom g, SpSlot* tb,
+                                         uint64_t cap) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const int64_t s = sp_insert(tb, cap, flat_of(idx + j * (g.ndim + 1), g));
+  if (s >= 0) atomicMax(&tb[s].val, (int32_t)j);
+}
+
+// regular / transposed: one bit per grid cell that some candidate reaches
+__global__ void spc_mark_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t n,
+                                int64_t K, uint32_t* __restrict__ bits) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * K) return;
+  const int64_t j = t / K, k = t - j * K;
+  if (!flags[k * n + j]) return;
+  const uint32_t c = cell[t];
+  const uint32_t m = 1u << (c & 31);
+  if (!(bits[c >> 5] & m)) atomicOr(bits + (c >> 5), m);  // skip the atomic once the bit is seen set
+}
+
+__global__ void spc_popc_kernel(const uint32_t* __restrict__ bits, int64_t words, uint32_t* __restrict__ cnt) {
+  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (w < words) cnt[w] = (uint32_t)__popc(bits[w]);
+}
+
+// regular: output id of a candidate = rank of its cell's bit
+__global__ void spc_rank_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t n,
+                                int64_t K, const uint32_t* __restrict__ bits, const uint32_t* __restrict__ prefix,
+                                int32_t* __restrict__ out_of) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * K) return;
+  const int64_t j = t / K, k = t - j * K;
+  if (!flags[k * n + j]) return;
+  const uint32_t c = cell[t], w = c >> 5;
+  out_of[t] = (int32_t)(__ldg(prefix + w) + (uint32_t)__popc(__ldg(bits + w) & ((1u << (c & 31)) - 1u)));
+}
+
+// submanifold: candidate -> the input at its cell, dropped when there is none
+__global__ void spc_lookup_kernel(const uint32_t* __restrict__ cell, uint32_t* __restrict__ flags, int64_t n,
+                                  int64_t K, const SpSlot* __restrict__ tb, uint64_t cap,
+                                  int32_t* __restrict__ out_of) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * K) return;
+  const int64_t j = t / K, k = t - j * K;
+  const int64_t f = k * n + j;
+  if (!flags[f]) return;
+  const int64_t s = sp_find(tb, cap, cell[t]);
+  if (s < 0) {
+    flags[f] = 0u;
+    return;
+  }
+  out_of[t] = tb[s].val;
+}
+
+// pos = exclusive scan of the rule-major flags (pos[n*K] = total): rule k's
+// pairs occupy [pos[k*n], pos[(k+1)*n]) in ascending j
+__global__ void spc_pack_kernel(const uint32_t* __restrict__ pos, int64_t n, int64_t K,
+                                const int32_t* __restrict__ out_of, int32_t* __restrict__ pairs) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= n * K) return;
+  if (pos[f + 1] == pos[f]) return;  // flag was 0
+  const int64_t k = f / n, j = f - k * n;
+  const int64_t slot = (int64_t)pos[f] - (int64_t)pos[k * n];
+  pairs[(k * 2 + 0) * n + slot] = (int32_t)j;
+  pairs[(k * 2 + 1) * n + slot] = out_of[j * K + k];
+}
+
+__global__ void spc_counts_kernel(const uint32_t* __restrict__ pos, int64_t n, int64_t K,
+                                  int32_t* __restrict__ num) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  num[k] = (int32_t)(pos[(k + 1) * n] - pos[k * n]);
+}
+
+// regular: set bits -> output rows, thread per bitmap word
+__global__ void spc_outids_kernel(const uint32_t* __restrict__ bits, const uint32_t* __restrict__ prefix,
+                                  int64_t words, SpGeom g, int32_t* __restrict__ outids) {
+  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (w >= words) return;
+  uint32_t m = bits[w];
+  uint32_t pos = prefix[w];
+  while (m) {
+    const int b = __ffs(m) - 1;
+    m &= m - 1;
+    uint64_t f = (uint64_t)w * 32 + (uint64_t)b;
+    int32_t* row = outids + (int64_t)pos * (g.ndim + 1);
+    row[0] = (int32_t)(f / (uint64_t)g.volume);
+    f %= (uint64_t)g.volume;
+    for (int d = g.ndim - 1; d >= 0; --d) {
+      row[1 + d] = (int32_t)(f % (uint64_t)g.out[d]);
+      f /= (uint64_t)g.out[d];
+    }
+    ++pos;
+  }
+}
+
+__global__ void spc_set_count_kernel(int32_t* __restrict__ total, int32_t v) { *total = v; }
+
+__global__ void spc_total_kernel(const uint32_t* __restrict__ prefix, int64_t words, int32_t* __restrict__ total) {
+  *total = (int32_t)prefix[words];
+}
+
+struct SpWork {
+  uint32_t* cell;    // [n*K] candidate cell
+  uint32_t* flags;   // [n*K + 1] rule-major flags, then their exclusive scan
+  int32_t* out_of;   // [n*K] output index per candidate
+  SpSlot* table;     // [cap] submanifold: cell -> input
+  uint32_t* bits;    // [words] regular: reached cells
+  uint32_t* prefix;  // [words + 1] regular: set bits before each word
+  uint32_t* scan;
+  uint64_t cap;
+  int64_t words;
+};
+
+size_t carve_work(void* base, int64_t n, int64_t K, int64_t cells, bool subm, SpWork* w) {
+  const int64_t c = n * K;
+  Carver cv(base);
+  w->cell = cv.take<uint32_t>((size_t)c);
+  w->flags = cv.take<uint32_t>((size_t)c + 1);
+  w->out_of = cv.take<int32_t>((size_t)c);
+  w->cap = subm ? sp_table_cap(n) : 0;
+  w->table = cv.take<SpSlot>((size_t)w->cap);
+  w->words = subm ? 0 : ceil_div(cells, 32);
+  w->bits = cv.take<uint32_t>((size_t)w->words);
+  w->prefix = cv.take<uint32_t>((size_t)w->words + 1);
+  const size_t sa = scan_scratch_elems(c + 1), sb = scan_scratch_elems(w->words + 1);
+  w->scan = cv.take<uint32_t>(sa > sb ? sa : sb);
+  return cv.bytes();
+}
+
+int make_sp_geom(int ndim, int64_t batch, const int64_t* out_shape, const int64_t* ksize, const int64_t* stride,
+                 const int64_t* padding, const int64_t* dilation, int transpose, SpGeom* g) {
+  if (ndim < 1 || ndim > kSpMaxDims || batch < 1) return BFB_ERR_INVALID_ARG;
+  if (!out_shape || !ksize || !stride || !padding || !dilation) return BFB_ERR_INVALID_ARG;
+  g->ndim = ndim;
+  g->transpose = transpose != 0;
+  g->volume = 1;
+  g->K = 1;
+  for (int d = 0; d < ndim; ++d) {
+    if (out_shape[d] <= 0 || ksize[d] <= 0 || stride[d] <= 0 || dilation[d] <= 0) return BFB_ERR_INVALID_ARG;
+    g->ks[d] = ksize[d]; g->st[d] = stride[d]; g->pad[d] = padding[d]; g->dil[d] = dilation[d];
+    g->out[d] = out_shape[d];
+    if (g->volume > (int64_t(1) << 40) / out_shape[d] || g->K > 4096 / ksize[d]) return BFB_ERR_TOO_LARGE;
+    g->volume *= out_shape[d];
+    g->K *= ksize[d];
+  }
+  if ((uint64_t)batch * (uint64_t)g->volume >= 0xffffffffull) return BFB_ERR_TOO_LARGE;  // cells fit 32 bits
+  return BFB_OK;
+}
+
+}  // namespace
+}  // namespace bfb
+
+using namespace bfb;
+
+extern "C" int bfb_indice_pairs_workspace_size(int64_t n, int ndim, int64_t batch, const int64_t* out_shape,
+                                               const int64_t* ksize, int subm, size_t* bytes) {
+  if (n < 0 || !bytes || !ksize || !out_shape) return BFB_ERR_INVALID_ARG;
+  const int64_t ones[kSpMaxDims] = {1, 1, 1, 1};
+  SpGeom g;
+  BFB_TRY(make_sp_geom(ndim, batch, out_shape, ksize, ones, ones, ones, 0, &g));
+  if (n * g.K >= 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
+  SpWork w;
+  *bytes = carve_work(nullptr, n, g.K, batch * g.volume, subm != 0, &w);
+  return BFB_OK;
+}
+
+extern "C" int bfb_get_indice_pairs(const int32_t* indices, int64_t n, int ndim, int64_t batch,
+                                    const int64_t* out_shape, const int64_t* ksize, const int64_t* stride,
+                                    const int64_t* padding, const int64_t* dilation, int subm, int transpose,
+                                    int32_t* indice_pairs, int32_t* indice_num, int32_t* num_out_dev,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  SpGeom g;
+  BFB_TRY(make_sp_geom(ndim, batch, out_shape, ksize, stride, padding, dilation, transpose, &g));
+  if (n < 0 || (n > 0 && (!indices || !indice_pairs)) || !indice_num || !num_out_dev) return BFB_ERR_INVALID_ARG;
+  if (n * g.K >= 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
+  SpWork w;
+  if (!workspace || carve_work(nullptr, n, g.K, batch * g.volume, subm != 0, &w) > workspace_bytes)
+    return BFB_ERR_WORKSPACE;
+  carve_work(workspace, n, g.K, batch * g.volume, subm != 0, &w);
+  cudaStream_t st = as_stream(stream);
+  const int64_t c = n * g.K;
+  if (c > 0) BFB_CUDA(cudaMemsetAsync(indice_pairs, 0xff, sizeof(int32_t) * (size_t)(2 * c), st));  // -1
+  BFB_CUDA(cudaMemsetAsync(indice_num, 0, sizeof(int32_t) * (size_t)g.K, st));
+  BFB_CUDA(cudaMemsetAsync(num_out_dev, 0, sizeof(int32_t), st));
+  if (n == 0) return BFB_OK;
+  const unsigned nbc = (unsigned)ceil_div(c, kSpThreads);
+  spc_candidates_kernel<<<nbc, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags);
+  BFB_CHECK_LAUNCH();
+  if (subm) {
+    BFB_CUDA(cudaMemsetAsync(w.table, 0xff, sizeof(SpSlot) * (size_t)w.cap, st));  // key free, val -1
+    spc_insert_inputs_kernel<<<(unsigned)ceil_div(n, kSpThreads), kSpThreads, 0, st>>>(indices, n, g, w.table,
+                                                                                      w.cap);
+    BFB_CHECK_LAUNCH();
+    spc_lookup_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.table, w.cap, w.out_of);
+    BFB_CHECK_LAUNCH();
+    spc_set_count_kernel<<<1, 1, 0, st>>>(num_out_dev, (int32_t)n);
+    BFB_CHECK_LAUNCH();
+  } else {
+    BFB_CUDA(cudaMemsetAsync(w.bits, 0, sizeof(uint32_t) * (size_t)w.words, st));
+    spc_mark_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.bits);
+    BFB_CHECK_LAUNCH();
+    spc_popc_kernel<<<(unsigned)ceil_div(w.words, kSpThreads), kSpThreads, 0, st>>>(w.bits, w.words, w.prefix);
+    BFB_CHECK_LAUNCH();
+    BFB_TRY(exclusive_scan_u32(w.prefix, w.prefix, w.words, w.scan, w.prefix + w.words, st));
+    spc_rank_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.bits, w.prefix, w.out_of);
+    BFB_CHECK_LAUNCH();
+    spc_total_kernel<<<1, 1, 0, st>>>(w.prefix, w.words, num_out_dev);
+    BFB_CHECK_LAUNCH();
+  }
+  BFB_TRY(exclusive_scan_u32(w.flags, w.flags, c, w.scan, w.flags + c, st));
+  spc_pack_kernel<<<nbc, kSpThreads, 0, st>>>(w.flags, n, g.K, w.out_of, indice_pairs);
+  BFB_CHECK_LAUNCH();
+  spc_counts_kernel<<<(unsigned)ceil_div(g.K, kSpThreads), kSpThreads, 0, st>>>(w.flags, n, g.K, indice_num);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}
+
+extern "C" int bfb_indice_pairs_outids(int64_t n, int ndim, int64_t batch, const int64_t* out_shape,
+                                       const int64_t* ksize, const void* workspace, size_t workspace_bytes,
+                                       int32_t* outids, void* stream) {
+  const int64_t ones[kSpMaxDims] = {1, 1, 1, 1};
+  SpGeom g;
+  BFB_TRY(make_sp_geom(ndim, batch, out_shape, ksize, ones, ones, ones, 0, &g));
+  SpWork w;
+  if (!workspace || carve_work(nullptr, n, g.K, batch * g.volume, false, &w) > workspace_bytes)
+    return BFB_ERR_WORKSPACE;
+  if (n == 0) return BFB_OK;
+  if (!outids) return BFB_ERR_INVALID_ARG;
+  carve_work(const_cast<void*>(workspace), n, g.K, batch * g.volume, false, &w);
+  spc_outids_kernel<<<(unsigned)ceil_div(w.words, kSpThreads), kSpThreads, 0, as_stream(stream)>>>(
+      w.bits, w.prefix, w.words, g, outids);
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}

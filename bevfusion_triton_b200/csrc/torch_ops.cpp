@@ -450,6 +450,45 @@ void dynamic_scatter_backward(at::Tensor& grad_feats, const at::Tensor& grad_out
 
 }  // namespace
 
+// ------------------------------------------------- sparse-convolution rulebook
+std::tuple<at::Tensor, at::Tensor, at::Tensor> get_indice_pairs(const at::Tensor& indices_in, int64_t batch,
+                                                                at::IntArrayRef out_shape, at::IntArrayRef ksize,
+                                                                at::IntArrayRef stride, at::IntArrayRef padding,
+                                                                at::IntArrayRef dilation, bool subm, bool transpose) {
+  require_cuda(indices_in, "indices");
+  c10::cuda::CUDAGuard guard(indices_in.device());
+  auto indices = indices_in.contiguous().to(at::kInt);
+  TORCH_CHECK_VALUE(indices.dim() == 2 && indices.size(1) >= 2, "indices must be [N, ndim + 1]");
+  const int64_t n = indices.size(0);
+  const int ndim = (int)indices.size(1) - 1;
+  TORCH_CHECK_VALUE((int64_t)out_shape.size() == ndim && (int64_t)ksize.size() == ndim &&
+                        (int64_t)stride.size() == ndim && (int64_t)padding.size() == ndim &&
+                        (int64_t)dilation.size() == ndim,
+                    "every convolution parameter needs ndim values");
+  int64_t K = 1;
+  for (auto k : ksize) K *= k;
+  size_t ws_b = 0;
+  check(bfb_indice_pairs_workspace_size(n, ndim, batch, out_shape.data(), ksize.data(), subm ? 1 : 0, &ws_b),
+        "indice pairs workspace query");
+  auto opts = indices.options();
+  auto ws = at::empty({(int64_t)ws_b}, opts.dtype(at::kByte));
+  auto pairs = at::empty({K, 2, n}, opts);
+  auto num = at::empty({K}, opts);
+  auto nout = at::empty({1}, opts);
+  check(bfb_get_indice_pairs(indices.data_ptr<int32_t>(), n, ndim, batch, out_shape.data(), ksize.data(),
+                             stride.data(), padding.data(), dilation.data(), subm ? 1 : 0, transpose ? 1 : 0,
+                             pairs.data_ptr<int32_t>(), num.data_ptr<int32_t>(), nout.data_ptr<int32_t>(),
+                             ws.data_ptr(), ws_b, stream_of(indices)),
+        "get_indice_pairs");
+  if (subm) return {indices, pairs, num};
+  const int64_t u = nout.item<int32_t>();  // one host sync, as the reference's
+  auto outids = at::empty({u, ndim + 1}, opts);
+  check(bfb_indice_pairs_outids(n, ndim, batch, out_shape.data(), ksize.data(), ws.data_ptr(), ws_b,
+                                outids.data_ptr<int32_t>(), stream_of(indices)),
+        "get_indice_pairs outids");
+  return {outids, pairs, num};
+}
+
 TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward(Tensor feats, Tensor coords, int B, int D, int H, int W) -> (Tensor, Tensor)");
   m.def("bev_pool_plan(Tensor coords, int B, int D, int H, int W) -> Tensor");
@@ -473,6 +512,9 @@ TORCH_LIBRARY(bfb_b200, m) {
       "hard_voxelize_batch(Tensor points, int[] offsets, Tensor(a!) voxels, Tensor(b!) coors, "
       "Tensor(c!) num_points, Tensor(d!) voxel_num, float[] voxel_size, float[] coors_range, int max_points, "
       "int max_voxels, bool zero_tail) -> ()");
+  m.def(
+      "get_indice_pairs(Tensor indices, int batch, int[] out_shape, int[] ksize, int[] stride, int[] padding, "
+      "int[] dilation, bool subm, bool transpose) -> (Tensor, Tensor, Tensor)");
   m.def("dynamic_scatter_forward(Tensor feats, Tensor coors, str reduce) -> (Tensor, Tensor, Tensor, Tensor)");
   m.def(
       "dynamic_scatter_backward(Tensor(a!) grad_feats, Tensor grad_out, Tensor feats, Tensor reduced, Tensor map, "
@@ -494,5 +536,6 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("hard_voxelize", &hard_voxelize);
   m.impl("hard_voxelize_batch", &hard_voxelize_batch);
   m.impl("dynamic_scatter_forward", &dynamic_scatter_forward);
+  m.impl("get_indice_pairs", &get_indice_pairs);
   m.impl("dynamic_scatter_backward", &dynamic_scatter_backward);
 }

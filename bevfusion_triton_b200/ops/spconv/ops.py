@@ -1,0 +1,82 @@
+"""Sparse-convolution rulebook (``get_indice_pairs``) on the sm_100a kernels.
+
+Reference: ops/spconv/ops.py:25-93 (output-size helpers, ``get_indice_pairs``)
+and ops/spconv/src/spconv_triton.py:608-652 (argument checks), :792-915 (the
+Triton path).  Same signature, exception types and results as the reference's
+GPU path: submanifold returns the input rows as outputs; a regular or
+transposed rulebook numbers its output sites in ascending (b, c0, ..) order;
+within a rule the pairs are in ascending input row, unused slots -1.
+
+Differences: CUDA tensors only (no CPU path); ``batch * prod(out_shape)``
+must stay below 2**32; the optional ``grid`` scratch tensor is not needed and
+is only reset to -1, as the reference leaves it.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..._lib import ops
+
+
+def get_conv_output_size(input_size, kernel_size, stride, padding, dilation):
+    """ops/spconv/ops.py:25-37."""
+    out = []
+    for i in range(len(input_size)):
+        size = (input_size[i] + 2 * padding[i] - dilation[i] * (kernel_size[i] - 1) - 1) // stride[i] + 1
+        out.append(1 if kernel_size[i] == -1 else size)
+    return out
+
+
+def get_deconv_output_size(input_size, kernel_size, stride, padding, dilation, output_padding):
+    """ops/spconv/ops.py:40-50."""
+    out = []
+    for i in range(len(input_size)):
+        if kernel_size[i] == -1:
+            raise ValueError("deconv don't support kernel_size < 0")
+        out.append((input_size[i] - 1) * stride[i] - 2 * padding[i] + kernel_size[i] + output_padding[i])
+    return out
+
+
+def _nd(value, ndim: int) -> list[int]:
+    if isinstance(value, (list, tuple)):
+        if len(value) != ndim:
+            raise ValueError(f'Expected parameter of length {ndim}, got {len(value)}')
+        return [int(v) for v in value]
+    return [int(value)] * ndim
+
+
+def get_indice_pairs(indices: torch.Tensor, batch_size: int, spatial_shape, ksize=3, stride=1, padding=0,
+                     dilation=1, out_padding=0, subm: bool = False, transpose: bool = False,
+                     grid: torch.Tensor | None = None):
+    """(outids [M, ndim + 1], indice_pairs [K, 2, N], indice_num [K]) of a
+    sparse convolution over ``indices`` [N, ndim + 1] (b, c0, ..)."""
+    if batch_size <= 0:
+        raise ValueError('batch_size must be positive')
+    if not indices.is_cuda:
+        raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
+    if indices.numel() > 0:
+        b = indices[:, 0]
+        if int(b.min().item()) < 0:
+            raise ValueError('indices batch column must be non-negative')
+        if int(b.max().item()) >= batch_size:
+            raise ValueError('indices batch column exceeds batch_size')
+    ndim = indices.shape[1] - 1
+    ksize, stride, padding = _nd(ksize, ndim), _nd(stride, ndim), _nd(padding, ndim)
+    dilation, out_padding = _nd(dilation, ndim), _nd(out_padding, ndim)
+    spatial_shape = [int(v) for v in spatial_shape]
+    for d, s in zip(dilation, stride):
+        assert any([s == 1, d == 1]), "don't support this."
+    if subm:
+        out_shape = spatial_shape
+    elif transpose:
+        out_shape = get_deconv_output_size(spatial_shape, ksize, stride, padding, dilation, out_padding)
+    else:
+        out_shape = get_conv_output_size(spatial_shape, ksize, stride, padding, dilation)
+    outids, pairs, num = ops().get_indice_pairs(indices, int(batch_size), out_shape, ksize, stride, padding,
+                                                dilation, bool(subm), bool(transpose))
+    if grid is not None:
+        grid.fill_(-1)
+    if subm:
+        outids = indices
+    dt = indices.dtype
+    return outids.to(dt), pairs.to(dt), num.to(dt)

@@ -320,6 +320,37 @@ int bfb_dynamic_scatter_backward(void* grad_feats_dev, const void* grad_out_dev,
                                  int dtype, int64_t n, int64_t m, int64_t c, int reduce,
                                  int32_t* argmax_ws_dev, size_t argmax_ws_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Sparse-convolution rulebook.  Replaces get_indice_pairs
+ * (ops/spconv/ops.py:53-93 -> ops/spconv/src/spconv_triton.py:792-915).
+ *
+ * indices [n, ndim + 1] int32 rows (b, c0, .., c{ndim-1}), 1 <= ndim <= 4;
+ * out_shape, ksize, stride, padding, dilation: ndim values each (host
+ * arrays; out_shape is the caller's output spatial shape, the input shape for
+ * submanifold).  K = prod(ksize).  Outputs: indice_pairs [K, 2, n] int32
+ * (rule k's pairs in [k, 0/1, 0 .. indice_num[k]) as (input row, output
+ * row), the rest -1), indice_num [K] int32, *num_out_dev (device int32) = the
+ * number of output rows.  Submanifold: the output rows are the input rows; a
+ * regular or transposed rulebook numbers its output sites in ascending
+ * (b, c0, .., c{ndim-1}) order (the Triton path's order) and
+ * bfb_indice_pairs_outids writes them, [num_out, ndim + 1], from the same
+ * workspace once the caller has read the count.  Within a rule, pairs are in
+ * ascending input row.  batch * prod(out_shape) must be below 2^32.  The
+ * workspace holds one bit per output grid cell for a regular rulebook.
+ * ---------------------------------------------------------------------- */
+int bfb_indice_pairs_workspace_size(int64_t n, int ndim, int64_t batch, const int64_t* out_shape,
+                                    const int64_t* ksize, int subm, size_t* bytes);
+
+int bfb_get_indice_pairs(const int32_t* indices_dev, int64_t n, int ndim, int64_t batch,
+                         const int64_t* out_shape, const int64_t* ksize, const int64_t* stride,
+                         const int64_t* padding, const int64_t* dilation, int subm, int transpose,
+                         int32_t* indice_pairs_dev, int32_t* indice_num_dev, int32_t* num_out_dev,
+                         void* workspace_dev, size_t workspace_bytes, void* stream);
+
+int bfb_indice_pairs_outids(int64_t n, int ndim, int64_t batch, const int64_t* out_shape,
+                            const int64_t* ksize, const void* workspace_dev, size_t workspace_bytes,
+                            int32_t* outids_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

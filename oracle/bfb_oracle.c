@@ -15,6 +15,10 @@
  *                         (`_hard_voxelize_cpu_fallback`).
  *   - dynamic scatter     ops/voxel/src/scatter_points_triton.py:150-250 (`_clean_coors`,
  *                         `_unique_with_inverse_and_counts`, forward) and :317-345 (backward).
+ *   - indice pairs        ops/spconv/src/spconv_triton.py:321-334 (`_row_array_idx`),
+ *                         :528-605 (`_valid_out_pos`, `_valid_out_pos_transpose`),
+ *                         :655-749 (`_get_indice_pairs_impl`, cuda_ordering=True: the
+ *                         order of the reference's GPU path).
  *
  * Compiled with -O2 -ffp-contract=off and without fast-math so every fp32
  * operation rounds exactly as in the reference (SSE fp32, one rounding per op).
@@ -287,4 +291,160 @@ void oracle_scatter_bwd(const float* grad_out, const float* feats, const float* 
     }
   }
   free(done);
+}
+
+/* ----------------------------------------------------------------------- */
+/* sparse-convolution rulebook                                             */
+/* ----------------------------------------------------------------------- */
+
+static int64_t floordiv64(int64_t a, int64_t b) {
+  int64_t q = a / b;
+  if ((a % b != 0) && ((a < 0) != (b < 0))) --q;
+  return q;
+}
+
+#define SP_MAXD 4
+
+/* Output positions reached from input position `in` with their kernel
+ * offsets, in the enumeration order of _valid_out_pos /
+ * _valid_out_pos_transpose.  Returns the count. */
+static int valid_out_pos(const int64_t* in, int ndim, const int64_t* ks, const int64_t* st, const int64_t* pad,
+                         const int64_t* dil, const int64_t* out_shape, int transpose, int64_t* coords_out,
+                         int64_t* offsets) {
+  int64_t lo[SP_MAXD], up[SP_MAXD], sz[SP_MAXD];
+  for (int i = 0; i < ndim; ++i) {
+    if (transpose) {
+      lo[i] = in[i] * st[i] - pad[i];
+      up[i] = lo[i] + (ks[i] - 1) * dil[i];
+    } else {
+      lo[i] = floordiv64(in[i] - (ks[i] - 1) * dil[i] - 1 + st[i] + pad[i], st[i]);
+      up[i] = floordiv64(in[i] + pad[i], st[i]);
+    }
+    sz[i] = floordiv64(up[i] - lo[i], dil[i]) + 1;
+    if (sz[i] <= 0) return 0;
+  }
+  int64_t ctr[SP_MAXD] = {0, 0, 0, 0};
+  int cnt = 0;
+  for (;;) {
+    int64_t off = 0, mult = 1;
+    int ok = 1;
+    for (int j = ndim - 1; j >= 0; --j) {
+      const int64_t val = up[j] - ctr[j] * dil[j];
+      coords_out[cnt * ndim + j] = val;
+      if (val < 0 || val > out_shape[j] - 1) ok = 0;
+      off += mult * (transpose ? floordiv64(val - lo[j], dil[j]) : floordiv64(in[j] - val * st[j] + pad[j], dil[j]));
+      mult *= ks[j];
+    }
+    if (ok) offsets[cnt++] = off;
+    int d = ndim - 1; /* itertools.product: last counter fastest */
+    while (d >= 0 && ++ctr[d] == sz[d]) ctr[d--] = 0;
+    if (d < 0) break;
+  }
+  return cnt;
+}
+
+static int cmp_i64(const void* a, const void* b) {
+  const int64_t x = *(const int64_t*)a, y = *(const int64_t*)b;
+  return x < y ? -1 : x > y;
+}
+
+/* pairs [K, 2, n] must be filled with -1 and num [K] with 0 by the caller;
+ * outids has room for n*K rows of ndim+1 (regular) and gets the input rows
+ * for submanifold.  Returns the number of output rows. */
+int64_t oracle_indice_pairs(const int32_t* idx, int64_t n, int ndim, const int64_t* out_shape,
+                            const int64_t* ks, const int64_t* st, const int64_t* pad, const int64_t* dil,
+                            int subm, int transpose, int32_t* pairs, int32_t* num, int32_t* outids) {
+  int64_t K = 1, vol = 1;
+  for (int i = 0; i < ndim; ++i) {
+    K *= ks[i];
+    vol *= out_shape[i];
+  }
+  int64_t maxpts = K;
+  int64_t* oc = (int64_t*)malloc(sizeof(int64_t) * (size_t)(maxpts * ndim + 1));
+  int64_t* ofs = (int64_t*)malloc(sizeof(int64_t) * (size_t)(maxpts + 1));
+  /* flat index of every input (submanifold map), last writer wins */
+  int64_t* inflat = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n + 1) * 2);
+  int64_t* pend = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n * K + 1) * 3);
+  int64_t npend = 0, nout = 0;
+  for (int64_t j = 0; j < n; ++j) {
+    const int32_t* row = idx + j * (ndim + 1);
+    int64_t f = 0;
+    for (int d = 0; d < ndim; ++d) f = f * out_shape[d] + row[1 + d];
+    inflat[2 * j] = f + vol * row[0];
+    inflat[2 * j + 1] = j;
+  }
+  if (subm) {
+    /* sort (flat, j) ascending; a lookup takes the last entry of a run */
+    qsort(inflat, (size_t)n, 2 * sizeof(int64_t), cmp_i64);
+    for (int64_t j = 0; j < n; ++j)
+      for (int d = 0; d <= ndim; ++d) outids[j * (ndim + 1) + d] = idx[j * (ndim + 1) + d];
+    nout = n;
+  }
+  for (int64_t j = 0; j < n; ++j) {
+    const int32_t* row = idx + j * (ndim + 1);
+    int64_t in[SP_MAXD];
+    for (int d = 0; d < ndim; ++d) in[d] = row[1 + d];
+    const int cnt = valid_out_pos(in, ndim, ks, st, pad, dil, out_shape, transpose, oc, ofs);
+    for (int q = 0; q < cnt; ++q) {
+      int64_t f = 0;
+      for (int d = 0; d < ndim; ++d) f = f * out_shape[d] + oc[q * ndim + d];
+      f += vol * row[0];
+      const int64_t off = ofs[q];
+      if (subm) {
+        /* binary search for the last (flat == f) entry */
+        int64_t lo = 0, hi = n;
+        while (lo < hi) {
+          const int64_t mid = (lo + hi) / 2;
+          if (inflat[2 * mid] <= f) lo = mid + 1; else hi = mid;
+        }
+        if (lo == 0 || inflat[2 * (lo - 1)] != f) continue;
+        /* among equal flats the sort put them in j order only if stable; take the max j */
+        int64_t best = -1;
+        for (int64_t e = lo - 1; e >= 0 && inflat[2 * e] == f; --e)
+          if (inflat[2 * e + 1] > best) best = inflat[2 * e + 1];
+        const int32_t slot = num[off]++;
+        pairs[(off * 2 + 0) * n + slot] = (int32_t)j;
+        pairs[(off * 2 + 1) * n + slot] = (int32_t)best;
+      } else {
+        pend[3 * npend] = off;
+        pend[3 * npend + 1] = j;
+        pend[3 * npend + 2] = f;
+        ++npend;
+      }
+    }
+  }
+  if (!subm) {
+    int64_t* uniq = (int64_t*)malloc(sizeof(int64_t) * (size_t)(npend + 1));
+    for (int64_t i = 0; i < npend; ++i) uniq[i] = pend[3 * i + 2];
+    qsort(uniq, (size_t)npend, sizeof(int64_t), cmp_i64);
+    for (int64_t i = 0; i < npend; ++i)
+      if (i == 0 || uniq[i] != uniq[i - 1]) uniq[nout++] = uniq[i];
+    for (int64_t o = 0; o < nout; ++o) {
+      int64_t f = uniq[o];
+      int32_t* r = outids + o * (ndim + 1);
+      r[0] = (int32_t)(f / vol);
+      f %= vol;
+      for (int d = ndim - 1; d >= 0; --d) {
+        r[1 + d] = (int32_t)(f % out_shape[d]);
+        f /= out_shape[d];
+      }
+    }
+    for (int64_t i = 0; i < npend; ++i) {
+      const int64_t off = pend[3 * i], f = pend[3 * i + 2];
+      int64_t lo = 0, hi = nout;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) / 2;
+        if (uniq[mid] < f) lo = mid + 1; else hi = mid;
+      }
+      const int32_t slot = num[off]++;
+      pairs[(off * 2 + 0) * n + slot] = (int32_t)pend[3 * i + 1];
+      pairs[(off * 2 + 1) * n + slot] = (int32_t)lo;
+    }
+    free(uniq);
+  }
+  free(oc);
+  free(ofs);
+  free(inflat);
+  free(pend);
+  return nout;
 }

@@ -49,6 +49,9 @@ def lib():
         L.oracle_scatter_fwd.argtypes = [_f32p, _i64, _i64, _i32p, _i32p, _i64, ctypes.c_int, _f32p]
         L.oracle_scatter_bwd.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i32p, _i32p, _i64,
                                          ctypes.c_int, _f32p]
+        L.oracle_indice_pairs.argtypes = [_i32p, _i64, ctypes.c_int, _i64p, _i64p, _i64p, _i64p, _i64p,
+                                          ctypes.c_int, ctypes.c_int, _i32p, _i32p, _i32p]
+        L.oracle_indice_pairs.restype = _i64
         _lib = L
     return _lib
 
@@ -140,3 +143,18 @@ def dynamic_scatter_backward(grad_out, feats, reduced, point2voxel, counts, redu
                              np.ascontiguousarray(counts, np.int32), r.shape[0],
                              _REDUCE[reduce_type], out)
     return out
+
+
+def indice_pairs(indices, out_shape, ksize, stride, padding, dilation, subm, transpose):
+    """Rulebook of a sparse convolution (the reference's sequential algorithm
+    with the GPU path's output order).  Returns (outids, pairs [K, 2, n],
+    num [K]) as int32 arrays."""
+    idx = np.ascontiguousarray(np.asarray(indices, dtype=np.int32))
+    n, nd = idx.shape[0], idx.shape[1] - 1
+    a = [np.ascontiguousarray(np.asarray(v, dtype=np.int64)) for v in (out_shape, ksize, stride, padding, dilation)]
+    K = int(np.prod(a[1]))
+    pairs = np.full((K, 2, n), -1, dtype=np.int32)
+    num = np.zeros((K,), dtype=np.int32)
+    outids = np.zeros((max(n * K, 1), nd + 1), dtype=np.int32)
+    m = lib().oracle_indice_pairs(idx, n, nd, *a, int(bool(subm)), int(bool(transpose)), pairs, num, outids)
+    return outids[:m], pairs, num

@@ -12,6 +12,10 @@ package modules:
 * ops/bev_pool/src/bev_pool_triton.py            ``bev_pool`` (CPU path: ``_bev_pool_cpu``)
 * ops/voxel/src/voxelization_triton.py           ``dynamic_voxelize``, ``hard_voxelize``
 * ops/voxel/src/scatter_points_triton.py         ``dynamic_point_to_voxel_forward/backward``
+* ops/spconv/src/spconv_triton.py                ``_get_indice_pairs_impl`` (rulebooks, with the
+                                                 GPU path's output order: cuda_ordering=True)
+
+``--only spconv`` regenerates only the rulebook fixture.
 
 Cases mirror the reference tests (tests/test_ops/test_bev_pool.py:24-84,
 tests/test_ops/test_voxel.py:27-79) plus seeded larger cases and full-size
@@ -38,7 +42,8 @@ from bevfusion_triton_b200 import synth  # noqa: E402
 
 def import_reference(ref: Path):
     for name, sub in [('ops', 'ops'), ('ops.bev_pool', 'ops/bev_pool'), ('ops.bev_pool.src', 'ops/bev_pool/src'),
-                      ('ops.voxel', 'ops/voxel'), ('ops.voxel.src', 'ops/voxel/src')]:
+                      ('ops.voxel', 'ops/voxel'), ('ops.voxel.src', 'ops/voxel/src'), ('ops.spconv', 'ops/spconv'),
+                      ('ops.spconv.src', 'ops/spconv/src')]:
         m = types.ModuleType(name)
         m.__path__ = [str(ref / sub)]
         sys.modules[name] = m
@@ -46,6 +51,50 @@ def import_reference(ref: Path):
     import ops.voxel.src.scatter_points_triton as spt
     import ops.voxel.src.voxelization_triton as vt
     return bpt, vt, spt
+
+
+def import_spconv():
+    import ops.spconv.src.spconv_triton as sct
+    return sct
+
+
+SPCONV_CASES = [
+    # spatial shape, ksize, stride, padding, dilation, subm, transpose
+    ([8, 8], [3, 3], [1, 1], [1, 1], [1, 1], True, False),
+    ([9, 7], [3, 3], [2, 2], [1, 1], [1, 1], False, False),
+    ([6, 5, 7], [3, 3, 3], [2, 2, 2], [0, 1, 1], [1, 1, 1], False, False),
+    ([6, 5, 7], [1, 1, 3], [1, 1, 2], [0, 0, 0], [1, 1, 1], False, False),
+    ([6, 5, 7], [3, 3, 3], [1, 1, 1], [1, 1, 1], [1, 1, 1], True, False),
+    ([5, 6], [3, 3], [2, 2], [1, 1], [1, 1], False, True),
+    ([8, 9], [3, 3], [1, 1], [2, 2], [2, 2], False, False),
+    ([4, 3, 3, 5], [3, 1, 3, 2], [1, 1, 1, 1], [1, 0, 1, 0], [1, 1, 1, 1], False, False),
+    ([20, 20, 6], [3, 3, 3], [2, 2, 2], [1, 1, 1], [1, 1, 1], False, False),
+]
+
+
+def spconv_cases(sct):
+    """Rulebooks of small sparse tensors (2 samples, unique random sites),
+    tests/test_ops/test_spconv/test_spconv_ops.py shapes and the sparse
+    encoder's layer kinds (submanifold 3x3x3, strided 3x3x3, (1, 1, 3)
+    stride (1, 1, 2))."""
+    g = torch.Generator().manual_seed(11)
+    out = {}
+    for i, (shape, k, st, pd, dl, subm, tr) in enumerate(SPCONV_CASES):
+        B = 2
+        n = min(60, B * int(np.prod(shape)) // 3)
+        cells = torch.randperm(B * int(np.prod(shape)), generator=g)[:n]
+        f, cols = cells.clone(), []
+        for d in reversed(shape):
+            cols.append(f % d)
+            f //= d
+        idx = torch.stack([f] + cols[::-1], 1).int()
+        _, ks, ss, ps, ds, _, outs = sct._prepare_indice_pair_args(idx, B, shape, ksize=k, stride=st, padding=pd,
+                                                                   dilation=dl, subm=subm, transpose=tr)
+        o, pr, nm = sct._get_indice_pairs_impl(idx, B, outs, ks, ss, ps, ds, subm=subm, transpose=tr,
+                                               cuda_ordering=True, grid=None)
+        out.update({f'c{i}_indices': idx, f'c{i}_cfg': np.array(shape + k + st + pd + dl + [int(subm), int(tr), B]),
+                    f'c{i}_outshape': np.array(outs), f'c{i}_outids': o, f'c{i}_pairs': pr, f'c{i}_num': nm})
+    save('spconv_cases', **out)
 
 
 def sha(a) -> str:
@@ -194,11 +243,15 @@ def main():
         raise SystemExit('usage: make_golden.py <path to the bevfusion-triton checkout>')
     ref = Path(sys.argv[1]).resolve()
     bpt, vt, spt = import_reference(ref)
+    if '--only' in sys.argv and sys.argv[sys.argv.index('--only') + 1] == 'spconv':
+        spconv_cases(import_spconv())
+        return
     torch.set_num_threads(8)
     digests = {}
     digests.update(bev_cases(bpt))
     digests.update(voxel_cases(vt))
     scatter_cases(spt)
+    spconv_cases(import_spconv())
     (HERE / 'digests.json').write_text(json.dumps(digests, indent=1, sort_keys=True) + '\n')
     print(json.dumps(digests, indent=1))
 

@@ -103,3 +103,25 @@ def test_dynamic_scatter(golden, case, red):
     np.testing.assert_allclose(vf, g[f'{case}_{red}_vf'], rtol=1e-6, atol=1e-6)
     grad = oracle.dynamic_scatter_backward(g[f'{case}_{red}_up'], f, vf, mp, cnt, red)
     np.testing.assert_allclose(grad, g[f'{case}_{red}_grad'], rtol=1e-6, atol=1e-6)
+
+
+def spconv_case(g, i):
+    """Decode one rulebook fixture: (indices, out_shape, params, expected)."""
+    cfg = [int(v) for v in g[f'c{i}_cfg']]
+    nd = (len(cfg) - 3) // 5
+    shape, k, s, p, d = (cfg[j * nd:(j + 1) * nd] for j in range(5))
+    subm, tr, B = cfg[5 * nd:]
+    return (g[f'c{i}_indices'], [int(v) for v in g[f'c{i}_outshape']], shape, k, s, p, d, bool(subm), bool(tr), B,
+            (g[f'c{i}_outids'], g[f'c{i}_pairs'], g[f'c{i}_num']))
+
+
+@pytest.mark.parametrize('i', range(9))
+def test_indice_pairs_match_reference(golden, i):
+    """The C restatement of the rulebook against the reference's own
+    _get_indice_pairs_impl (GPU ordering): outputs, pairs and counts equal."""
+    g = golden('spconv_cases')
+    idx, outs, _, k, s, p, d, subm, tr, _, (w_out, w_pairs, w_num) = spconv_case(g, i)
+    o, pr, nm = oracle.indice_pairs(idx, outs, k, s, p, d, subm, tr)
+    np.testing.assert_array_equal(o, w_out)
+    np.testing.assert_array_equal(pr, w_pairs)
+    np.testing.assert_array_equal(nm, w_num)
