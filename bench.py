@@ -302,6 +302,8 @@ def run_ours(args, ws, rank, local):
     }
     if not args.no_e2e:
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
+    if not args.no_rulebook:
+        line['sparse_rulebook'] = run_rulebook(args, wl, ws)
     if not args.no_fused:
         del wl
         torch.cuda.empty_cache()
@@ -404,6 +406,39 @@ def run_e2e(args, wl, ws, samples_total):
     return {'value': round(ms / samples_total, 4), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
             'd2h_bytes_per_step': d2h, 'steps': steps, 'ms_per_step': round(ms, 3),
             'pipeline': 'per sample over 3 streams (H2D / compute / D2H), consecutive steps overlap', 'voxel_counts_match_device_step': ok}
+
+
+def run_rulebook(args, wl, ws):
+    """Sparse-convolution rulebooks of the sparse encoder's layer kinds over
+    the rank's voxelised LiDAR samples (the voxel sites of the step above,
+    (b, x, y, z) on the (1440, 1440, 41) sparse shape), device-resident: ms
+    per get_indice_pairs call, including its one host read of the output
+    count as in the reference."""
+    from bevfusion_triton_b200.ops.spconv import get_indice_pairs
+    S = wl.S
+    vn = wl.vn.tolist()
+    idx = torch.cat([torch.cat((torch.full((int(vn[b]), 1), b, dtype=torch.int32, device=wl.vcoors.device),
+                                wl.vcoors[b, :int(vn[b])]), 1) for b in range(S)]).contiguous()
+    shape = [1440, 1440, 41]
+    layers = {'subm_k3': dict(ksize=3, stride=1, padding=1, subm=True),
+              'down_k3_s2': dict(ksize=3, stride=2, padding=1),
+              'out_k113_s112': dict(ksize=(1, 1, 3), stride=(1, 1, 2), padding=0)}
+    res = {'sites': int(idx.size(0)), 'sparse_shape': shape}
+    for name, kw in layers.items():
+        for _ in range(3):
+            get_indice_pairs(idx, S, shape, **kw)
+        torch.cuda.synchronize()
+        barrier(ws)
+        k = max(3, min(args.steps, 20))
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            o, pr, nm = get_indice_pairs(idx, S, shape, **kw)
+        s1.record()
+        torch.cuda.synchronize()
+        res[name] = {'ms_per_call': round(max_over_ranks(s0.elapsed_time(s1), ws) / k, 4),
+                     'out_sites': int(o.size(0)), 'pairs': int(nm.sum())}
+    return res
 
 
 def run_fused(args, rank, ws):
@@ -555,6 +590,7 @@ def main():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-fused', action='store_true')
+    ap.add_argument('--no-rulebook', action='store_true')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3  # timing rule: at least 3 warm-up steps
