@@ -26,6 +26,8 @@
 //   spc_pack writes indice_pairs[k, 0/1, slot] and spc_counts indice_num.
 //   spc_outids (regular only, second call once the caller knows the count)
 //   decodes the set bits into [b, c0, .., c{ndim-1}] rows.
+#include <algorithm>
+
 #include "scan.cuh"
 
 namespace bfb {
@@ -91,36 +93,46 @@ __device__ __forceinline__ uint32_t flat_of(const int32_t* row, const SpGeom& g)
   return (uint32_t)((uint64_t)row[0] * (uint64_t)g.volume + f);
 }
 
+// Rule-major launches: blockIdx.y = kernel offset k, threads stride over
+// the sites j; every per-candidate array is indexed k * n + j, so no thread
+// divides by K or n.
+__device__ __forceinline__ void kernel_offset(int64_t k, const SpGeom& g, int64_t (&kd)[kSpMaxDims]) {
+  for (int d = g.ndim - 1; d >= 0; --d) {  // last dimension fastest
+    kd[d] = k % g.ks[d];
+    k /= g.ks[d];
+  }
+}
+
 __global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n, SpGeom g,
                                       uint32_t* __restrict__ cell, uint32_t* __restrict__ flags) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n * g.K) return;
-  const int64_t j = t / g.K;
-  int64_t rem = t - j * g.K;
-  const int32_t* row = idx + j * (g.ndim + 1);
+  const int64_t k = blockIdx.y;
   int64_t kd[kSpMaxDims];
-  for (int d = g.ndim - 1; d >= 0; --d) {  // last dimension fastest
-    kd[d] = rem % g.ks[d];
-    rem /= g.ks[d];
-  }
-  bool ok = true;
-  uint64_t f = 0;
-  for (int d = 0; d < g.ndim; ++d) {
-    const int64_t in = row[1 + d];
-    int64_t o;
-    if (g.transpose) {
-      o = in * g.st[d] - g.pad[d] + kd[d] * g.dil[d];
-    } else {
-      const int64_t num = in + g.pad[d] - kd[d] * g.dil[d];
-      ok = ok && num % g.st[d] == 0;
-      o = num / g.st[d];
+  kernel_offset(k, g, kd);
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t* row = idx + j * (g.ndim + 1);
+    bool ok = true;
+    uint64_t f = 0;
+    for (int d = 0; d < g.ndim; ++d) {
+      const int64_t in = __ldg(row + 1 + d);
+      int64_t o;
+      if (g.transpose) {
+        o = in * g.st[d] - g.pad[d] + kd[d] * g.dil[d];
+      } else {
+        const int64_t num = in + g.pad[d] - kd[d] * g.dil[d];
+        if (g.st[d] == 1) {
+          o = num;
+        } else {
+          ok = ok && num % g.st[d] == 0;
+          o = num / g.st[d];
+        }
+      }
+      ok = ok && o >= 0 && o < g.out[d];
+      f = f * (uint64_t)g.out[d] + (uint64_t)(ok ? o : 0);
     }
-    ok = ok && o >= 0 && o < g.out[d];
-    f = f * (uint64_t)g.out[d] + (uint64_t)(ok ? o : 0);
+    const int64_t t = k * n + j;
+    cell[t] = (uint32_t)((uint64_t)__ldg(row) * (uint64_t)g.volume + f);
+    flags[t] = ok ? 1u : 0u;
   }
-  const int64_t k = t - j * g.K;
-  cell[t] = (uint32_t)((uint64_t)row[0] * (uint64_t)g.volume + f);
-  flags[k * n + j] = ok ? 1u : 0u;
 }
 
 // submanifold: cell of every input -> the largest input index holding it
@@ -133,15 +145,14 @@ __global__ void spc_insert_inputs_kernel(const int32_t* __restrict__ idx, int64_
 }
 
 // regular / transposed: one bit per grid cell that some candidate reaches
-__global__ void spc_mark_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t n,
-                                int64_t K, uint32_t* __restrict__ bits) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n * K) return;
-  const int64_t j = t / K, k = t - j * K;
-  if (!flags[k * n + j]) return;
-  const uint32_t c = cell[t];
-  const uint32_t m = 1u << (c & 31);
-  if (!(bits[c >> 5] & m)) atomicOr(bits + (c >> 5), m);  // skip the atomic once the bit is seen set
+__global__ void spc_mark_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t c,
+                                uint32_t* __restrict__ bits) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < c; t += (int64_t)gridDim.x * blockDim.x) {
+    if (!flags[t]) continue;
+    const uint32_t x = cell[t];
+    const uint32_t m = 1u << (x & 31);
+    if (!(bits[x >> 5] & m)) atomicOr(bits + (x >> 5), m);  // skip the atomic once the bit is seen set
+  }
 }
 
 __global__ void spc_popc_kernel(const uint32_t* __restrict__ bits, int64_t words, uint32_t* __restrict__ cnt) {
@@ -150,45 +161,44 @@ __global__ void spc_popc_kernel(const uint32_t* __restrict__ bits, int64_t words
 }
 
 // regular: output id of a candidate = rank of its cell's bit
-__global__ void spc_rank_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t n,
-                                int64_t K, const uint32_t* __restrict__ bits, const uint32_t* __restrict__ prefix,
+__global__ void spc_rank_kernel(const uint32_t* __restrict__ cell, const uint32_t* __restrict__ flags, int64_t c,
+                                const uint32_t* __restrict__ bits, const uint32_t* __restrict__ prefix,
                                 int32_t* __restrict__ out_of) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n * K) return;
-  const int64_t j = t / K, k = t - j * K;
-  if (!flags[k * n + j]) return;
-  const uint32_t c = cell[t], w = c >> 5;
-  out_of[t] = (int32_t)(__ldg(prefix + w) + (uint32_t)__popc(__ldg(bits + w) & ((1u << (c & 31)) - 1u)));
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < c; t += (int64_t)gridDim.x * blockDim.x) {
+    if (!flags[t]) continue;
+    const uint32_t x = cell[t], w = x >> 5;
+    out_of[t] = (int32_t)(__ldg(prefix + w) + (uint32_t)__popc(__ldg(bits + w) & ((1u << (x & 31)) - 1u)));
+  }
 }
 
 // submanifold: candidate -> the input at its cell, dropped when there is none
-__global__ void spc_lookup_kernel(const uint32_t* __restrict__ cell, uint32_t* __restrict__ flags, int64_t n,
-                                  int64_t K, const SpSlot* __restrict__ tb, uint64_t cap,
-                                  int32_t* __restrict__ out_of) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n * K) return;
-  const int64_t j = t / K, k = t - j * K;
-  const int64_t f = k * n + j;
-  if (!flags[f]) return;
-  const int64_t s = sp_find(tb, cap, cell[t]);
-  if (s < 0) {
-    flags[f] = 0u;
-    return;
+__global__ void spc_lookup_kernel(const uint32_t* __restrict__ cell, uint32_t* __restrict__ flags, int64_t c,
+                                  const SpSlot* __restrict__ tb, uint64_t cap, int32_t* __restrict__ out_of) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < c; t += (int64_t)gridDim.x * blockDim.x) {
+    if (!flags[t]) continue;
+    const int64_t s = sp_find(tb, cap, cell[t]);
+    if (s < 0) {
+      flags[t] = 0u;
+      continue;
+    }
+    out_of[t] = tb[s].val;
   }
-  out_of[t] = tb[s].val;
 }
 
 // pos = exclusive scan of the rule-major flags (pos[n*K] = total): rule k's
 // pairs occupy [pos[k*n], pos[(k+1)*n]) in ascending j
-__global__ void spc_pack_kernel(const uint32_t* __restrict__ pos, int64_t n, int64_t K,
-                                const int32_t* __restrict__ out_of, int32_t* __restrict__ pairs) {
-  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (f >= n * K) return;
-  if (pos[f + 1] == pos[f]) return;  // flag was 0
-  const int64_t k = f / n, j = f - k * n;
-  const int64_t slot = (int64_t)pos[f] - (int64_t)pos[k * n];
-  pairs[(k * 2 + 0) * n + slot] = (int32_t)j;
-  pairs[(k * 2 + 1) * n + slot] = out_of[j * K + k];
+__global__ void spc_pack_kernel(const uint32_t* __restrict__ pos, int64_t n, const int32_t* __restrict__ out_of,
+                                int32_t* __restrict__ pairs) {
+  const int64_t k = blockIdx.y;
+  const uint32_t base = pos[k * n];
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = k * n + j;
+    const uint32_t p = pos[t];
+    if (pos[t + 1] == p) continue;  // flag was 0
+    const int64_t slot = (int64_t)(p - base);
+    pairs[(k * 2 + 0) * n + slot] = (int32_t)j;
+    pairs[(k * 2 + 1) * n + slot] = out_of[t];
+  }
 }
 
 __global__ void spc_counts_kernel(const uint32_t* __restrict__ pos, int64_t n, int64_t K,
@@ -227,9 +237,9 @@ __global__ void spc_total_kernel(const uint32_t* __restrict__ prefix, int64_t wo
 }
 
 struct SpWork {
-  uint32_t* cell;    // [n*K] candidate cell
-  uint32_t* flags;   // [n*K + 1] rule-major flags, then their exclusive scan
-  int32_t* out_of;   // [n*K] output index per candidate
+  uint32_t* cell;    // [K*n] candidate cell, rule-major
+  uint32_t* flags;   // [K*n + 1] rule-major flags, then their exclusive scan
+  int32_t* out_of;   // [K*n] output index per candidate
   SpSlot* table;     // [cap] submanifold: cell -> input
   uint32_t* bits;    // [words] regular: reached cells
   uint32_t* prefix;  // [words + 1] regular: set bits before each word
@@ -310,32 +320,33 @@ extern "C" int bfb_get_indice_pairs(const int32_t* indices, int64_t n, int ndim,
   BFB_CUDA(cudaMemsetAsync(indice_num, 0, sizeof(int32_t) * (size_t)g.K, st));
   BFB_CUDA(cudaMemsetAsync(num_out_dev, 0, sizeof(int32_t), st));
   if (n == 0) return BFB_OK;
-  const unsigned nbc = (unsigned)ceil_div(c, kSpThreads);
-  spc_candidates_kernel<<<nbc, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags);
+  const unsigned nbc = (unsigned)std::min<int64_t>(ceil_div(c, kSpThreads), 148 * 32);  // grid-stride over t
+  const dim3 grid_kj((unsigned)std::min<int64_t>(ceil_div(n, kSpThreads), 1024), (unsigned)g.K);
+  spc_candidates_kernel<<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags);
   BFB_CHECK_LAUNCH();
   if (subm) {
     BFB_CUDA(cudaMemsetAsync(w.table, 0xff, sizeof(SpSlot) * (size_t)w.cap, st));  // key free, val -1
     spc_insert_inputs_kernel<<<(unsigned)ceil_div(n, kSpThreads), kSpThreads, 0, st>>>(indices, n, g, w.table,
                                                                                       w.cap);
     BFB_CHECK_LAUNCH();
-    spc_lookup_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.table, w.cap, w.out_of);
+    spc_lookup_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, c, w.table, w.cap, w.out_of);
     BFB_CHECK_LAUNCH();
     spc_set_count_kernel<<<1, 1, 0, st>>>(num_out_dev, (int32_t)n);
     BFB_CHECK_LAUNCH();
   } else {
     BFB_CUDA(cudaMemsetAsync(w.bits, 0, sizeof(uint32_t) * (size_t)w.words, st));
-    spc_mark_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.bits);
+    spc_mark_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, c, w.bits);
     BFB_CHECK_LAUNCH();
     spc_popc_kernel<<<(unsigned)ceil_div(w.words, kSpThreads), kSpThreads, 0, st>>>(w.bits, w.words, w.prefix);
     BFB_CHECK_LAUNCH();
     BFB_TRY(exclusive_scan_u32(w.prefix, w.prefix, w.words, w.scan, w.prefix + w.words, st));
-    spc_rank_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, n, g.K, w.bits, w.prefix, w.out_of);
+    spc_rank_kernel<<<nbc, kSpThreads, 0, st>>>(w.cell, w.flags, c, w.bits, w.prefix, w.out_of);
     BFB_CHECK_LAUNCH();
     spc_total_kernel<<<1, 1, 0, st>>>(w.prefix, w.words, num_out_dev);
     BFB_CHECK_LAUNCH();
   }
   BFB_TRY(exclusive_scan_u32(w.flags, w.flags, c, w.scan, w.flags + c, st));
-  spc_pack_kernel<<<nbc, kSpThreads, 0, st>>>(w.flags, n, g.K, w.out_of, indice_pairs);
+  spc_pack_kernel<<<grid_kj, kSpThreads, 0, st>>>(w.flags, n, w.out_of, indice_pairs);
   BFB_CHECK_LAUNCH();
   spc_counts_kernel<<<(unsigned)ceil_div(g.K, kSpThreads), kSpThreads, 0, st>>>(w.flags, n, g.K, indice_num);
   BFB_CHECK_LAUNCH();

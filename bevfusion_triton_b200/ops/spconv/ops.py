@@ -55,10 +55,10 @@ def get_indice_pairs(indices: torch.Tensor, batch_size: int, spatial_shape, ksiz
     if not indices.is_cuda:
         raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
     if indices.numel() > 0:
-        b = indices[:, 0]
-        if int(b.min().item()) < 0:
+        bmin, bmax = (int(v) for v in torch.aminmax(indices[:, 0]))  # one host read
+        if bmin < 0:
             raise ValueError('indices batch column must be non-negative')
-        if int(b.max().item()) >= batch_size:
+        if bmax >= batch_size:
             raise ValueError('indices batch column exceeds batch_size')
     ndim = indices.shape[1] - 1
     ksize, stride, padding = _nd(ksize, ndim), _nd(stride, ndim), _nd(padding, ndim)
