@@ -43,6 +43,7 @@ struct SpGeom {
   int64_t volume;  // product of out[]
   int64_t K;       // product of ks[]
   bool transpose;
+  FastDiv vol_div, out_div[kSpMaxDims];  // flat cells fit 32 bits
 };
 
 struct SpSlot {
@@ -96,41 +97,51 @@ __device__ __forceinline__ uint32_t flat_of(const int32_t* row, const SpGeom& g)
 // Rule-major launches: blockIdx.y = kernel offset k, threads stride over
 // the sites j; every per-candidate array is indexed k * n + j, so no thread
 // divides by K or n.
-__device__ __forceinline__ void kernel_offset(int64_t k, const SpGeom& g, int64_t (&kd)[kSpMaxDims]) {
+__device__ __forceinline__ void kernel_offset(int k, const SpGeom& g, int (&kd)[kSpMaxDims]) {
   for (int d = g.ndim - 1; d >= 0; --d) {  // last dimension fastest
-    kd[d] = k % g.ks[d];
-    k /= g.ks[d];
+    const int ks = (int)g.ks[d];
+    kd[d] = k % ks;
+    k /= ks;
   }
 }
 
+// 32-bit coordinate arithmetic: coordinates, offsets and output extents are
+// below 2^31 and every flat cell below 2^32 (checked on the host).
 __global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n, SpGeom g,
                                       uint32_t* __restrict__ cell, uint32_t* __restrict__ flags) {
-  const int64_t k = blockIdx.y;
-  int64_t kd[kSpMaxDims];
+  const int k = blockIdx.y;
+  int kd[kSpMaxDims];
   kernel_offset(k, g, kd);
+  int base[kSpMaxDims], st[kSpMaxDims];
+  uint32_t out[kSpMaxDims];
+  for (int d = 0; d < g.ndim; ++d) {  // out = (in + base) / st  or  in * st + base
+    base[d] = g.transpose ? (int)(kd[d] * g.dil[d] - g.pad[d]) : (int)(g.pad[d] - kd[d] * g.dil[d]);
+    st[d] = (int)g.st[d];
+    out[d] = (uint32_t)g.out[d];
+  }
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
     const int32_t* row = idx + j * (g.ndim + 1);
     bool ok = true;
-    uint64_t f = 0;
+    uint32_t f = 0;
     for (int d = 0; d < g.ndim; ++d) {
-      const int64_t in = __ldg(row + 1 + d);
-      int64_t o;
+      const int in = __ldg(row + 1 + d);
+      int o;
       if (g.transpose) {
-        o = in * g.st[d] - g.pad[d] + kd[d] * g.dil[d];
+        o = in * st[d] + base[d];
       } else {
-        const int64_t num = in + g.pad[d] - kd[d] * g.dil[d];
-        if (g.st[d] == 1) {
+        const int num = in + base[d];
+        if (st[d] == 1) {
           o = num;
         } else {
-          ok = ok && num % g.st[d] == 0;
-          o = num / g.st[d];
+          ok = ok && num % st[d] == 0;
+          o = num / st[d];
         }
       }
-      ok = ok && o >= 0 && o < g.out[d];
-      f = f * (uint64_t)g.out[d] + (uint64_t)(ok ? o : 0);
+      ok = ok && o >= 0 && (uint32_t)o < out[d];
+      f = f * out[d] + (ok ? (uint32_t)o : 0u);
     }
-    const int64_t t = k * n + j;
-    cell[t] = (uint32_t)((uint64_t)__ldg(row) * (uint64_t)g.volume + f);
+    const int64_t t = (int64_t)k * n + j;
+    cell[t] = (uint32_t)__ldg(row) * (uint32_t)g.volume + f;
     flags[t] = ok ? 1u : 0u;
   }
 }
@@ -214,17 +225,20 @@ __global__ void spc_outids_kernel(const uint32_t* __restrict__ bits, const uint3
   const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (w >= words) return;
   uint32_t m = bits[w];
+  if (!m) return;
   uint32_t pos = prefix[w];
   while (m) {
     const int b = __ffs(m) - 1;
     m &= m - 1;
-    uint64_t f = (uint64_t)w * 32 + (uint64_t)b;
+    const uint32_t flat = (uint32_t)w * 32u + (uint32_t)b;
     int32_t* row = outids + (int64_t)pos * (g.ndim + 1);
-    row[0] = (int32_t)(f / (uint64_t)g.volume);
-    f %= (uint64_t)g.volume;
+    const uint32_t bi = g.vol_div.div(flat);
+    uint32_t f = flat - bi * g.vol_div.d;
+    row[0] = (int32_t)bi;
     for (int d = g.ndim - 1; d >= 0; --d) {
-      row[1 + d] = (int32_t)(f % (uint64_t)g.out[d]);
-      f /= (uint64_t)g.out[d];
+      const uint32_t q = g.out_div[d].div(f);
+      row[1 + d] = (int32_t)(f - q * g.out_div[d].d);
+      f = q;
     }
     ++pos;
   }
@@ -281,6 +295,13 @@ int make_sp_geom(int ndim, int64_t batch, const int64_t* out_shape, const int64_
     g->K *= ksize[d];
   }
   if ((uint64_t)batch * (uint64_t)g->volume >= 0xffffffffull) return BFB_ERR_TOO_LARGE;  // cells fit 32 bits
+  for (int d = 0; d < ndim; ++d) {
+    const int64_t reach = (ksize[d] - 1) * dilation[d] + (padding[d] < 0 ? -padding[d] : padding[d]);
+    if (reach > 0x3fffffffLL || stride[d] > 0x3fffffffLL || out_shape[d] > 0x3fffffffLL)
+      return BFB_ERR_TOO_LARGE;  // 32-bit coordinate arithmetic
+    g->out_div[d] = FastDiv((uint32_t)out_shape[d]);
+  }
+  g->vol_div = FastDiv((uint32_t)g->volume);
   return BFB_OK;
 }
 
