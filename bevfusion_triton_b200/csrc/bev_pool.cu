@@ -331,8 +331,11 @@ __global__ void bev_tile_plan_kernel(const int2* __restrict__ cell_se, int64_t t
     cnt = se.y - se.x;
   }
   uint32_t mask = 1u;
+  int tot = cnt;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
   int run = __shfl_sync(0xffffffffu, cnt, 0);
-  for (int l = 1; l < nc; ++l) {
+  for (int l = tot <= kPiecePoints ? nc : 1; l < nc; ++l) {  // a tile that fits is one piece
     const int c = __shfl_sync(0xffffffffu, cnt, l);
     if (run > 0 && run + c > kPiecePoints) {
       mask |= 1u << l;
