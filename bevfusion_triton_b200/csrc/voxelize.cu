@@ -19,10 +19,12 @@
 //                num_points, record the voxel's table slot and member count
 //   vox_fill     bucket every kept point by voxel (slots from a scan of the counts)
 //   vox_rank     a thread per kept point: its slot = number of smaller point indices in
-//                its voxel's bucket (input order); slots below max_points get its row
+//                its voxel's bucket (input order); slots below max_points get its row;
+//                rank 0 frees the table slot
 //   vox_pad      a thread per (voxel, slot): zero the slots past the voxel's points
-//   vox_order    a lane per voxel: reset the table slot; voxels above 4096 points are
-//                ordered and written by a whole warp (repeated minimum)
+//   vox_order    a lane per voxel: voxels above 4096 points are ordered and written by
+//                a whole warp (repeated minimum); dropped voxels free their slot in
+//                vox_assign
 // The table therefore stays clean between calls: it is initialised once
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
@@ -256,6 +258,11 @@ __global__ void vox_assign_kernel(const T* __restrict__ pts, int64_t n, int64_t 
   gcnt[g] = kept ? c : 0u;
   vinfo[g] = make_int2(s, (int)local);
   tb.slots[slot].gvid = kept ? (int32_t)g : -1;
+  if (!kept) {  // dropped by max_voxels: no later kernel visits this slot, free it now
+    tb.slots[slot].key = kEmptyKey;  // (gvid stays -1 for vox_fill)
+    tb.slots[slot].first = kNoFirst;
+    tb.slots[slot].cnt = 0u;
+  }
   if (kept) {
     float xyz[3];
     load_xyz<T>(pts, p, f, xyz);
@@ -311,11 +318,13 @@ constexpr int kRankMax = 4096;  // voxels with more points are ordered by a whol
 // One thread per kept point (bucket slot): its slot within the voxel is the
 // number of smaller point indices in the voxel's bucket, i.e. its rank in
 // input order; points ranked below P copy their features into that slot.
+// The voxel's first point (rank 0) also frees its table slot.
 template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
     const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, const uint32_t* __restrict__ gcnt,
     const uint32_t* __restrict__ cursor, const int2* __restrict__ vinfo, const uint32_t* __restrict__ members,
-    const int32_t* __restrict__ mvox, int64_t P, int64_t max_voxels, T* __restrict__ voxels) {
+    const int32_t* __restrict__ mvox, const int32_t* __restrict__ gslot, TableView tb, int64_t P,
+    int64_t max_voxels, T* __restrict__ voxels) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   // kept points over the batch: the bucket offset one past the last voxel
   // (vox_fill advances only the offsets of voxels that own points)
@@ -327,6 +336,12 @@ __global__ __launch_bounds__(kVoxThreads) void vox_rank_kernel(
   const uint32_t p = members[i];
   uint32_t r = 0;
   for (uint32_t j = start; j < end; ++j) r += __ldg(members + j) < p;
+  if (r == 0) {  // leave the table clean for the next call
+    VoxSlot& sl = tb.slots[gslot[g]];
+    sl.key = kEmptyKey;
+    sl.first = kNoFirst;
+    sl.cnt = 0u;
+  }
   if ((int64_t)r >= P) return;
   const int2 vi = vinfo[g];
   T* dst = voxels + (((int64_t)vi.x * max_voxels + vi.y) * P + r) * f;
@@ -369,9 +384,9 @@ __global__ __launch_bounds__(kVoxThreads) void vox_pad_kernel(const uint32_t* __
   }
 }
 
-// One lane per voxel: reset the voxel's table slot; voxels above kRankMax
-// points are written by the whole warp: first P points by repeated minimum
-// selection (input order), zero padding.
+// One lane per voxel; voxels above kRankMax points are written by the whole
+// warp (first P points by repeated minimum selection, input order; zero
+// padding) and their table slots freed.
 template <class T>
 __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
     const T* __restrict__ pts, int64_t f, const uint32_t* __restrict__ total_dev, TableView tb,
@@ -386,13 +401,15 @@ __global__ __launch_bounds__(kVoxThreads) void vox_order_kernel(
   uint32_t cnt = 0, end = 0;
   int2 vi = make_int2(0, 0);
   if (g < total) {
-    const int32_t slot = gslot[g];
-    tb.slots[slot].key = kEmptyKey;  // leave the table clean for the next call
-    tb.slots[slot].first = kNoFirst;
-    tb.slots[slot].cnt = 0u;
     cnt = gcnt[g];
-    end = cursor[g];
-    vi = vinfo[g];
+    if (cnt > (uint32_t)kRankMax) {  // the rank kernel skipped this voxel
+      const int32_t slot = gslot[g];
+      tb.slots[slot].key = kEmptyKey;  // leave the table clean for the next call
+      tb.slots[slot].first = kNoFirst;
+      tb.slots[slot].cnt = 0u;
+      end = cursor[g];
+      vi = vinfo[g];
+    }
   }
   unsigned big = __ballot_sync(0xffffffffu, cnt > (uint32_t)kRankMax);
   while (big) {
@@ -491,7 +508,7 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
     vox_fill_kernel<<<nb, kVoxThreads, 0, st>>>(sv.slot_of, n, tb.slots, sv.cursor, sv.members, sv.mvox);
     BFB_CHECK_LAUNCH();
     vox_rank_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, f, sv.excl + n, sv.gcnt, sv.cursor, sv.vinfo, sv.members,
-                                                   sv.mvox, P, MV, static_cast<T*>(voxels));
+                                                   sv.mvox, sv.gslot, tb, P, MV, static_cast<T*>(voxels));
     BFB_CHECK_LAUNCH();
     vox_pad_kernel<T><<<148 * 16, kVoxThreads, 0, st>>>(sv.excl + n, sv.gcnt, sv.vinfo, f, FastDiv((uint32_t)P), MV,
                                                         static_cast<T*>(voxels));
