@@ -107,6 +107,7 @@ __device__ __forceinline__ void kernel_offset(int k, const SpGeom& g, int (&kd)[
 
 // 32-bit coordinate arithmetic: coordinates, offsets and output extents are
 // below 2^31 and every flat cell below 2^32 (checked on the host).
+template <int NDIM>
 __global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n, SpGeom g,
                                       uint32_t* __restrict__ cell, uint32_t* __restrict__ flags) {
   const int k = blockIdx.y;
@@ -114,16 +115,18 @@ __global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n
   kernel_offset(k, g, kd);
   int base[kSpMaxDims], st[kSpMaxDims];
   uint32_t out[kSpMaxDims];
-  for (int d = 0; d < g.ndim; ++d) {  // out = (in + base) / st  or  in * st + base
+#pragma unroll
+  for (int d = 0; d < NDIM; ++d) {  // out = (in + base) / st  or  in * st + base
     base[d] = g.transpose ? (int)(kd[d] * g.dil[d] - g.pad[d]) : (int)(g.pad[d] - kd[d] * g.dil[d]);
     st[d] = (int)g.st[d];
     out[d] = (uint32_t)g.out[d];
   }
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t* row = idx + j * (g.ndim + 1);
+    const int32_t* row = idx + j * (NDIM + 1);
     bool ok = true;
     uint32_t f = 0;
-    for (int d = 0; d < g.ndim; ++d) {
+#pragma unroll
+    for (int d = 0; d < NDIM; ++d) {
       const int in = __ldg(row + 1 + d);
       int o;
       if (g.transpose) {
@@ -342,8 +345,14 @@ extern "C" int bfb_get_indice_pairs(const int32_t* indices, int64_t n, int ndim,
   BFB_CUDA(cudaMemsetAsync(num_out_dev, 0, sizeof(int32_t), st));
   if (n == 0) return BFB_OK;
   const unsigned nbc = (unsigned)std::min<int64_t>(ceil_div(c, kSpThreads), 148 * 32);  // grid-stride over t
-  const dim3 grid_kj((unsigned)std::min<int64_t>(ceil_div(n, kSpThreads), 1024), (unsigned)g.K);
-  spc_candidates_kernel<<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags);
+  // each thread walks ~8 sites of one offset (the per-offset setup is amortised)
+  const dim3 grid_kj((unsigned)std::min<int64_t>(ceil_div(n, kSpThreads * 8), 1024), (unsigned)g.K);
+  switch (ndim) {
+    case 1: spc_candidates_kernel<1><<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags); break;
+    case 2: spc_candidates_kernel<2><<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags); break;
+    case 3: spc_candidates_kernel<3><<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags); break;
+    default: spc_candidates_kernel<4><<<grid_kj, kSpThreads, 0, st>>>(indices, n, g, w.cell, w.flags); break;
+  }
   BFB_CHECK_LAUNCH();
   if (subm) {
     BFB_CUDA(cudaMemsetAsync(w.table, 0xff, sizeof(SpSlot) * (size_t)w.cap, st));  // key free, val -1
