@@ -1407,8 +1407,8 @@ __global__ __launch_bounds__(256) void dc_backward_kernel(const float* __restric
           float dot = 0.f;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            dot = __fadd_rn(dot, __fmul_rn(v[u][q], cx[q]));
-            acc[q] = __fadd_rn(acc[q], __fmul_rn(dep, v[u][q]));
+            dot = __fmaf_rn(v[u][q], cx[q], dot);  // gradients: fp32 tolerance, fused multiply-adds
+            acc[q] = __fmaf_rn(dep, v[u][q], acc[q]);
           }
           part[k0 + u] = dot;
         }
