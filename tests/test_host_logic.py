@@ -102,3 +102,38 @@ def test_bev_pool_has_no_cpu_path():
     from bevfusion_triton_b200.ops.bev_pool import bev_pool
     with pytest.raises(RuntimeError, match='CUDA'):
         bev_pool(torch.randn(4, 3), torch.zeros((4, 4), dtype=torch.int32), 1, 1, 1, 1)
+
+
+def test_rulebook_output_shapes_and_checks(cabi):
+    """ops/spconv/ops.py:25-50 output-size helpers, the rulebook's argument
+    errors (before any device work) and the C-ABI workspace query."""
+    from bevfusion_triton_b200.ops.spconv import get_conv_output_size, get_deconv_output_size, get_indice_pairs
+    assert get_conv_output_size([1440, 1440, 41], [3, 3, 3], [2, 2, 2], [1, 1, 1], [1, 1, 1]) == [720, 720, 21]
+    assert get_conv_output_size([8, 8], [-1, 3], [1, 1], [0, 0], [1, 1]) == [1, 6]
+    assert get_deconv_output_size([5, 6], [3, 3], [2, 2], [1, 1], [1, 1], [0, 0]) == [9, 11]
+    with pytest.raises(ValueError):
+        get_deconv_output_size([5], [-1], [1], [0], [1], [0])
+    idx = torch.zeros((3, 4), dtype=torch.int32)
+    with pytest.raises(ValueError):
+        get_indice_pairs(idx, 0, [8, 8, 8])
+    with pytest.raises(RuntimeError, match='CUDA'):
+        get_indice_pairs(idx, 1, [8, 8, 8])
+    ws = ctypes.c_size_t()
+    shape = (ctypes.c_int64 * 3)(720, 720, 21)
+    ks = (ctypes.c_int64 * 3)(3, 3, 3)
+    assert cabi.bfb_indice_pairs_workspace_size(ctypes.c_int64(1000), 3, ctypes.c_int64(8), shape, ks, 0,
+                                                ctypes.byref(ws)) == 0
+    assert ws.value >= 8 * 720 * 720 * 21 // 8  # one bit per output cell
+    big = (ctypes.c_int64 * 3)(1 << 20, 1 << 20, 8)
+    assert cabi.bfb_indice_pairs_workspace_size(ctypes.c_int64(10), 3, ctypes.c_int64(1), big, ks, 0,
+                                                ctypes.byref(ws)) == -4  # cells must fit 32 bits
+
+
+def test_bev_grid_matches_reference_formula():
+    """gen_dx_bx + the lower edge of models/vtransforms/base.py:19-23,138."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_grid
+    lower, dx, nx = bev_grid((-54.0, 54.0, 0.3), (-54.0, 54.0, 0.3), (-10.0, 10.0, 20.0))
+    assert nx == [360, 360, 1]
+    d = torch.tensor([0.3, 0.3, 20.0])
+    b = torch.tensor([-54.0 + 0.15, -54.0 + 0.15, 0.0])
+    assert lower == (b - d / 2.0).tolist() and dx == d.tolist()
