@@ -508,9 +508,6 @@ struct DenseRows {
   }
 };
 
-// Unsigned 32-bit division by a runtime constant with a multiply-high and
-// shifts (round-up magic number, d >= 1).
-
 // The permutation handed to this source holds the PIXEL of each sorted point
 // and `depth` is in sorted order too (both written by dc_stream_kernel), so a
 // row is one context vector times one scalar with no index arithmetic.
