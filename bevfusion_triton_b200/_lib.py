@@ -43,3 +43,16 @@ def load_native():
 def ops():
     load_native()
     return torch.ops.bfb_b200
+
+
+def bev_pool_plan_bytes(n: int, B: int, D: int, H: int, W: int) -> int:
+    """Size in bytes of a bev_pool plan for (n, B, D, H, W): a host-only query
+    of the C ABI (no GPU needed).  Raises ValueError for sizes it refuses."""
+    lib = load_native()
+    plan = ctypes.c_size_t(0)
+    st = lib.bfb_bev_pool_workspace_sizes(ctypes.c_int64(n), ctypes.c_int64(1), ctypes.c_int64(B),
+                                          ctypes.c_int64(D), ctypes.c_int64(H), ctypes.c_int64(W),
+                                          ctypes.byref(plan), None)
+    if st != 0:
+        raise ValueError(f'bev_pool geometry (n={n}, B={B}, D={D}, H={H}, W={W}) is refused (status {st})')
+    return plan.value

@@ -40,17 +40,47 @@ constexpr int kPiecePoints = 2048;
 constexpr int kPoolWarps = 4;
 constexpr int kPoolThreads = kPoolWarps * 32;
 
+// The geometry a plan was built for (points n, grid B, D, H, W).  Every
+// kernel that reads a plan is given the caller's geometry and compares it
+// with the one stamped into the plan header; on a mismatch it writes nothing,
+// reads nothing past the header and raises `mismatch`, because the plan's
+// arrays would otherwise be carved at the wrong offsets.
+struct PlanGeo {
+  uint32_t n, B, D, H, W;
+};
+
 struct PlanHeader {
   uint32_t n_valid;
   uint32_t total_pieces;
   uint32_t n_invalid;
-  uint32_t pad[61];
+  uint32_t mismatch;  // set by a kernel handed a plan of another geometry
+  PlanGeo geo;
+  uint32_t pad[55];
 };
 static_assert(sizeof(PlanHeader) == 256, "header is one aligned block");
+
+// True when the plan was built for `g`.  Otherwise one thread of the grid
+// raises the header's mismatch flag; the caller then returns.
+__device__ __forceinline__ bool plan_matches(const PlanHeader* hdr, const PlanGeo& g) {
+  const PlanGeo h = hdr->geo;
+  const bool ok = h.n == g.n && h.B == g.B && h.D == g.D && h.H == g.H && h.W == g.W;
+  if (!ok && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+    atomicExch(const_cast<uint32_t*>(&hdr->mismatch), 1u);
+  return ok;
+}
+
+// Zeroes a new plan's header and stamps the geometry it is built for.
+__global__ void plan_stamp_kernel(PlanHeader* hdr, PlanGeo g) {
+  uint32_t* w = reinterpret_cast<uint32_t*>(hdr);
+  for (int i = threadIdx.x; i < (int)(sizeof(PlanHeader) / 4); i += blockDim.x) w[i] = 0u;
+  __syncthreads();
+  if (threadIdx.x == 0) hdr->geo = g;
+}
 
 struct Geometry {
   int64_t n, B, D, H, W;
   int64_t dhw, cells, tpb, tiles, max_pieces;
+  PlanGeo geo() const { return PlanGeo{(uint32_t)n, (uint32_t)B, (uint32_t)D, (uint32_t)H, (uint32_t)W}; }
 };
 
 int make_geometry(int64_t n, int64_t B, int64_t D, int64_t H, int64_t W, Geometry* g) {
@@ -567,10 +597,11 @@ template <class T, int VE, int PU, class Src>
 __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
     Src src, int64_t C, int nvec, int64_t dhw, int64_t tpb,
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
-    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ out) {
+    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, PlanGeo geo, T* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_cell[kTileCells], s_beg[kTileCells], s_cnt[kTileCells];
   __shared__ int s_m, s_next;
+  if (!plan_matches(hdr, geo)) return;
   const int e = blockIdx.x;
   if (e >= (int)hdr->total_pieces) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -695,10 +726,11 @@ template <class T, int VE>
 __global__ __launch_bounds__(kPoolThreads) void bev_bwd_kernel(
     const T* __restrict__ gout, int64_t C, int nvec, int64_t dhw, int64_t tpb, int64_t n,
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
-    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, T* __restrict__ gfeat) {
+    const int4* __restrict__ pieces, const PlanHeader* __restrict__ hdr, PlanGeo geo, T* __restrict__ gfeat) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_cell[kTileCells], s_beg[kTileCells], s_cnt[kTileCells];
   __shared__ int s_m, s_next;
+  if (!plan_matches(hdr, geo)) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v0 = blockIdx.y * 32;
   const int nvs = min(32, nvec - v0);
@@ -836,7 +868,9 @@ template <class T, int VE>
 __global__ __launch_bounds__(kPoolThreads) void bev_rows_kernel(const T* __restrict__ gout, int64_t C, int nvec,
                                                                 int64_t dhw, int64_t tpb,
                                                                 const int2* __restrict__ cell_se,
+                                                                const PlanHeader* __restrict__ hdr, PlanGeo geo,
                                                                 T* __restrict__ rows) {
+  if (!plan_matches(hdr, geo)) return;
   const int64_t t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int64_t r0, s0;
@@ -877,8 +911,10 @@ template <class T, int VE>
 __global__ __launch_bounds__(kGatherThreads) void bev_gather_kernel(const T* __restrict__ rows,
                                                                     const uint32_t* __restrict__ pkey,
                                                                     uint32_t sentinel, int64_t n, int nvec,
-                                                                    FastDiv dv, T* __restrict__ gfeat) {
+                                                                    FastDiv dv, const PlanHeader* __restrict__ hdr,
+                                                                    PlanGeo geo, T* __restrict__ gfeat) {
   using V = Vec<T, VE>;
+  if (!plan_matches(hdr, geo)) return;
   const int64_t p0 = (int64_t)blockIdx.x * kGatherPoints;
   const uint32_t np = (uint32_t)min((int64_t)kGatherPoints, n - p0);
   const uint32_t total = np * (uint32_t)nvec;  // channel vectors of this CTA's points
@@ -931,7 +967,7 @@ int launch_fwd_v(const Src& src, int64_t C, const Geometry& g, const PlanView& p
     BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
   bev_fwd_kernel<T, VE, PU, Src><<<grid, kPoolThreads, smem, st>>>(
-      src, C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
+      src, C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr, g.geo(),
       static_cast<T*>(out));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
@@ -958,7 +994,7 @@ int launch_bwd(const void* gout, int64_t C, const Geometry& g, const PlanView& p
   dim3 grid((unsigned)(g.max_pieces + ceil_div(g.n, kPiecePoints)), (unsigned)slices);
   bev_bwd_kernel<T, VE><<<grid, kPoolThreads, smem, st>>>(
       static_cast<const T*>(gout), C, nvec, g.dhw, g.tpb, g.n, pv.perm, pv.cell_se, pv.pieces, pv.hdr,
-      static_cast<T*>(gfeat));
+      g.geo(), static_cast<T*>(gfeat));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
@@ -968,11 +1004,11 @@ int launch_bwd_gather(const void* gout, int64_t C, const Geometry& g, const Plan
                       void* gfeat, cudaStream_t st) {
   const int nvec = (int)(C / VE);
   bev_rows_kernel<T, VE><<<(unsigned)g.tiles, kPoolThreads, 0, st>>>(
-      static_cast<const T*>(gout), C, nvec, g.dhw, g.tpb, pv.cell_se, static_cast<T*>(rows));
+      static_cast<const T*>(gout), C, nvec, g.dhw, g.tpb, pv.cell_se, pv.hdr, g.geo(), static_cast<T*>(rows));
   BFB_CHECK_LAUNCH();
   bev_gather_kernel<T, VE><<<(unsigned)ceil_div(g.n, kGatherPoints), kGatherThreads, 0, st>>>(
       static_cast<const T*>(rows), pv.pkey, (uint32_t)g.cells, g.n, nvec, FastDiv((uint32_t)nvec),
-      static_cast<T*>(gfeat));
+      pv.hdr, g.geo(), static_cast<T*>(gfeat));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
@@ -1093,7 +1129,8 @@ extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64
   cudaStream_t st = as_stream(stream);
   const RadixPlan rp = make_radix_plan((uint32_t)g.cells);
 
-  BFB_CUDA(cudaMemsetAsync(pv.hdr, 0, sizeof(PlanHeader), st));
+  plan_stamp_kernel<<<1, 64, 0, st>>>(pv.hdr, g.geo());
+  BFB_CHECK_LAUNCH();
   if (n > 0) {
     const int64_t ntiles = radix_tiles(n);
     const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
@@ -1137,7 +1174,8 @@ extern "C" int bfb_bev_pool_geometry_plan(const float* frustum, int64_t nd, int6
   CameraCells cc{frustum, post_rots, post_trans, combine, trans, extra_rots, extra_trans,
                  FastDiv((uint32_t)fpts), FastDiv((uint32_t)ncam), {lower[0], lower[1], lower[2]},
                  {dx[0], dx[1], dx[2]}, D, H, W};
-  BFB_CUDA(cudaMemsetAsync(pv.hdr, 0, sizeof(PlanHeader), st));
+  plan_stamp_kernel<<<1, 64, 0, st>>>(pv.hdr, g.geo());
+  BFB_CHECK_LAUNCH();
   const int64_t ntiles = radix_tiles(n);
   const size_t hsm = sizeof(uint32_t) * skewed_size(1 << rp.digit_bits[0]);
   bev_keys_kernel<<<(unsigned)ntiles, kRadixThreads, hsm, st>>>(cc, n, (uint32_t)g.cells, sv.keys0, pv.pkey,
@@ -1222,7 +1260,8 @@ extern "C" int bfb_bev_pool_backward_gather(const void* gout, int dtype, int64_t
 
 // cells[p] = cell rank of point p in the plan, -1 when it was dropped
 __global__ void plan_cells_kernel(const uint32_t* __restrict__ pkey, int64_t n, uint32_t sentinel,
-                                  int64_t* __restrict__ cells) {
+                                  const PlanHeader* __restrict__ hdr, PlanGeo geo, int64_t* __restrict__ cells) {
+  if (!plan_matches(hdr, geo)) return;
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= n) return;
   const uint32_t k = pkey[p];
@@ -1239,7 +1278,8 @@ extern "C" int bfb_bev_pool_plan_cells(const void* plan, size_t plan_bytes, int6
   if (carve_plan(nullptr, g, &pv) > plan_bytes) return BFB_ERR_WORKSPACE;
   carve_plan(const_cast<void*>(plan), g, &pv);
   if (n == 0) return BFB_OK;
-  plan_cells_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, as_stream(stream)>>>(pv.pkey, n, (uint32_t)g.cells, cells);
+  plan_cells_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, as_stream(stream)>>>(pv.pkey, n, (uint32_t)g.cells, pv.hdr,
+                                                                                     g.geo(), cells);
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
@@ -1253,6 +1293,21 @@ extern "C" int bfb_bev_pool_invalid_count(const void* plan, int64_t* count, void
   BFB_CUDA(cudaStreamSynchronize(st));
   *count = v;
   return BFB_OK;
+}
+
+extern "C" int bfb_bev_pool_plan_check(const void* plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W,
+                                       void* stream) {
+  if (!plan) return BFB_ERR_INVALID_ARG;
+  Geometry g;
+  BFB_TRY(make_geometry(n, B, D, H, W, &g));
+  PlanHeader h;
+  cudaStream_t st = as_stream(stream);
+  BFB_CUDA(cudaMemcpyAsync(&h, plan, sizeof(h), cudaMemcpyDeviceToHost, st));
+  BFB_CUDA(cudaStreamSynchronize(st));
+  const PlanGeo want = g.geo();
+  const bool same = h.geo.n == want.n && h.geo.B == want.B && h.geo.D == want.D && h.geo.H == want.H &&
+                    h.geo.W == want.W;
+  return (same && h.mismatch == 0u) ? BFB_OK : BFB_ERR_PLAN_MISMATCH;
 }
 
 // ---------------------------------------------------------------------------
@@ -1346,7 +1401,9 @@ struct DcDims {
 
 // Sorted-order stream of the fused forward: pixel and depth of every sorted point.
 __global__ void dc_stream_kernel(const uint32_t* __restrict__ perm, int64_t n, const float* __restrict__ depth,
-                                 FastDiv dhw, FastDiv hw, uint32_t* __restrict__ pix, float* __restrict__ dep) {
+                                 FastDiv dhw, FastDiv hw, const PlanHeader* __restrict__ hdr, PlanGeo geo,
+                                 uint32_t* __restrict__ pix, float* __restrict__ dep) {
+  if (!plan_matches(hdr, geo)) return;
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= n) return;
   const uint32_t pid = perm[p];
@@ -1500,7 +1557,8 @@ extern "C" int bfb_bev_pool_dc_forward_planned(const float* depth, const float* 
   if (sc.bytes() > scratch_bytes) return BFB_ERR_WORKSPACE;
   dc_stream_kernel<<<(unsigned)ceil_div(dm.n(), 256), 256, 0, st>>>(pv.perm, dm.n(), depth,
                                                                    FastDiv((uint32_t)(nd * dm.hw)),
-                                                                   FastDiv((uint32_t)dm.hw), spix, sdep);
+                                                                   FastDiv((uint32_t)dm.hw), pv.hdr, g.geo(), spix,
+                                                                   sdep);
   BFB_CHECK_LAUNCH();
   PlanView sv = pv;
   sv.perm = spix;

@@ -31,6 +31,7 @@ extern "C" const char* bfb_status_string(int status) {
     case BFB_ERR_TOO_LARGE: return "sizes exceed the 32-bit index space";
     case BFB_ERR_CUDA: return "CUDA error";
     case BFB_ERR_DEVICE_STATUS: return "device-side check failed";
+    case BFB_ERR_PLAN_MISMATCH: return "bev_pool plan was built for another geometry";
     default: return "unknown status";
   }
 }

@@ -46,6 +46,20 @@ void require_cuda(const at::Tensor& t, const char* name) {
 }
 
 // ---------------------------------------------------------------- bev_pool
+// A plan tensor is allocated at exactly the size its geometry needs, so a plan
+// handed in with other (n, B, D, H, W) is refused here when its size differs;
+// the kernels compare the geometry stamped in the plan as well and write
+// nothing on a mismatch.
+void check_plan(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
+  require_cuda(plan, "plan");
+  TORCH_CHECK_VALUE(plan.scalar_type() == at::kByte && plan.dim() == 1 && plan.is_contiguous(),
+                    "plan must be the uint8 tensor returned by a bev_pool plan call");
+  size_t plan_b = 0;
+  check(bfb_bev_pool_workspace_sizes(n, 1, B, D, H, W, &plan_b, nullptr), "bev_pool workspace query");
+  TORCH_CHECK_VALUE((size_t)plan.numel() == plan_b, "bev_pool plan was built for another geometry: it holds ",
+                    plan.numel(), " bytes, (n=", n, ", B=", B, ", D=", D, ", H=", H, ", W=", W, ") needs ", plan_b);
+}
+
 std::tuple<at::Tensor, at::Tensor> bev_pool_forward(const at::Tensor& feats_in, const at::Tensor& coords_in,
                                                      int64_t B, int64_t D, int64_t H, int64_t W) {
   require_cuda(feats_in, "feats");
@@ -92,6 +106,7 @@ at::Tensor bev_pool_forward_planned(const at::Tensor& feats_in, const at::Tensor
   c10::cuda::CUDAGuard guard(feats_in.device());
   auto feats = feats_in.contiguous();
   const int64_t n = feats.size(0), c = feats.size(1);
+  check_plan(plan, n, B, D, H, W);
   auto out = at::empty({B, c, D, H, W}, feats.options());
   check(bfb_bev_pool_forward_planned(feats.data_ptr(), dtype_code(feats), n, c, B, D, H, W, plan.data_ptr(),
                                      (size_t)plan.numel(), out.data_ptr(), stream_of(feats)),
@@ -107,6 +122,7 @@ at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, 
   TORCH_CHECK(grad.dim() == 5 && grad.size(0) == B && grad.size(2) == D && grad.size(3) == H && grad.size(4) == W,
               "grad_out must have shape [B, C, D, H, W]");
   const int64_t c = grad.size(1);
+  check_plan(plan, n, B, D, H, W);
   auto gfeat = at::empty({n, c}, grad.options());
   // Gather form when its row buffer (one row per grid cell) is no larger than
   // grad_feats itself; the scatter form needs no buffer.
@@ -130,11 +146,21 @@ at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, 
 at::Tensor bev_pool_plan_cells(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
   require_cuda(plan, "plan");
   c10::cuda::CUDAGuard guard(plan.device());
+  check_plan(plan, n, B, D, H, W);
   auto cells = at::empty({n}, plan.options().dtype(at::kLong));
   check(bfb_bev_pool_plan_cells(plan.data_ptr(), (size_t)plan.numel(), n, B, D, H, W, cells.data_ptr<int64_t>(),
                                 stream_of(plan)),
         "bev_pool plan cells");
   return cells;
+}
+
+bool bev_pool_plan_check(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
+  require_cuda(plan, "plan");
+  c10::cuda::CUDAGuard guard(plan.device());
+  const int s = bfb_bev_pool_plan_check(plan.data_ptr(), n, B, D, H, W, stream_of(plan));
+  if (s == BFB_ERR_PLAN_MISMATCH) return false;
+  check(s, "bev_pool plan check");
+  return true;
 }
 
 int64_t bev_pool_invalid_count(const at::Tensor& plan) {
@@ -192,6 +218,7 @@ std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward_planned(const at::Tensor&
   auto ctx = ctx_in.contiguous();
   const int64_t cams = depth.size(0), nd = depth.size(1), fh = depth.size(2), fw = depth.size(3), c = ctx.size(1);
   TORCH_CHECK_VALUE(ctx.size(0) == cams && ctx.size(2) == fh && ctx.size(3) == fw, "context does not match depth");
+  check_plan(plan, cams * nd * fh * fw, B, D, H, W);
   size_t plan_b = 0, scr_b = 0, aux_b = 0;
   check(bfb_bev_pool_dc_workspace_sizes(cams, nd, fh, fw, c, B, D, H, W, &plan_b, &scr_b, &aux_b, nullptr),
         "bev_pool_dc workspace query");
@@ -495,6 +522,7 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward_planned(Tensor feats, Tensor plan, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_backward(Tensor grad_out, Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_invalid_count(Tensor plan) -> int");
+  m.def("bev_pool_plan_check(Tensor plan, int n, int B, int D, int H, int W) -> bool");
   m.def("bev_pool_plan_cells(Tensor plan, int n, int B, int D, int H, int W) -> Tensor");
   m.def("bev_pool_dc_forward(Tensor depth, Tensor context, Tensor coords, int B, int D, int H, int W) -> (Tensor, Tensor)");
   m.def("bev_pool_dc_forward_planned(Tensor depth, Tensor context, Tensor plan, int B, int D, int H, int W) -> (Tensor, Tensor)");
@@ -527,6 +555,7 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("bev_pool_forward_planned", &bev_pool_forward_planned);
   m.impl("bev_pool_backward", &bev_pool_backward);
   m.impl("bev_pool_invalid_count", &bev_pool_invalid_count);
+  m.impl("bev_pool_plan_check", &bev_pool_plan_check);
   m.impl("bev_pool_plan_cells", &bev_pool_plan_cells);
   m.impl("bev_pool_dc_forward", &bev_pool_dc_forward);
   m.impl("bev_pool_dc_forward_planned", &bev_pool_dc_forward_planned);

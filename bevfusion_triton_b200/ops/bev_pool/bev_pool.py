@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import torch
 
-from ..._lib import ops
+from ..._lib import bev_pool_plan_bytes, ops
 
 
 def _check_inputs(feats: torch.Tensor, coords: torch.Tensor, B: int, D: int, H: int, W: int) -> None:
@@ -96,12 +96,34 @@ def bev_pool_plan(coords: torch.Tensor, B: int, D: int, H: int, W: int) -> torch
     return ops().bev_pool_plan(coords, B, D, H, W)
 
 
+def check_plan(plan: torch.Tensor, n: int, B: int, D: int, H: int, W: int) -> None:
+    """Raise ValueError unless ``plan`` has the size of a plan for (n, B, D, H,
+    W).  A plan reused for another point count or grid (a fixed-rig plan
+    handed a short last batch, say) would carve its arrays at the wrong
+    offsets; the kernels also compare the geometry stamped in the plan and
+    write nothing on a mismatch (``plan_matches`` below reads that back)."""
+    if plan.dtype != torch.uint8 or plan.dim() != 1:
+        raise ValueError('plan must be the uint8 tensor returned by bev_pool_plan / bev_pool_geometry_plan.')
+    need = bev_pool_plan_bytes(int(n), int(B), int(D), int(H), int(W))
+    if plan.numel() != need:
+        raise ValueError(f'bev_pool plan was built for another geometry: it holds {plan.numel()} bytes, '
+                         f'(n={n}, B={B}, D={D}, H={H}, W={W}) needs {need}.')
+
+
+def plan_matches(plan: torch.Tensor, n: int, B: int, D: int, H: int, W: int) -> bool:
+    """True when ``plan`` was built for (n, B, D, H, W) and no call has been
+    handed it with another geometry since (reads the plan header: synchronises
+    the stream)."""
+    return bool(ops().bev_pool_plan_check(plan, int(n), int(B), int(D), int(H), int(W)))
+
+
 def bev_pool_planned(feats: torch.Tensor, plan: torch.Tensor, B: int, D: int, H: int, W: int) -> torch.Tensor:
     """``bev_pool`` with a plan from ``bev_pool_plan`` (same coords, same N)."""
     if feats.dim() != 2:
         raise ValueError('feats must have shape [N, C].')
     if feats.dtype not in (torch.float16, torch.float32, torch.bfloat16):
         raise TypeError('feats must have dtype torch.float16, torch.float32, or torch.bfloat16.')
+    check_plan(plan, feats.size(0), B, D, H, W)
     _require_cuda(feats, plan)
     return _BevPoolPlannedFunction.apply(feats, plan, int(B), int(D), int(H), int(W))
 
@@ -167,6 +189,8 @@ def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: t
         raise TypeError('depth and context must have dtype torch.float32.')
     if min(B, D, H, W) <= 0:
         raise ValueError('B, D, H, W must be positive integers.')
+    if plan is not None:
+        check_plan(plan, depth.size(0) * depth.size(1) * depth.size(2) * depth.size(3), B, D, H, W)
     _require_cuda(depth, context, *((coords,) if plan is None else (plan,)))
     return _BevPoolDepthContextFunction.apply(depth, context, coords, plan, int(B), int(D), int(H), int(W))
 

@@ -49,6 +49,7 @@ typedef enum bfb_status {
   BFB_ERR_TOO_LARGE = -4,         /* sizes exceed the 32-bit index space */
   BFB_ERR_CUDA = -5,              /* a CUDA runtime call or launch failed */
   BFB_ERR_DEVICE_STATUS = -6,     /* device-side check failed (see op doc) */
+  BFB_ERR_PLAN_MISMATCH = -7,     /* a bev_pool plan used with another geometry */
 } bfb_status;
 
 /* Library ABI version (BFB_ABI_VERSION of the build). */
@@ -84,6 +85,12 @@ uint64_t bfb_kernel_launches(void);
  * bfb_bev_pool_forward_planned and bfb_bev_pool_backward, so keep it alive
  * between the forward and the backward.  `scratch_dev` is only used during
  * the call.
+ *
+ * A plan records the geometry (n, B, D, H, W) it was built for.  Every call
+ * that reads a plan compares it with its own arguments on the device: on a
+ * mismatch the call's kernels write no output and read nothing past the plan
+ * header, and they raise a flag in the header.  bfb_bev_pool_plan_check
+ * reads that state (synchronously) and returns BFB_ERR_PLAN_MISMATCH.
  * ---------------------------------------------------------------------- */
 int bfb_bev_pool_workspace_sizes(int64_t n, int64_t c, int64_t B, int64_t D, int64_t H,
                                  int64_t W, size_t* plan_bytes, size_t* scratch_bytes);
@@ -210,6 +217,13 @@ int bfb_bev_pool_forward_noalloc(const void* feats_dev, int feats_dtype, const v
                                  int coords_itype, int64_t n, int64_t c, int64_t B, int64_t D,
                                  int64_t H, int64_t W, void* out_dev, void* stream);
 size_t bfb_bev_pool_noalloc_capacity(void);
+
+/* Synchronously checks that `plan_dev` was built for (n, B, D, H, W) and that
+ * no call has been handed it with another geometry since: BFB_OK, or
+ * BFB_ERR_PLAN_MISMATCH.  No reference counterpart (the reference keeps no
+ * plan between calls). */
+int bfb_bev_pool_plan_check(const void* plan_dev, int64_t n, int64_t B, int64_t D, int64_t H,
+                            int64_t W, void* stream);
 
 /* Synchronously reads how many points the plan dropped as out of range. */
 int bfb_bev_pool_invalid_count(const void* plan_dev, int64_t* count, void* stream);

@@ -173,6 +173,36 @@ def test_cabi_direct_call(cuda):
     assert rc == -3
 
 
+def test_plan_of_another_geometry_writes_nothing(cuda):
+    """A plan built for 10000 points / B=2, handed (through the C ABI, with a
+    buffer size that passes the size check) to a forward of 5000 points /
+    B=1: the kernels compare the stamped geometry, write no output, and the
+    plan check reports the mismatch.  The torch layer refuses it outright."""
+    from bevfusion_triton_b200 import load_native
+    from bevfusion_triton_b200.ops.bev_pool import plan_matches
+    L = load_native()
+    i64 = ctypes.c_int64
+    feats, coords = rand_bev_case(10000, 8, 2, 1, 16, 16, seed=11)
+    feats, coords = feats.cuda(), coords.cuda()
+    plan = bev_pool_plan(coords, 2, 1, 16, 16)
+    assert plan_matches(plan, 10000, 2, 1, 16, 16)
+    short = feats[:5000].contiguous()
+    out = torch.full((1, 8, 1, 16, 16), 7.0, device='cuda')
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = L.bfb_bev_pool_forward_planned(ctypes.c_void_p(short.data_ptr()), 0, i64(5000), i64(8), i64(1), i64(1),
+                                        i64(16), i64(16), ctypes.c_void_p(plan.data_ptr()),
+                                        ctypes.c_size_t(plan.numel()), ctypes.c_void_p(out.data_ptr()), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.all(out == 7.0)
+    rc = L.bfb_bev_pool_plan_check(ctypes.c_void_p(plan.data_ptr()), i64(5000), i64(1), i64(1), i64(16), i64(16),
+                                   stream)
+    assert rc == -7
+    assert not plan_matches(plan, 10000, 2, 1, 16, 16)  # the flag stays raised
+    with pytest.raises(ValueError, match='another geometry'):
+        bev_pool_planned(short, bev_pool_plan(coords, 2, 1, 16, 16), 1, 1, 16, 16)
+
+
 def test_seg_batch4_fwd_bwd_vs_oracle(cuda):
     """Config 4: segmentation grid 256 x 256, batch 4, fp32, forward + backward."""
     case = synth.seg_bev_pool_case(4, device='cuda')

@@ -137,3 +137,25 @@ def test_bev_grid_matches_reference_formula():
     d = torch.tensor([0.3, 0.3, 20.0])
     b = torch.tensor([-54.0 + 0.15, -54.0 + 0.15, 0.0])
     assert lower == (b - d / 2.0).tolist() and dx == d.tolist()
+
+
+def test_plan_of_another_geometry_is_refused():
+    """A plan kept for a fixed rig and handed a short last batch (fewer points,
+    smaller B) must be refused before any device work."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool_planned, check_plan
+    from bevfusion_triton_b200._lib import bev_pool_plan_bytes
+    full = bev_pool_plan_bytes(200_000, 8, 1, 64, 64)
+    plan = torch.zeros(full, dtype=torch.uint8)
+    check_plan(plan, 200_000, 8, 1, 64, 64)  # its own geometry passes
+    with pytest.raises(ValueError, match='another geometry'):
+        check_plan(plan, 100_000, 4, 1, 64, 64)
+    feats = torch.zeros(100_000, 8)
+    with pytest.raises(ValueError, match='another geometry'):
+        bev_pool_planned(feats, plan, 4, 1, 64, 64)
+    with pytest.raises(ValueError, match='uint8'):
+        check_plan(plan.view(torch.int32), 200_000, 8, 1, 64, 64)
+
+
+def test_plan_mismatch_status_string(cabi):
+    cabi.bfb_status_string.restype = ctypes.c_char_p
+    assert b'another geometry' in cabi.bfb_status_string(-7)
