@@ -36,7 +36,8 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from bevfusion_triton_b200 import shard, synth  # noqa: E402
+from bevfusion_triton_b200 import shard  # noqa: E402
+from tests import synth  # noqa: E402
 
 METRIC = 'bev_pool fwd+bwd & voxelize ms/sample and GB/s (% of B200 HBM peak), 1/2/4/8 GPU'
 UNIT = 'ms/sample'
@@ -44,11 +45,11 @@ SAMPLES_PER_GPU = 8
 C = synth.CHANNELS
 FALLBACK_HBM_GBS = 6650.0
 
-# DRAM traffic (read + write bytes) of the dominant kernels per point, from the
-# ncu capture of a one-sample launch summarised in profiles/; traffic grows in
-# proportion to the points, so a launch's traffic is this times its points.
+# DRAM traffic (read + write bytes) of the dominant kernels per point, from an
+# ncu capture of a one-sample launch; traffic grows in proportion to the
+# points, so a launch's traffic is this times its points.
 NCU_TRAFFIC_PER_POINT = {
-    'bev_fwd_kernel': 340.6,  # profiles/bev_fwd_bwd_kernels_det1.md
+    'bev_fwd_kernel': 340.6,
     # backward: bev_rows_kernel (37.3 MB) + bev_gather_kernel (533.7 MB) of one sample
     'bev_rows_kernel+bev_gather_kernel': 322.4,
 }
@@ -304,6 +305,8 @@ def run_ours(args, ws, rank, local):
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
     if not args.no_rulebook:
         line['sparse_rulebook'] = run_rulebook(args, wl, ws)
+    if not args.no_triton:
+        line['triton_reference'] = run_triton_reference(args, wl, ws)
     if not args.no_fused:
         del wl
         torch.cuda.empty_cache()
@@ -406,6 +409,68 @@ def run_e2e(args, wl, ws, samples_total):
     return {'value': round(ms / samples_total, 4), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
             'd2h_bytes_per_step': d2h, 'steps': steps, 'ms_per_step': round(ms, 3),
             'pipeline': 'per sample over 3 streams (H2D / compute / D2H), consecutive steps overlap', 'voxel_counts_match_device_step': ok}
+
+
+def run_triton_reference(args, wl, ws):
+    """The reference's own Triton GPU path (installed unmodified under
+    baseline/_ref) on the rank's device-resident workload, beside this
+    library through the same public calls: bev_pool forward + backward
+    through autograd over the det batch, and hard_voxelize sample by sample
+    (the reference API takes one cloud per call).  CUDA events, same warm-up
+    rule; ms per sample."""
+    sys.path.insert(0, str(ROOT / 'baseline'))
+    import ref_triton
+    why = ref_triton.available()
+    if why:
+        return {'unavailable': why}
+    rbev, rvox, _ = ref_triton.load()
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool
+    from bevfusion_triton_b200.ops.voxel.voxel_layer import hard_voxelize
+    B, D, H, W = wl.shape
+    S = wl.S
+    F = wl.points.size(1)
+    clouds = [wl.points[a:b] for a, b in zip(wl.offs, wl.offs[1:])]
+    vox = torch.empty((wl.mv, wl.mp, F), device=wl.points.device)
+    vco = torch.empty((wl.mv, 3), dtype=torch.int32, device=wl.points.device)
+    vnm = torch.empty((wl.mv,), dtype=torch.int32, device=wl.points.device)
+
+    def bev(fn):
+        def run():
+            x = wl.feats.detach().requires_grad_(True)
+            fn(x, wl.coords, B, D, H, W).backward(wl.up)
+        return run
+
+    def voxelize(fn):
+        def run():
+            for c in clouds:
+                fn(c, vox, vco, vnm, wl.vsize, wl.crange, wl.mp, wl.mv, 3, True)
+        return run
+
+    def timed(fn, k):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(ws)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        return max_over_ranks(s0.elapsed_time(s1), ws) / k / S
+
+    k = max(3, min(args.steps, 10))
+    res = {}
+    for name, pair in (('bev_pool_fwd_bwd', (bev(bev_pool), bev(rbev.bev_pool))),
+                       ('hard_voxelize', (voxelize(hard_voxelize), voxelize(rvox.hard_voxelize)))):
+        ours, ref = timed(pair[0], k), timed(pair[1], k)
+        res[name] = {'ours_ms_per_sample': round(ours, 4), 'triton_ms_per_sample': round(ref, 4),
+                     'speedup': round(ref / ours, 2)}
+    res['note'] = ('reference Triton kernels (bev_pool_triton.py, voxelization_triton.py, unmodified) vs this '
+                   'library, both through their public Python calls on the same device-resident inputs; '
+                   'bev_pool over the det batch with autograd, hard_voxelize one cloud per call (deterministic)')
+    return res
 
 
 def run_rulebook(args, wl, ws):
@@ -591,6 +656,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-fused', action='store_true')
     ap.add_argument('--no-rulebook', action='store_true')
+    ap.add_argument('--no-triton', action='store_true', help='skip timing the reference Triton GPU path')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3  # timing rule: at least 3 warm-up steps

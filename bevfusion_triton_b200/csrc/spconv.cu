@@ -42,6 +42,7 @@ struct SpGeom {
   int64_t ks[kSpMaxDims], st[kSpMaxDims], pad[kSpMaxDims], dil[kSpMaxDims], out[kSpMaxDims];
   int64_t volume;  // product of out[]
   int64_t K;       // product of ks[]
+  int64_t batch;   // rows with a batch column outside [0, batch) are ignored
   bool transpose;
   FastDiv vol_div, out_div[kSpMaxDims];  // flat cells fit 32 bits
 };
@@ -123,7 +124,7 @@ __global__ void spc_candidates_kernel(const int32_t* __restrict__ idx, int64_t n
   }
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
     const int32_t* row = idx + j * (NDIM + 1);
-    bool ok = true;
+    bool ok = (uint32_t)__ldg(row) < (uint32_t)g.batch;  // a bad batch index would address past the bitmap
     uint32_t f = 0;
 #pragma unroll
     for (int d = 0; d < NDIM; ++d) {
@@ -154,7 +155,11 @@ __global__ void spc_insert_inputs_kernel(const int32_t* __restrict__ idx, int64_
                                          uint64_t cap) {
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
-  const int64_t s = sp_insert(tb, cap, flat_of(idx + j * (g.ndim + 1), g));
+  const int32_t* row = idx + j * (g.ndim + 1);
+  bool ok = (uint32_t)row[0] < (uint32_t)g.batch;
+  for (int d = 0; d < g.ndim; ++d) ok = ok && (uint32_t)row[1 + d] < (uint32_t)g.out[d];
+  if (!ok) return;  // a site outside the grid can be nobody's neighbour
+  const int64_t s = sp_insert(tb, cap, flat_of(row, g));
   if (s >= 0) atomicMax(&tb[s].val, (int32_t)j);
 }
 
@@ -286,6 +291,7 @@ int make_sp_geom(int ndim, int64_t batch, const int64_t* out_shape, const int64_
   if (ndim < 1 || ndim > kSpMaxDims || batch < 1) return BFB_ERR_INVALID_ARG;
   if (!out_shape || !ksize || !stride || !padding || !dilation) return BFB_ERR_INVALID_ARG;
   g->ndim = ndim;
+  g->batch = batch;
   g->transpose = transpose != 0;
   g->volume = 1;
   g->K = 1;

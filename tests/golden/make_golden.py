@@ -37,7 +37,7 @@ ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 sys.dont_write_bytecode = True
 
-from bevfusion_triton_b200 import synth  # noqa: E402
+from tests import synth  # noqa: E402
 
 
 def import_reference(ref: Path):

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from bevfusion_triton_b200.ops.bev_pool import bev_pool, bev_pool_depth_context
 from oracle import oracle
 

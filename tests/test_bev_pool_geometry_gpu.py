@@ -13,7 +13,7 @@ downstream of the cells is compared bit for bit.
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from bevfusion_triton_b200.ops.bev_pool import (bev_grid, bev_pool, bev_pool_depth_context, bev_pool_geometry_plan,
                                                 bev_pool_planned)
 from bevfusion_triton_b200.ops.bev_pool.bev_pool import invalid_count, plan_cells

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from bevfusion_triton_b200.ops.bev_pool import bev_pool, bev_pool_plan, bev_pool_planned
 from bevfusion_triton_b200.ops.bev_pool.bev_pool import invalid_count
 from oracle import oracle

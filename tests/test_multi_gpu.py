@@ -25,7 +25,7 @@ def _free_port():
 def _shard_outputs(first, count, device):
     """bev_pool fwd + bwd of det samples [first, first + count) and hard
     voxelisation of LiDAR samples of the same ids, on `device`."""
-    from bevfusion_triton_b200 import synth
+    from tests import synth
     from bevfusion_triton_b200.ops.bev_pool import bev_pool
     from bevfusion_triton_b200.ops.voxel.voxel_layer import hard_voxelize_batch
     case = synth.det_bev_pool_case(count, device=device, sample_offset=first)

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from oracle import oracle
 from tests._util import sha
 

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from bevfusion_triton_b200.ops.spconv import get_conv_output_size, get_indice_pairs
 from bevfusion_triton_b200.ops.voxel.voxel_layer import hard_voxelize_batch
 from oracle import oracle
@@ -82,3 +82,28 @@ def test_edge_cases(cuda):
     # a site whose every neighbour is outside the grid: corner, 1x1x1 output
     o, pr, nm = get_indice_pairs(idx[:1], 1, [2, 2, 2], ksize=2, stride=2)
     assert o.tolist() == [[0, 0, 0, 0]] and int(nm.sum()) == 1
+
+
+@pytest.mark.parametrize('subm', [False, True])
+def test_out_of_range_batch_rows_are_ignored_by_the_c_abi(cuda, subm):
+    """The C entry point is memory-safe on its own: rows whose batch column is
+    outside [0, batch) (which the Python wrapper refuses) reach no output cell
+    and pair with nothing, instead of addressing past the output bitmap."""
+    from bevfusion_triton_b200._lib import ops
+    good = lidar_voxel_indices(2)[:20000].contiguous()
+    bad = good[:4].clone()
+    bad[:, 0] = torch.tensor([2, 7, -1, 1 << 30], dtype=torch.int32)
+    mixed = torch.cat([good, bad]).contiguous()
+    shape, ks, st, pd = SPARSE_SHAPE, [3, 3, 3], [1, 1, 1] if subm else [2, 2, 2], [1, 1, 1]
+    outs = SPARSE_SHAPE if subm else get_conv_output_size(SPARSE_SHAPE, ks, st, pd, [1, 1, 1])
+    a = ops().get_indice_pairs(good, 2, outs, ks, st, pd, [1, 1, 1], subm, False)
+    b = ops().get_indice_pairs(mixed, 2, outs, ks, st, pd, [1, 1, 1], subm, False)
+    assert torch.equal(a[2], b[2])
+    if not subm:
+        assert torch.equal(a[0], b[0])
+    n = good.size(0)
+    for k in range(27):
+        m = int(a[2][k])
+        assert torch.equal(a[1][k, :, :m], b[1][k, :, :m])
+        assert bool((b[1][k, :, m:] == -1).all())
+    assert int(b[2].sum()) == int(a[2].sum()) and int((b[1][:, 0] >= n).sum()) == 0

@@ -1,0 +1,205 @@
+"""Parity against the reference's own Triton GPU path, run on the same B200.
+
+The reference's Triton kernels (installed unmodified under baseline/_ref by
+baseline/ref_triton.py) are the GPU-side oracle:
+
+* ``bev_pool`` (ops/bev_pool/src/bev_pool_triton.py:219-227): its forward is
+  one ``tl.atomic_add`` per element, so fp32 sums come in a run-dependent
+  order; ours must agree within rtol = atol = 1e-5.  fp16 features: the
+  Triton atomics accumulate in fp16 while ours sums in fp32 and rounds once,
+  so both are held to 1e-2 of an fp64 sum and ours must be the closer one.
+  The backward is a gather in both, compared exactly.
+* ``hard_voxelize`` (ops/voxel/src/voxelization_triton.py:674-710,
+  deterministic mode): voxel_num, coords and counts exact.  The Triton path
+  fills a voxel's slots with ``tl.atomic_add`` (:295), so the order of the
+  points inside a voxel, and which points survive in a voxel that overflows
+  ``max_points``, vary run to run: voxels that do not overflow are compared
+  as sets of rows, overflowing ones by membership of every stored row.
+* ``dynamic_voxelize`` (:428-463): the Triton kernel leaves columns of an
+  out-of-range row untouched, so valid rows are compared exactly and invalid
+  rows by their first column (-1).
+* dynamic scatter (ops/voxel/src/scatter_points_triton.py:253-424): coords,
+  map and counts exact; max exact; sum / mean (atomics) within 1e-5; the
+  backward exactly.
+
+The reference Triton ``bev_pool`` has no bounds check (an out-of-grid
+coordinate makes it write outside its output), so only in-grid coordinates
+are given to it.
+"""
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from bevfusion_triton_b200.ops.bev_pool import bev_pool
+from bevfusion_triton_b200.ops.voxel.voxel_layer import (dynamic_point_to_voxel_backward,
+                                                         dynamic_point_to_voxel_forward, dynamic_voxelize,
+                                                         hard_voxelize)
+from tests import synth
+from tests._util import rand_bev_case
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent / 'baseline'))
+import ref_triton  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+@pytest.fixture(scope='module')
+def ref(cuda):
+    why = ref_triton.available()
+    if why:
+        pytest.skip(why)
+    return ref_triton.load()
+
+
+def _fwd_bwd(fn, feats, coords, shape, up):
+    x = feats.clone().requires_grad_(True)
+    out = fn(x, coords, *shape)
+    (out * up).sum().backward()
+    torch.cuda.synchronize()
+    return out.detach(), x.grad
+
+
+@pytest.mark.parametrize('cdtype', [torch.int32, torch.int64])
+def test_bev_pool_random_vs_triton(ref, cdtype):
+    bev, _, _ = ref
+    feats, coords = rand_bev_case(200_000, 80, 2, 2, 64, 64, seed=21, cdtype=cdtype, hot=3000)
+    feats, coords = feats.cuda(), coords.cuda()
+    shape = (2, 2, 64, 64)
+    up = torch.randn((2, 80, 2, 64, 64), generator=torch.Generator().manual_seed(3)).cuda()
+    a, ga = _fwd_bwd(bev_pool, feats, coords, shape, up)
+    b, gb = _fwd_bwd(bev.bev_pool, feats, coords, shape, up)
+    torch.testing.assert_close(a, b, **FP32_TOL)
+    assert torch.equal(ga, gb)
+
+
+def test_bev_pool_det_sample_vs_triton(ref):
+    """One full det sample (1.77 M frustum points, 360 x 360 grid), fp32."""
+    bev, _, _ = ref
+    case = synth.det_bev_pool_case(1, device='cuda')
+    shape = (case.B, case.D, case.H, case.W)
+    up = torch.randn((case.B, case.feats.size(1), case.D, case.H, case.W),
+                     generator=torch.Generator().manual_seed(4)).cuda()
+    a, ga = _fwd_bwd(bev_pool, case.feats, case.coords, shape, up)
+    b, gb = _fwd_bwd(bev.bev_pool, case.feats, case.coords, shape, up)
+    torch.testing.assert_close(a, b, **FP32_TOL)
+    assert torch.equal(ga, gb)
+
+
+def test_bev_pool_fp16_vs_triton(ref):
+    bev, _, _ = ref
+    case = synth.det_bev_pool_case(1, device='cuda', dtype=torch.float16)
+    shape = (case.B, case.D, case.H, case.W)
+    ranks = ((case.coords[:, 3] * case.D + case.coords[:, 2]) * case.H + case.coords[:, 0]) * case.W + case.coords[:, 1]
+    want = torch.zeros((case.B * case.D * case.H * case.W, case.feats.size(1)), dtype=torch.float64, device='cuda')
+    want.index_add_(0, ranks, case.feats.double())
+    want = want.view(case.B, case.D, case.H, case.W, -1).permute(0, 4, 1, 2, 3)
+    a = bev_pool(case.feats, case.coords, *shape)
+    b = bev.bev_pool(case.feats, case.coords, *shape)
+    torch.cuda.synchronize()
+    err_a = (a.double() - want).abs().max().item()
+    err_b = (b.double() - want).abs().max().item()
+    torch.testing.assert_close(a.double(), want, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(b.double(), want, rtol=1e-2, atol=1e-2)
+    assert err_a <= err_b
+
+
+def _hard_outputs(fn, pts, vs, cr, mp, mv):
+    voxels = torch.zeros((mv, mp, pts.size(1)), dtype=pts.dtype, device='cuda')
+    coors = torch.zeros((mv, 3), dtype=torch.int32, device='cuda')
+    num = torch.zeros((mv,), dtype=torch.int32, device='cuda')
+    vn = fn(pts, voxels, coors, num, vs, cr, mp, mv, 3, True)
+    torch.cuda.synchronize()
+    return voxels, coors, num, int(vn)
+
+
+@pytest.mark.parametrize('sample', [0, 1])
+def test_hard_voxelize_lidar_vs_triton(ref, sample):
+    _, vox, _ = ref
+    pts = synth.lidar_sweeps(sample).cuda()
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    mp, mv = synth.LIDAR_MAX_POINTS, synth.LIDAR_MAX_VOXELS
+    v, c, n, vn = _hard_outputs(hard_voxelize, pts, vs, cr, mp, mv)
+    rv, rc, rn, rvn = _hard_outputs(vox.hard_voxelize, pts, vs, cr, mp, mv)
+    assert vn == rvn and vn > 0
+    assert torch.equal(c, rc) and torch.equal(n, rn)
+    # rows past voxel_num are zero in both
+    assert not v[vn:].any() and not rv[vn:].any()
+    # per-voxel contents: sets of rows for voxels that kept every point
+    cnt = torch.zeros(vn, dtype=torch.int64, device='cuda')
+    cells = torch.floor((pts[:, :3] - torch.tensor(cr[:3], device='cuda')) /
+                        torch.tensor(vs, device='cuda')).long()
+    grid = [round((cr[3 + i] - cr[i]) / vs[i]) for i in range(3)]
+    inr = ((cells >= 0) & (cells < torch.tensor(grid, device='cuda'))).all(1)
+    key = (cells[:, 0] * grid[1] + cells[:, 1]) * grid[2] + cells[:, 2]
+    vkey = (c[:vn, 0].long() * grid[1] + c[:vn, 1].long()) * grid[2] + c[:vn, 2].long()
+    order = torch.argsort(vkey)
+    pos = torch.searchsorted(vkey[order], key[inr])
+    pos = pos.clamp(max=vn - 1)
+    hit = vkey[order][pos] == key[inr]
+    cnt.index_add_(0, order[pos[hit]], torch.ones_like(pos[hit]))
+    full = cnt <= mp  # the voxel stored all of its points
+    assert torch.equal(cnt.clamp(max=mp).to(torch.int32), n[:vn])
+
+    def row_sets(vx, sel):
+        rows = vx[:vn][sel]  # [m, P, F]
+        # sort each voxel's rows lexicographically (zero padding rows sort first)
+        m, P, F = rows.shape
+        keyed = rows.double()
+        for f in reversed(range(F)):
+            idx = torch.argsort(keyed[:, :, f], dim=1, stable=True)
+            keyed = torch.gather(keyed, 1, idx.unsqueeze(-1).expand(-1, -1, F))
+        return keyed
+
+    assert torch.equal(row_sets(v, full), row_sets(rv, full))
+    # overflowing voxels: every stored Triton row lies in its voxel
+    over = torch.nonzero(~full).squeeze(1)
+    if over.numel():
+        rows = rv[over]  # [m, P, F], all P slots filled
+        rc3 = torch.floor((rows[..., :3] - torch.tensor(cr[:3], device='cuda')) /
+                          torch.tensor(vs, device='cuda')).to(torch.int32)
+        assert torch.equal(rc3, c[over].unsqueeze(1).expand_as(rc3))
+
+
+def test_dynamic_voxelize_vs_triton(ref):
+    _, vox, _ = ref
+    pts = synth.lidar_sweeps(0).cuda()
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    a = torch.zeros((pts.size(0), 3), dtype=torch.int32, device='cuda')
+    b = torch.zeros_like(a)
+    dynamic_voxelize(pts, a, vs, cr, 3)
+    vox.dynamic_voxelize(pts, b, vs, cr, 3)
+    torch.cuda.synchronize()
+    valid = b[:, 0] != -1
+    assert torch.equal(a[:, 0] != -1, valid)
+    assert torch.equal(a[valid], b[valid])
+    assert bool((a[~valid] == -1).all())
+
+
+@pytest.mark.parametrize('red', ['sum', 'mean', 'max'])
+def test_dynamic_scatter_vs_triton(ref, red):
+    _, _, sc = ref
+    g = torch.Generator().manual_seed(12)
+    n, C = 60_000, 16
+    f = torch.randn((n, C), generator=g).cuda()
+    c = torch.randint(-1, 30, (n, 3), generator=g).to(torch.int32).cuda()
+    a = dynamic_point_to_voxel_forward(f, c, red)
+    b = sc.dynamic_point_to_voxel_forward(f, c, red)
+    torch.cuda.synchronize()
+    m = b[1].size(0)
+    assert torch.equal(a[1][:m], b[1]) and a[1].size(0) == m
+    assert torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+    if red == 'max':
+        assert torch.equal(a[0], b[0])
+    else:
+        torch.testing.assert_close(a[0], b[0], **FP32_TOL)
+    up = torch.randn((m, C), generator=g).cuda()
+    ga = torch.empty_like(f)
+    gb = torch.empty_like(f)
+    dynamic_point_to_voxel_backward(ga, up, f, b[0], b[2], b[3], red)
+    sc.dynamic_point_to_voxel_backward(gb, up, f, b[0], b[2], b[3], red)
+    torch.cuda.synchronize()
+    assert torch.equal(ga, gb)

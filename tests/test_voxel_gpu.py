@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from bevfusion_triton_b200 import synth
+from tests import synth
 from bevfusion_triton_b200.ops.voxel import DynamicScatter, Voxelization, dynamic_scatter, voxelization, voxelize_batch
 from bevfusion_triton_b200.ops.voxel.voxel_layer import (dynamic_point_to_voxel_backward,
                                                          dynamic_point_to_voxel_forward, dynamic_voxelize,

@@ -69,11 +69,22 @@ def test_noalloc_matches_regular_entry_point_twice():
 
 
 def test_noalloc_refuses_sizes_beyond_its_array():
+    """A grid whose plan exceeds the fixed array is refused.  Every buffer
+    handed over is a real device allocation sized for the call (16 in-grid
+    points, 4 channels, a 4096 x 4096 grid whose per-cell plan table alone
+    needs 128 MiB), so the call is valid apart from the size limit."""
     if not torch.cuda.is_available():
         pytest.skip('CUDA device required')
     L = _lib()
     cap = L.bfb_bev_pool_noalloc_capacity()
-    n = cap // 8  # plan + scratch take more than 8 bytes per point
-    rc = L.bfb_bev_pool_forward_noalloc(vp(16), 0, vp(16), 1, i64(n), i64(80), i64(1), i64(1), i64(16), i64(16),
-                                        vp(16), vp(torch.cuda.current_stream().cuda_stream))
+    shape = (1, 1, 4096, 4096)
+    assert (shape[2] * shape[3] + 1) * 8 > cap
+    feats, coords = rand_bev_case(16, 4, *shape, seed=23, cdtype=torch.int64)
+    feats, coords = feats.cuda(), coords.cuda()
+    out = torch.full((1, 4, 1, 4096, 4096), 5.0, device='cuda')
+    rc = L.bfb_bev_pool_forward_noalloc(vp(feats.data_ptr()), 0, vp(coords.data_ptr()), 1, i64(16), i64(4),
+                                        *[i64(x) for x in shape], vp(out.data_ptr()),
+                                        vp(torch.cuda.current_stream().cuda_stream))
     assert rc == -4  # BFB_ERR_TOO_LARGE, before any device work
+    torch.cuda.synchronize()
+    assert bool((out == 5.0).all())
