@@ -37,6 +37,8 @@ def load_native():
     _cdll = ctypes.CDLL(str(LIB), mode=ctypes.RTLD_GLOBAL)
     torch.ops.load_library(str(TORCH_LIB))
     _loaded = True
+    from .ops import _registry  # fake kernels + autograd of the ops just loaded
+    _registry.register()
     return _cdll
 
 

@@ -184,12 +184,19 @@ __global__ __launch_bounds__(kRadixThreads, 2) void radix_downsweep_kernel(
 int radix_sort_index(uint32_t* keys0, uint32_t* keys1, uint32_t* vals_tmp, uint32_t* vals_out,
                      int64_t n, const RadixPlan& plan, uint32_t* hist, uint32_t* scan_scratch,
                      bool hist0_ready, cudaStream_t stream, uint32_t** keys_sorted) {
+  return radix_sort_pairs(keys0, keys1, nullptr, vals_tmp, vals_out, n, plan, hist, scan_scratch, hist0_ready,
+                          stream, keys_sorted);
+}
+
+int radix_sort_pairs(uint32_t* keys0, uint32_t* keys1, const uint32_t* vals_in, uint32_t* vals_tmp,
+                     uint32_t* vals_out, int64_t n, const RadixPlan& plan, uint32_t* hist,
+                     uint32_t* scan_scratch, bool hist0_ready, cudaStream_t stream, uint32_t** keys_sorted) {
   uint32_t* kbuf[2] = {keys0, keys1};
   if (keys_sorted) *keys_sorted = kbuf[plan.passes & 1];
   if (n == 0) return BFB_OK;
   const int64_t ntiles = radix_tiles(n);
   if (ntiles > 0x7fffffff) return BFB_ERR_TOO_LARGE;
-  const uint32_t* vin = nullptr;  // pass 0: values are the indices
+  const uint32_t* vin = vals_in;  // null: pass 0's values are the indices
   for (int ps = 0; ps < plan.passes; ++ps) {
     const int bits = plan.digit_bits[ps], shift = plan.shift[ps];
     const int nd = 1 << bits;

@@ -52,4 +52,12 @@ int radix_sort_index(uint32_t* keys0, uint32_t* keys1, uint32_t* vals_tmp, uint3
                      int64_t n, const RadixPlan& plan, uint32_t* hist, uint32_t* scan_scratch,
                      bool hist0_ready, cudaStream_t stream, uint32_t** keys_sorted);
 
+// The same sort carrying given values: vals_out[i] = vals_in[j] of the
+// element j that lands at position i.  vals_in must not alias vals_tmp or
+// vals_out.  Two stable sorts chained this way (low word first, then the
+// high word carrying the first permutation) order 64-bit keys.
+int radix_sort_pairs(uint32_t* keys0, uint32_t* keys1, const uint32_t* vals_in, uint32_t* vals_tmp,
+                     uint32_t* vals_out, int64_t n, const RadixPlan& plan, uint32_t* hist,
+                     uint32_t* scan_scratch, bool hist0_ready, cudaStream_t stream, uint32_t** keys_sorted);
+
 }  // namespace bfb

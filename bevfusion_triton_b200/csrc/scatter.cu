@@ -9,11 +9,16 @@
 //             channel's gradient to the lowest point index whose feature equals
 //             the reduced value
 //
-// Design: each valid row gets a packed lexicographic key (bit widths from the
-// per-dimension maxima), the stable radix sort groups equal rows with points in
-// ascending index order, segment heads are scanned into voxel ids, and a warp
-// per voxel reduces its points in that order in fp32 (sums therefore follow
-// torch.index_add_'s order exactly).
+// Design: each valid row gets a packed lexicographic key whose per-column bit
+// widths come from the grid extents (when the caller knows them) or from the
+// column maxima (one device pass and one host read).  Keys of up to 31 bits
+// are sorted in one stable radix sort; wider keys (up to 62 bits, e.g. batched
+// (b, x, y, z) rows on a LiDAR grid) are sorted low word first and then by
+// the high word carrying the first permutation, which orders them as 64-bit
+// keys.  Equal rows then sit together with their points in ascending index
+// order; segment heads are scanned into voxel ids, and a group of lanes per
+// voxel reduces its points in that order in fp32 with 16-byte row loads (sums
+// therefore follow torch.index_add_'s order exactly).
 #include <algorithm>
 #include <cmath>
 
@@ -24,15 +29,21 @@ namespace bfb {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kMaxKeyBits = 62;
 
 struct ScatterWs {
-  int32_t* dmax;    // [8]   per-dimension maxima, then status
-  uint32_t* keys0;  // [n]
-  uint32_t* keys1;  // [n]
-  uint32_t* vtmp;   // [n]
-  uint32_t* perm;   // [n]
-  uint32_t* head;   // [n+1] segment-head flags, then voxel id of each sorted position
-  uint32_t* seg;    // [n+1] sorted start of every voxel
+  int32_t* dmax;       // [8]  per-column maxima
+  uint32_t* status;    // [8]  [0]: rows with a coordinate past the given extent
+  uint32_t* lo0;       // [n]  key (narrow) or its low word (wide)
+  uint32_t* lo1;       // [n]
+  uint32_t* lo_keep;   // [n]  low words in input order (wide)
+  uint32_t* hi0;       // [n]  high words (wide)
+  uint32_t* hi1;       // [n]
+  uint32_t* vtmp;      // [n]
+  uint32_t* perm1;     // [n]  order by low word (wide)
+  uint32_t* perm;      // [n]  final order
+  uint32_t* head;      // [n+1] segment-head flags, then voxel id of each sorted position
+  uint32_t* seg;       // [n+1] sorted start of every voxel
   uint32_t* hist;
   uint32_t* scan;
 };
@@ -42,9 +53,14 @@ size_t carve_ws(void* base, int64_t n, ScatterWs* w) {
   rp.max_digit_bits = kRadixMaxBits;  // upper bound over every key width
   Carver c(base);
   w->dmax = c.take<int32_t>(8);
-  w->keys0 = c.take<uint32_t>((size_t)n);
-  w->keys1 = c.take<uint32_t>((size_t)n);
+  w->status = c.take<uint32_t>(8);
+  w->lo0 = c.take<uint32_t>((size_t)n);
+  w->lo1 = c.take<uint32_t>((size_t)n);
+  w->lo_keep = c.take<uint32_t>((size_t)n);
+  w->hi0 = c.take<uint32_t>((size_t)n);
+  w->hi1 = c.take<uint32_t>((size_t)n);
   w->vtmp = c.take<uint32_t>((size_t)n);
+  w->perm1 = c.take<uint32_t>((size_t)n);
   w->perm = c.take<uint32_t>((size_t)n);
   w->head = c.take<uint32_t>((size_t)n + 1);
   w->seg = c.take<uint32_t>((size_t)n + 1);
@@ -72,47 +88,77 @@ __global__ void dim_max_kernel(const int32_t* __restrict__ coors, int64_t n, int
 
 struct KeySpec {
   int ndim;
-  int shift[4];
-  uint32_t invalid;  // key of rows with a negative coordinate (sorts last)
+  int bits;            // total key width
+  bool wide;           // bits > 31: two 32-bit words
+  int shift[4];        // of each column inside the 64-bit key
+  uint32_t extent[4];  // 0 = unchecked
+  uint32_t invalid;    // key (narrow) or high word (wide) of a row with a negative coordinate: sorts last
 };
 
-__global__ void row_keys_kernel(const int32_t* __restrict__ coors, int64_t n, KeySpec ks, uint32_t* __restrict__ keys) {
+__global__ void row_keys_kernel(const int32_t* __restrict__ coors, int64_t n, KeySpec ks, uint32_t* __restrict__ lo,
+                                uint32_t* __restrict__ lo_keep, uint32_t* __restrict__ hi,
+                                uint32_t* __restrict__ status) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  uint32_t k = 0;
-  bool ok = true;
+  uint64_t k = 0;
+  bool ok = true, over = false;
   for (int d = 0; d < ks.ndim; ++d) {
     const int32_t v = coors[i * ks.ndim + d];
     ok &= v >= 0;
-    k |= (uint32_t)v << ks.shift[d];
+    over |= ks.extent[d] != 0u && v >= 0 && (uint32_t)v >= ks.extent[d];
+    k |= (uint64_t)(uint32_t)v << ks.shift[d];
   }
-  keys[i] = ok ? k : ks.invalid;
+  if (ok && over) atomicAdd(status, 1u);
+  if (!ks.wide) {
+    lo[i] = ok ? (uint32_t)k : ks.invalid;
+  } else {
+    const uint32_t l = ok ? (uint32_t)k : 0u;
+    lo[i] = l;
+    lo_keep[i] = l;
+    hi[i] = ok ? (uint32_t)(k >> 32) : ks.invalid;
+  }
 }
 
-__global__ void seg_head_kernel(const uint32_t* __restrict__ keys, int64_t n, uint32_t invalid, uint32_t* __restrict__ head) {
+__global__ void gather_u32_kernel(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx, int64_t n,
+                                  uint32_t* __restrict__ dst) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = __ldg(src + __ldg(idx + i));
+}
+
+// The sorted key at position i: its primary word and, for wide keys, the low
+// word (in the same final order).
+struct SortedKeys {
+  const uint32_t* key;
+  const uint32_t* lo;  // null for narrow keys
+  uint32_t invalid;
+  __device__ __forceinline__ bool same(int64_t i, int64_t j) const {
+    return key[i] == key[j] && (!lo || lo[i] == lo[j]);
+  }
+  __device__ __forceinline__ bool bad(int64_t i) const { return key[i] == invalid; }
+};
+
+__global__ void seg_head_kernel(SortedKeys sk, int64_t n, uint32_t* __restrict__ head) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const uint32_t k = keys[i];
-  head[i] = (k != invalid && (i == 0 || keys[i - 1] != k)) ? 1u : 0u;
+  head[i] = (!sk.bad(i) && (i == 0 || !sk.same(i, i - 1))) ? 1u : 0u;
 }
 
 // head (scanned) -> voxel id per sorted position; map, unique coords, segment starts
-__global__ void seg_assign_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ perm, int64_t n,
-                                  uint32_t invalid, const uint32_t* __restrict__ vid, const int32_t* __restrict__ coors,
-                                  int ndim, int32_t* __restrict__ map, int32_t* __restrict__ out_coors,
+__global__ void seg_assign_kernel(SortedKeys sk, const uint32_t* __restrict__ perm, int64_t n,
+                                  const uint32_t* __restrict__ vid, const int32_t* __restrict__ coors, int ndim,
+                                  int32_t* __restrict__ map, int32_t* __restrict__ out_coors,
                                   uint32_t* __restrict__ seg) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const uint32_t k = keys[i];
   const uint32_t p = perm[i];
-  if (k == invalid) {
+  if (sk.bad(i)) {
     map[p] = -1;
-    if (i == 0 || keys[i - 1] != invalid) seg[vid[n]] = (uint32_t)i;  // end of the last voxel
+    if (i == 0 || !sk.bad(i - 1)) seg[vid[n]] = (uint32_t)i;  // end of the last voxel
     return;
   }
   const uint32_t m = vid[i + 1] - 1;  // inclusive count of heads up to i, minus one
   map[p] = (int32_t)m;
-  if (i == 0 || keys[i - 1] != k) {
+  if (i == 0 || !sk.same(i, i - 1)) {
     seg[m] = (uint32_t)i;
     for (int d = 0; d < ndim; ++d) out_coors[(int64_t)m * ndim + d] = coors[(int64_t)p * ndim + d];
   }
@@ -126,24 +172,55 @@ __global__ void seg_count_kernel(const uint32_t* __restrict__ seg, const uint32_
   counts[m] = (int32_t)(seg[m + 1] - seg[m]);
 }
 
-// reduce: 0 sum, 1 mean, 2 max.  Warp per voxel, lanes over channels.
-template <class T>
-__global__ void seg_reduce_kernel(const T* __restrict__ feats, int64_t c, const uint32_t* __restrict__ perm,
-                                  const uint32_t* __restrict__ seg, const uint32_t* __restrict__ total, int reduce,
-                                  T* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+// VE consecutive channels of one row, as fp32 (one 16-byte load when VE > 1).
+template <class T, int VE>
+__device__ __forceinline__ void load_row(const T* p, float (&f)[VE]) {
+  if constexpr (VE == 1) {
+    f[0] = to_f32<T>(__ldg(p));
+  } else {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int q = 0; q < VE; ++q) f[q] = to_f32<T>(e[q]);
+  }
+}
+
+// reduce: 0 sum, 1 mean, 2 max.  A group of 2^glog lanes per voxel; each lane
+// owns channel vectors lane, lane + G, ...  Points are taken in sorted
+// (ascending index) order, kU row loads in flight ahead of the adds.
+template <class T, int VE>
+__global__ __launch_bounds__(kThreads) void seg_reduce_kernel(const T* __restrict__ feats, int64_t c, int nvec,
+                                                              int glog, const uint32_t* __restrict__ perm,
+                                                              const uint32_t* __restrict__ seg,
+                                                              const uint32_t* __restrict__ total, int reduce,
+                                                              T* __restrict__ out) {
+  constexpr int kU = 4;
+  const int G = 1 << glog;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int sub = (int)(tid & (G - 1));
+  const int64_t groups = ((int64_t)gridDim.x * blockDim.x) >> glog;
   const int64_t m_total = *total;
-  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < m_total; m += warps) {
+  for (int64_t m = tid >> glog; m < m_total; m += groups) {
     const uint32_t a = seg[m], b = seg[m + 1];
-    for (int64_t ch = lane; ch < c; ch += 32) {
-      float acc = reduce == 2 ? -INFINITY : 0.f;
-      for (uint32_t i = a; i < b; ++i) {
-        const float v = to_f32<T>(feats[(int64_t)perm[i] * c + ch]);
-        acc = reduce == 2 ? fmaxf(acc, v) : acc + v;
+    for (int v = sub; v < nvec; v += G) {
+      float acc[VE];
+#pragma unroll
+      for (int q = 0; q < VE; ++q) acc[q] = reduce == 2 ? -INFINITY : 0.f;
+      for (uint32_t i = a; i < b; i += kU) {
+        float r[kU][VE];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (i + u < b) load_row<T, VE>(feats + (int64_t)__ldg(perm + i + u) * c + (int64_t)v * VE, r[u]);
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (i + u < b) {
+#pragma unroll
+            for (int q = 0; q < VE; ++q) acc[q] = reduce == 2 ? fmaxf(acc[q], r[u][q]) : __fadd_rn(acc[q], r[u][q]);
+          }
       }
-      if (reduce == 1) acc = acc / (float)(b - a);
-      out[m * c + ch] = from_f32<T>(acc);
+      T* dst = out + m * c + (int64_t)v * VE;
+#pragma unroll
+      for (int q = 0; q < VE; ++q) dst[q] = from_f32<T>(reduce == 1 ? __fdiv_rn(acc[q], (float)(b - a)) : acc[q]);
     }
   }
 }
@@ -161,7 +238,7 @@ __global__ void grad_sum_kernel(const T* __restrict__ gout, const int32_t* __res
     return;
   }
   float g = to_f32<T>(gout[(int64_t)m * c + ch]);
-  if (mean) g = g / (float)counts[m];
+  if (mean) g = __fdiv_rn(g, (float)counts[m]);
   gfeat[idx] = from_f32<T>(g);
 }
 
@@ -186,52 +263,101 @@ __global__ void grad_max_scatter_kernel(const T* __restrict__ gout, const int32_
   if (src < n) gfeat[(int64_t)src * c + ch] = gout[idx];
 }
 
+int width_of(int64_t max_value) {
+  int b = 0;
+  while (b < 31 && ((int64_t)1 << b) <= max_value) ++b;
+  return b;
+}
+
 template <class T>
 int scatter_forward_t(const void* feats, const int32_t* coors, int64_t n, int64_t c, int64_t ndim, int reduce,
-                      const ScatterWs& w, void* out_feats, int32_t* out_coors, int32_t* map, int32_t* counts,
-                      int64_t* m_out, cudaStream_t st) {
-  BFB_CUDA(cudaMemsetAsync(w.dmax, 0xff, 8 * sizeof(int32_t), st));
-  dim_max_kernel<<<(unsigned)std::min<int64_t>(ceil_div(n, kThreads), 1184), kThreads, 0, st>>>(coors, n, (int)ndim, w.dmax);
-  BFB_CHECK_LAUNCH();
-  int32_t dmax[4] = {-1, -1, -1, -1};
-  BFB_CUDA(cudaMemcpyAsync(dmax, w.dmax, sizeof(int32_t) * ndim, cudaMemcpyDeviceToHost, st));
-  BFB_CUDA(cudaStreamSynchronize(st));
-  KeySpec ks;
+                      const int64_t* extents, const ScatterWs& w, void* out_feats, int32_t* out_coors, int32_t* map,
+                      int32_t* counts, int64_t* m_out, cudaStream_t st) {
+  KeySpec ks{};
   ks.ndim = (int)ndim;
+  int width[4] = {0, 0, 0, 0};
+  if (extents) {
+    for (int d = 0; d < ndim; ++d) {
+      if (extents[d] <= 0 || extents[d] > 0x7fffffffLL) return BFB_ERR_INVALID_ARG;
+      width[d] = width_of(extents[d] - 1);
+      ks.extent[d] = (uint32_t)extents[d];
+    }
+  } else {
+    BFB_CUDA(cudaMemsetAsync(w.dmax, 0xff, 8 * sizeof(int32_t), st));
+    dim_max_kernel<<<(unsigned)std::min<int64_t>(ceil_div(n, kThreads), 1184), kThreads, 0, st>>>(coors, n, (int)ndim,
+                                                                                                  w.dmax);
+    BFB_CHECK_LAUNCH();
+    int32_t dmax[4] = {-1, -1, -1, -1};
+    BFB_CUDA(cudaMemcpyAsync(dmax, w.dmax, sizeof(int32_t) * ndim, cudaMemcpyDeviceToHost, st));
+    BFB_CUDA(cudaStreamSynchronize(st));
+    for (int d = 0; d < ndim; ++d) width[d] = width_of(dmax[d]);
+  }
   int bits = 0;
   for (int d = (int)ndim - 1; d >= 0; --d) {
-    int b = 0;
-    while (b < 31 && ((int64_t)1 << b) <= (int64_t)dmax[d]) ++b;
     ks.shift[d] = bits;
-    bits += b;
+    bits += width[d];
   }
-  if (bits > 31) return BFB_ERR_TOO_LARGE;
-  ks.invalid = bits == 0 ? 1u : (1u << bits);  // above every valid key
+  if (bits > kMaxKeyBits) return BFB_ERR_TOO_LARGE;
+  ks.bits = bits;
+  ks.wide = bits > 31;
+  ks.invalid = ks.wide ? (1u << (bits - 32)) : (bits == 0 ? 1u : (1u << bits));  // above every valid key
+  BFB_CUDA(cudaMemsetAsync(w.status, 0, 8 * sizeof(uint32_t), st));
   const unsigned nb = (unsigned)ceil_div(n, kThreads);
-  row_keys_kernel<<<nb, kThreads, 0, st>>>(coors, n, ks, w.keys0);
+  row_keys_kernel<<<nb, kThreads, 0, st>>>(coors, n, ks, w.lo0, w.lo_keep, w.hi0, w.status);
   BFB_CHECK_LAUNCH();
-  const RadixPlan rp = make_radix_plan(ks.invalid);
-  uint32_t* sorted = nullptr;
-  BFB_TRY(radix_sort_index(w.keys0, w.keys1, w.vtmp, w.perm, n, rp, w.hist, w.scan, false, st, &sorted));
-  seg_head_kernel<<<nb, kThreads, 0, st>>>(sorted, n, ks.invalid, w.head);
+
+  SortedKeys sk{};
+  sk.invalid = ks.invalid;
+  if (!ks.wide) {
+    uint32_t* sorted = nullptr;
+    BFB_TRY(radix_sort_index(w.lo0, w.lo1, w.vtmp, w.perm, n, make_radix_plan(ks.invalid), w.hist, w.scan, false, st,
+                             &sorted));
+    sk.key = sorted;
+  } else {
+    // low word first (all 32 bits), then the high word carrying that order
+    BFB_TRY(radix_sort_index(w.lo0, w.lo1, w.vtmp, w.perm1, n, make_radix_plan(0xffffffffu), w.hist, w.scan, false,
+                             st, nullptr));
+    gather_u32_kernel<<<nb, kThreads, 0, st>>>(w.hi0, w.perm1, n, w.hi1);
+    BFB_CHECK_LAUNCH();
+    uint32_t* sorted = nullptr;
+    BFB_TRY(radix_sort_pairs(w.hi1, w.hi0, w.perm1, w.vtmp, w.perm, n, make_radix_plan(ks.invalid), w.hist, w.scan,
+                             false, st, &sorted));
+    uint32_t* lo_final = sorted == w.hi1 ? w.hi0 : w.hi1;  // the free key buffer
+    gather_u32_kernel<<<nb, kThreads, 0, st>>>(w.lo_keep, w.perm, n, lo_final);
+    BFB_CHECK_LAUNCH();
+    sk.key = sorted;
+    sk.lo = lo_final;
+  }
+  seg_head_kernel<<<nb, kThreads, 0, st>>>(sk, n, w.head);
   BFB_CHECK_LAUNCH();
   // inclusive voxel ids: vid[i + 1] = heads in [0, i]; vid[n] = M
   BFB_CUDA(cudaMemsetAsync(w.head + n, 0, sizeof(uint32_t), st));
   BFB_TRY(exclusive_scan_u32(w.head, w.head, n + 1, w.scan, nullptr, st));
-  seg_assign_kernel<<<nb, kThreads, 0, st>>>(sorted, w.perm, n, ks.invalid, w.head, coors, (int)ndim, map, out_coors,
-                                             w.seg);
+  seg_assign_kernel<<<nb, kThreads, 0, st>>>(sk, w.perm, n, w.head, coors, (int)ndim, map, out_coors, w.seg);
   BFB_CHECK_LAUNCH();
-  uint32_t m = 0;
+  seg_count_kernel<<<(unsigned)ceil_div(n, kThreads), kThreads, 0, st>>>(w.seg, w.head + n, counts);
+  BFB_CHECK_LAUNCH();
+  const bool v16 = (c * (int64_t)sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(feats) & 15) == 0;
+  constexpr int kVE = 16 / sizeof(T);
+  const int nvec = v16 ? (int)(c / kVE) : (int)c;
+  int glog = 0;
+  while ((1 << glog) < nvec && glog < 5) ++glog;
+  // grid sized for the worst case (one voxel per point); groups stride over the voxels
+  const unsigned blocks = (unsigned)std::min<int64_t>(ceil_div(n << glog, kThreads), 148 * 16);
+  if (v16)
+    seg_reduce_kernel<T, kVE><<<blocks, kThreads, 0, st>>>(static_cast<const T*>(feats), c, nvec, glog, w.perm, w.seg,
+                                                          w.head + n, reduce, static_cast<T*>(out_feats));
+  else
+    seg_reduce_kernel<T, 1><<<blocks, kThreads, 0, st>>>(static_cast<const T*>(feats), c, nvec, glog, w.perm, w.seg,
+                                                        w.head + n, reduce, static_cast<T*>(out_feats));
+  BFB_CHECK_LAUNCH();
+  // the one host read: the voxel count (the caller sizes its outputs by it)
+  uint32_t m = 0, over = 0;
   BFB_CUDA(cudaMemcpyAsync(&m, w.head + n, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  BFB_CUDA(cudaMemcpyAsync(&over, w.status, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
   BFB_CUDA(cudaStreamSynchronize(st));
   *m_out = m;
-  if (m == 0) return BFB_OK;
-  seg_count_kernel<<<(unsigned)ceil_div(m, kThreads), kThreads, 0, st>>>(w.seg, w.head + n, counts);
-  BFB_CHECK_LAUNCH();
-  seg_reduce_kernel<T><<<(unsigned)std::min<int64_t>(ceil_div((int64_t)m * 32, kThreads), 148 * 16), kThreads, 0, st>>>(
-      static_cast<const T*>(feats), c, w.perm, w.seg, w.head + n, reduce, static_cast<T*>(out_feats));
-  BFB_CHECK_LAUNCH();
-  return BFB_OK;
+  return over ? BFB_ERR_DEVICE_STATUS : BFB_OK;
 }
 
 template <class T>
@@ -273,9 +399,9 @@ extern "C" int bfb_dynamic_scatter_workspace_size(int64_t n, int64_t c, int64_t 
 }
 
 extern "C" int bfb_dynamic_scatter_forward(const void* feats, int dtype, const int32_t* coors, int64_t n, int64_t c,
-                                           int64_t ndim, int reduce, void* out_feats, int32_t* out_coors,
-                                           int32_t* point2voxel, int32_t* counts, int64_t* num_voxels, void* ws,
-                                           size_t ws_bytes, void* stream) {
+                                           int64_t ndim, int reduce, const int64_t* extents, void* out_feats,
+                                           int32_t* out_coors, int32_t* point2voxel, int32_t* counts,
+                                           int64_t* num_voxels, void* ws, size_t ws_bytes, void* stream) {
   if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (n < 0 || c <= 0 || ndim < 1 || ndim > 4 || reduce < 0 || reduce > 2 || !num_voxels) return BFB_ERR_INVALID_ARG;
   if (n > 0x7ffffffeLL) return BFB_ERR_TOO_LARGE;
@@ -288,14 +414,14 @@ extern "C" int bfb_dynamic_scatter_forward(const void* feats, int dtype, const i
   cudaStream_t st = as_stream(stream);
   switch (dtype) {
     case BFB_F32:
-      return scatter_forward_t<float>(feats, coors, n, c, ndim, reduce, w, out_feats, out_coors, point2voxel, counts,
-                                      num_voxels, st);
+      return scatter_forward_t<float>(feats, coors, n, c, ndim, reduce, extents, w, out_feats, out_coors, point2voxel,
+                                      counts, num_voxels, st);
     case BFB_F16:
-      return scatter_forward_t<__half>(feats, coors, n, c, ndim, reduce, w, out_feats, out_coors, point2voxel, counts,
-                                       num_voxels, st);
+      return scatter_forward_t<__half>(feats, coors, n, c, ndim, reduce, extents, w, out_feats, out_coors,
+                                       point2voxel, counts, num_voxels, st);
     default:
-      return scatter_forward_t<__nv_bfloat16>(feats, coors, n, c, ndim, reduce, w, out_feats, out_coors, point2voxel,
-                                              counts, num_voxels, st);
+      return scatter_forward_t<__nv_bfloat16>(feats, coors, n, c, ndim, reduce, extents, w, out_feats, out_coors,
+                                              point2voxel, counts, num_voxels, st);
   }
 }
 

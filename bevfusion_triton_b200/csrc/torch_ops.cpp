@@ -428,7 +428,8 @@ int reduce_code(c10::string_view r) {
 
 std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> dynamic_scatter_forward(const at::Tensor& feats_in,
                                                                                    const at::Tensor& coors_in,
-                                                                                   c10::string_view reduce) {
+                                                                                   c10::string_view reduce,
+                                                                                   at::OptionalIntArrayRef extents) {
   require_cuda(feats_in, "feats");
   require_cuda(coors_in, "coors");
   c10::cuda::CUDAGuard guard(feats_in.device());
@@ -444,10 +445,14 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> dynamic_scatter_forwa
   auto map = at::empty({n}, coors.options());
   auto cnt = at::empty({n}, coors.options());
   int64_t m = 0;
-  check(bfb_dynamic_scatter_forward(feats.data_ptr(), dtype_code(feats), coors.data_ptr<int32_t>(), n, c, ndim, r,
-                                    out.data_ptr(), oc.data_ptr<int32_t>(), map.data_ptr<int32_t>(),
-                                    cnt.data_ptr<int32_t>(), &m, ws.data_ptr(), wb, stream_of(feats)),
-        "dynamic_scatter forward");
+  if (extents.has_value())
+    TORCH_CHECK_VALUE((int64_t)extents->size() == ndim, "extents must give one value per coordinate column");
+  const int64_t* ext = extents.has_value() ? extents->data() : nullptr;
+  const int st = bfb_dynamic_scatter_forward(feats.data_ptr(), dtype_code(feats), coors.data_ptr<int32_t>(), n, c, ndim, r,
+                                    ext, out.data_ptr(), oc.data_ptr<int32_t>(), map.data_ptr<int32_t>(),
+                                    cnt.data_ptr<int32_t>(), &m, ws.data_ptr(), wb, stream_of(feats));
+  TORCH_CHECK_VALUE(st != BFB_ERR_DEVICE_STATUS, "dynamic_scatter: a coordinate lies beyond the given extents");
+  check(st, "dynamic_scatter forward");
   return {out.narrow(0, 0, m), oc.narrow(0, 0, m), map, cnt.narrow(0, 0, m)};
 }
 
@@ -543,7 +548,9 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def(
       "get_indice_pairs(Tensor indices, int batch, int[] out_shape, int[] ksize, int[] stride, int[] padding, "
       "int[] dilation, bool subm, bool transpose) -> (Tensor, Tensor, Tensor)");
-  m.def("dynamic_scatter_forward(Tensor feats, Tensor coors, str reduce) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def(
+      "dynamic_scatter_forward(Tensor feats, Tensor coors, str reduce, int[]? extents=None) -> (Tensor, Tensor, "
+      "Tensor, Tensor)");
   m.def(
       "dynamic_scatter_backward(Tensor(a!) grad_feats, Tensor grad_out, Tensor feats, Tensor reduced, Tensor map, "
       "Tensor counts, str reduce) -> ()");

@@ -2,7 +2,9 @@
 
 Reference: ops/bev_pool/src/bev_pool_triton.py:219-227 (``bev_pool``), input
 checks :12-31 (``_check_inputs``: same exception types and messages),
-autograd :153-216.  ``feats`` [N, C] (fp32 / fp16 / bf16), ``coords`` [N, 4]
+autograd :153-216 (registered on the custom op with
+``torch.library.register_autograd``, see ``ops/_registry.py``).  ``feats``
+[N, C] (fp32 / fp16 / bf16), ``coords`` [N, 4]
 int32 / int64 with columns (x, y, z, b); returns [B, C, D, H, W] in the
 dtype of ``feats``, differentiable w.r.t. ``feats``.
 
@@ -44,42 +46,12 @@ def _require_cuda(*ts: torch.Tensor) -> None:
             raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
 
 
-class _BevPoolFunction(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, feats, coords, B, D, H, W):
-        out, plan = ops().bev_pool_forward(feats, coords, B, D, H, W)
-        ctx.save_for_backward(plan)
-        ctx.shape = (feats.size(0), B, D, H, W)
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        (plan,) = ctx.saved_tensors
-        n, B, D, H, W = ctx.shape
-        gfeat = ops().bev_pool_backward(grad_out, plan, n, B, D, H, W)
-        return gfeat, None, None, None, None, None
-
-
-class _BevPoolPlannedFunction(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, feats, plan, B, D, H, W):
-        ctx.save_for_backward(plan)
-        ctx.shape = (feats.size(0), B, D, H, W)
-        return ops().bev_pool_forward_planned(feats, plan, B, D, H, W)
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        (plan,) = ctx.saved_tensors
-        n, B, D, H, W = ctx.shape
-        return ops().bev_pool_backward(grad_out, plan, n, B, D, H, W), None, None, None, None, None
-
-
 def bev_pool(feats: torch.Tensor, coords: torch.Tensor, B: int, D: int, H: int, W: int) -> torch.Tensor:
     """Sum-pool point features into a dense [B, C, D, H, W] grid."""
     B, D, H, W = int(B), int(D), int(H), int(W)
     _check_inputs(feats, coords, B, D, H, W)
     _require_cuda(feats, coords)
-    return _BevPoolFunction.apply(feats, coords, B, D, H, W)
+    return ops().bev_pool_forward(feats, coords, B, D, H, W)[0]
 
 
 def bev_pool_plan(coords: torch.Tensor, B: int, D: int, H: int, W: int) -> torch.Tensor:
@@ -125,7 +97,7 @@ def bev_pool_planned(feats: torch.Tensor, plan: torch.Tensor, B: int, D: int, H:
         raise TypeError('feats must have dtype torch.float16, torch.float32, or torch.bfloat16.')
     check_plan(plan, feats.size(0), B, D, H, W)
     _require_cuda(feats, plan)
-    return _BevPoolPlannedFunction.apply(feats, plan, int(B), int(D), int(H), int(W))
+    return ops().bev_pool_forward_planned(feats, plan, int(B), int(D), int(H), int(W))
 
 
 def plan_cells(plan: torch.Tensor, n: int, B: int, D: int, H: int, W: int) -> torch.Tensor:
@@ -137,26 +109,6 @@ def plan_cells(plan: torch.Tensor, n: int, B: int, D: int, H: int, W: int) -> to
 def invalid_count(plan: torch.Tensor) -> int:
     """Points a plan dropped as out of range (synchronises the stream)."""
     return int(ops().bev_pool_invalid_count(plan))
-
-
-class _BevPoolDepthContextFunction(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, depth, context, coords, plan, B, D, H, W):
-        if plan is None:
-            out, aux = ops().bev_pool_dc_forward(depth, context, coords, B, D, H, W)
-        else:
-            out, aux = ops().bev_pool_dc_forward_planned(depth, context, plan, B, D, H, W)
-        ctx.save_for_backward(depth, aux)
-        ctx.shape = (context.size(1), B, D, H, W)
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        depth, aux = ctx.saved_tensors
-        C, B, D, H, W = ctx.shape
-        none = depth.new_empty(0, dtype=torch.int64)  # the cells come from aux
-        gdepth, gctx = ops().bev_pool_dc_backward(grad_out, depth, none, aux, C, B, D, H, W)
-        return gdepth, gctx, None, None, None, None, None, None
 
 
 def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: torch.Tensor | None,
@@ -192,7 +144,10 @@ def bev_pool_depth_context(depth: torch.Tensor, context: torch.Tensor, coords: t
     if plan is not None:
         check_plan(plan, depth.size(0) * depth.size(1) * depth.size(2) * depth.size(3), B, D, H, W)
     _require_cuda(depth, context, *((coords,) if plan is None else (plan,)))
-    return _BevPoolDepthContextFunction.apply(depth, context, coords, plan, int(B), int(D), int(H), int(W))
+    B, D, H, W = int(B), int(D), int(H), int(W)
+    if plan is None:
+        return ops().bev_pool_dc_forward(depth, context, coords, B, D, H, W)[0]
+    return ops().bev_pool_dc_forward_planned(depth, context, plan, B, D, H, W)[0]
 
 
 def bev_grid(xbound, ybound, zbound):

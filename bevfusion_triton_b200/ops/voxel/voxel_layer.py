@@ -96,9 +96,9 @@ def hard_voxelize_batch(points: torch.Tensor, offsets: Sequence[int], voxel_size
 _REDUCE_MODE = {'none', 'mean', 'sum', 'max'}
 
 
-def dynamic_point_to_voxel_forward(feats: torch.Tensor, coors: torch.Tensor, reduce_type: str):
-    """(voxel_feats, voxel_coors, point2voxel_map, voxel_points_count);
-    scatter_points_triton.py:253-314."""
+def _check_scatter_args(feats: torch.Tensor, coors: torch.Tensor, reduce_type: str) -> None:
+    """The argument checks of scatter_points_triton.py:258-265 (same
+    exception types)."""
     if reduce_type not in _REDUCE_MODE:
         raise ValueError(f'Unsupported reduce_type: {reduce_type}')
     if feats.dim() != 2:
@@ -107,11 +107,21 @@ def dynamic_point_to_voxel_forward(feats: torch.Tensor, coors: torch.Tensor, red
         raise AssertionError('coors must have shape [N, ndim]')
     if feats.size(0) != coors.size(0):
         raise AssertionError('feats and coors must have the same first dimension')
+
+
+def dynamic_point_to_voxel_forward(feats: torch.Tensor, coors: torch.Tensor, reduce_type: str,
+                                   extents: Sequence[int] | None = None):
+    """(voxel_feats, voxel_coors, point2voxel_map, voxel_points_count);
+    scatter_points_triton.py:253-314.  ``extents`` (optional, not in the
+    reference signature): one bound per coordinate column, which saves the
+    kernel a pass over the coordinates and a host read."""
+    _check_scatter_args(feats, coors, reduce_type)
     if feats.size(0) == 0:
         return (feats.clone().detach(), coors.clone().detach(),
                 coors.new_empty((0,), dtype=torch.int32), coors.new_empty((0,), dtype=torch.int32))
     _require_cuda(feats, coors)
-    vf, vc, mp, cnt = ops().dynamic_scatter_forward(feats, coors.to(torch.int32), reduce_type)
+    ext = None if extents is None else [int(e) for e in extents]
+    vf, vc, mp, cnt = ops().dynamic_scatter_forward(feats, coors.to(torch.int32), reduce_type, ext)
     return vf, vc, mp, cnt
 
 

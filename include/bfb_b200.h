@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define BFB_ABI_VERSION 1
+#define BFB_ABI_VERSION 2
 
 typedef enum bfb_dtype {
   BFB_F32 = 0,
@@ -313,14 +313,18 @@ int bfb_hard_voxelize_status(const void* scratch_dev, int64_t n, int64_t batch,
  * are sized for the worst case (n voxels): out_feats [n, c] (dtype of feats),
  * out_coors [n, ndim], point2voxel [n] (-1 for ignored rows), counts [n];
  * the first *num_voxels rows are valid.  Synchronous: the voxel count is
- * returned on the host.  The packed lexicographic key of a row must fit in 31
- * bits (BFB_ERR_TOO_LARGE otherwise).
+ * returned on the host.  `extents` (HOST, ndim values, or NULL) bounds each
+ * column (0 <= coors[:, d] < extents[d]): with it the row keys are packed
+ * without a pass over the coordinates and one host read is saved; a valid
+ * row beyond an extent makes the call return BFB_ERR_DEVICE_STATUS.  The
+ * packed row key may be up to 62 bits wide (e.g. batched (b, x, y, z) rows
+ * on a 1440 x 1440 x 41 grid for any batch up to 2^30).
  * ---------------------------------------------------------------------- */
 int bfb_dynamic_scatter_workspace_size(int64_t n, int64_t c, int64_t ndim, size_t* bytes);
 
 int bfb_dynamic_scatter_forward(const void* feats_dev, int dtype, const int32_t* coors_dev, int64_t n,
-                                int64_t c, int64_t ndim, int reduce, void* out_feats_dev,
-                                int32_t* out_coors_dev, int32_t* point2voxel_dev,
+                                int64_t c, int64_t ndim, int reduce, const int64_t* extents,
+                                void* out_feats_dev, int32_t* out_coors_dev, int32_t* point2voxel_dev,
                                 int32_t* counts_dev, int64_t* num_voxels, void* ws_dev,
                                 size_t ws_bytes, void* stream);
 

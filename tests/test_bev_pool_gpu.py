@@ -271,3 +271,40 @@ def test_backward_gather_equals_scatter(cuda, case, fdtype):
     rgrad = oracle.bev_pool_backward(up.float().cpu().numpy(), coords.numpy(), B, D, H, W)
     np.testing.assert_array_equal(g_gather.float().cpu().numpy(), rgrad)
     assert torch.equal(g_gather, g_scatter)
+
+
+def test_torch_compile_fullgraph_matches_eager(cuda):
+    """bev_pool forward + backward under torch.compile(fullgraph=True): the
+    custom ops trace through their fake kernels and registered backward, and
+    the compiled step returns what eager returns, bit for bit."""
+    feats, coords = rand_bev_case(20000, 80, 2, 1, 40, 40, seed=31)
+    feats, coords = feats.cuda(), coords.cuda()
+    up = torch.randn((2, 80, 1, 40, 40), generator=torch.Generator().manual_seed(1)).cuda()
+
+    def pool(x, c):
+        return bev_pool(x, c, 2, 1, 40, 40)
+
+    torch._dynamo.reset()
+    compiled = torch.compile(pool, fullgraph=True)
+    results = []
+    for fn in (pool, compiled):  # AOTAutograd compiles the backward graph as well
+        x = feats.clone().requires_grad_(True)
+        out = fn(x, coords)
+        (out * up).sum().backward()
+        results.append((out.detach(), x.grad))
+    (a, ga), (b, gb) = results
+    assert torch.equal(a, b) and torch.equal(ga, gb)
+
+
+def test_opcheck_bev_pool_ops(cuda):
+    """torch.library.opcheck: schema (mutation / aliasing), fake kernel
+    against the real one, autograd registration."""
+    feats, coords = rand_bev_case(3000, 16, 1, 1, 20, 20, seed=32)
+    feats, coords = feats.cuda().requires_grad_(True), coords.cuda()
+    utils = ('test_schema', 'test_faketensor', 'test_autograd_registration')
+    O = torch.ops.bfb_b200
+    torch.library.opcheck(O.bev_pool_forward, (feats, coords, 1, 1, 20, 20), test_utils=utils)
+    plan = O.bev_pool_plan(coords, 1, 1, 20, 20)
+    torch.library.opcheck(O.bev_pool_forward_planned, (feats, plan, 1, 1, 20, 20), test_utils=utils)
+    g = torch.randn((1, 16, 1, 20, 20), device='cuda')
+    torch.library.opcheck(O.bev_pool_backward, (g, plan, 3000, 1, 1, 20, 20), test_utils=utils)

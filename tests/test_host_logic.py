@@ -34,7 +34,7 @@ def test_cabi_exports_every_declared_symbol(cabi):
 
 
 def test_version_and_status_strings(cabi):
-    assert cabi.bfb_abi_version() == 1
+    assert cabi.bfb_abi_version() == 2
     cabi.bfb_status_string.restype = ctypes.c_char_p
     assert cabi.bfb_status_string(0) == b'ok'
     assert cabi.bfb_status_string(-3).startswith(b'workspace')

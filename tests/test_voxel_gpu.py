@@ -220,3 +220,77 @@ def test_dynamic_scatter_module(cuda, golden):
     fb = torch.cat([f, f * 2])
     ob, ocb = m(fb, cb)
     assert ob.shape[0] == 2 * b[0].shape[0] and torch.equal(ocb[:, 1:], torch.cat([b[1], b[1]]))
+
+
+def _lidar_rows(samples):
+    """(b, x, y, z) int32 rows and 5 features of `samples` LiDAR clouds on
+    the config-3 grid (out-of-range points keep their -1 rows)."""
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    feats, rows = [], []
+    for b in range(samples):
+        p = synth.lidar_sweeps(b).cuda()
+        c = torch.empty((p.size(0), 3), dtype=torch.int32, device='cuda')
+        dynamic_voxelize(p, c, vs, cr, 3)
+        rows.append(torch.cat((torch.full((p.size(0), 1), b, dtype=torch.int32, device='cuda'), c), 1))
+        feats.append(p)
+    return torch.cat(feats), torch.cat(rows)
+
+
+@pytest.mark.parametrize('red', ['sum', 'mean', 'max'])
+def test_dynamic_scatter_batch16_wide_keys(cuda, red):
+    """16 samples of (b, x, y, z) rows on the 1440 x 1440 x 40 grid need a
+    32-bit row key (4 + 11 + 11 + 6 bits), past the one-word sort: the wide
+    path must equal sample-by-sample calls (one-word keys) bit for bit,
+    forward and backward, and so must the single module call."""
+    feats, rows = _lidar_rows(16)
+    x = feats.clone().requires_grad_(True)
+    vf, vc = dynamic_scatter(x, rows, red)
+    up = torch.randn(vf.shape, generator=torch.Generator().manual_seed(2)).cuda()
+    (vf * up).sum().backward()
+    wf, wc, wg, off = [], [], torch.zeros_like(feats), 0
+    for b in range(16):
+        sel = torch.nonzero(rows[:, 0] == b).squeeze(1)
+        xb = feats[sel].clone().requires_grad_(True)
+        f, c = dynamic_scatter(xb, rows[sel, 1:], red)
+        (f * up[off:off + f.size(0)]).sum().backward()
+        off += f.size(0)
+        wf.append(f.detach())
+        wc.append(torch.cat((torch.full((c.size(0), 1), b, dtype=torch.int32, device='cuda'), c), 1))
+        wg[sel] = xb.grad
+    assert off == vf.size(0)
+    assert torch.equal(vc, torch.cat(wc)) and torch.equal(vf.detach(), torch.cat(wf))
+    assert torch.equal(x.grad, wg)
+    m = DynamicScatter(list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE), average_points=(red == 'mean'))
+    if red in ('mean', 'max'):
+        mf, mc = m(feats, rows)
+        assert torch.equal(mf, vf.detach()) and torch.equal(mc, vc)
+
+
+def test_dynamic_scatter_extents(cuda):
+    """Known extents pack the keys without the coordinate pass: same result;
+    a valid row beyond an extent is refused."""
+    feats, rows = _lidar_rows(3)
+    a = dynamic_point_to_voxel_forward(feats, rows, 'mean')
+    b = dynamic_point_to_voxel_forward(feats, rows, 'mean', extents=[3, 1440, 1440, 40])
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    with pytest.raises(ValueError, match='beyond the given extents'):
+        dynamic_point_to_voxel_forward(feats, rows, 'mean', extents=[2, 1440, 1440, 40])
+
+
+def test_opcheck_voxel_ops(cuda):
+    """torch.library.opcheck on the voxel ops: the schemas declare exactly
+    the buffers the kernels write, and the fake kernels match."""
+    O = torch.ops.bfb_b200
+    pts = synth.lidar_sweeps(0)[:5000].cuda()
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    coors = torch.empty((5000, 3), dtype=torch.int32, device='cuda')
+    torch.library.opcheck(O.dynamic_voxelize, (pts, coors, vs, cr), test_utils=('test_schema', 'test_faketensor'))
+    vox = torch.zeros((4000, 10, 5), device='cuda')
+    co = torch.zeros((4000, 3), dtype=torch.int32, device='cuda')
+    num = torch.zeros((4000,), dtype=torch.int32, device='cuda')
+    torch.library.opcheck(O.hard_voxelize, (pts, vox, co, num, vs, cr, 10, 4000, True), test_utils=('test_schema',))
+    f = torch.randn((5000, 8), device='cuda', requires_grad=True)
+    c = torch.randint(0, 20, (5000, 3), dtype=torch.int32, device='cuda')
+    torch.library.opcheck(O.dynamic_scatter_forward, (f, c, 'max', None),
+                          test_utils=('test_schema', 'test_autograd_registration'))
