@@ -392,7 +392,8 @@ void hard_voxelize_batch(const at::Tensor& points_in, c10::ArrayRef<int64_t> off
   auto vs = as_floats(voxel_size, 3, "voxel_size");
   auto cr = as_floats(coors_range, 6, "coors_range");
   size_t table_b = 0, scratch_b = 0;
-  check(bfb_hard_voxelize_workspace_sizes(n, batch, &table_b, &scratch_b), "hard_voxelize workspace query");
+  check(bfb_hard_voxelize_workspace_sizes(n, batch, max_points, &table_b, &scratch_b),
+        "hard_voxelize workspace query");
   void* st = stream_of(points);
   auto table = table_for(points, table_b, st);
   auto scratch = at::empty({(int64_t)scratch_b}, points.options().dtype(at::kByte));

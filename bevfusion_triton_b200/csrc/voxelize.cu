@@ -9,7 +9,26 @@
 //                                                 its first max_points points in input
 //                                                 order, buffers zero-filled
 //
-// Pipeline for a batch of samples (one launch per stage for the whole batch):
+// Fast pipeline (max_points <= kFastMaxP), five launches for a whole batch:
+//   vox_fast_insert   cell + 64-bit key (sample, cell) per point; warp-aggregated insert
+//                     into the open-addressing table (first point by atomicMin); the
+//                     thread that creates a slot takes a dense voxel number d from a
+//                     counter and empties row d of the member table
+//   vox_fast_members  per point: d and the "first point" flag; the point index goes into
+//                     row d of the member table, which keeps the P smallest indices of
+//                     the voxel in ascending order (an atomicMin insertion chain: each
+//                     slot keeps the smaller of what it holds and what arrives and passes
+//                     the larger on, so slot j ends with the (j+1)-th smallest index
+//                     whatever the arrival order); per-tile flag counts, per-sample
+//                     voxel counts
+//   vox_fast_scan     one CTA: exclusive scans of the tile counts and the sample counts,
+//                     voxel_num
+//   vox_fast_assign   per tile: the exclusive scan of the flags numbers every voxel by
+//                     its first point, which writes the voxel's coords and count, notes
+//                     its output row and frees its table slot
+//   vox_fast_copy     a thread per output element of the kept voxels: the P rows
+//                     gathered through the member table, zero padding, written in order
+// General pipeline (any max_points, including -1), one launch per stage:
 //   vox_insert   cell + 64-bit key (sample, cell) per point; warp-aggregated insert into
 //                an open-addressing table that records the voxel's first point
 //                (atomicMin) and its point count
@@ -29,6 +48,7 @@
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
 #include <cmath>
+#include <vector>
 
 #include "scan.cuh"
 
@@ -104,6 +124,55 @@ size_t carve_scratch(void* base, int64_t n, int64_t batch, VoxScratch* v) {
   v->scan = c.take<uint32_t>(scan_scratch_elems(n + 1));
   v->err = c.take<uint32_t>(4);
   return c.bytes();
+}
+
+constexpr int kFastMaxP = 64;              // the member table holds up to 64 indices per voxel
+constexpr uint32_t kEmptyMember = 0xffffffffu;
+constexpr int kFastThreads = 256;          // one point per thread; a tile is one CTA's points
+
+// Member-table row stride (uint32): P rounded up to whole 16-byte vectors.
+inline int64_t member_stride(int64_t P) { return (P + 3) / 4 * 4; }
+
+struct FastTile;
+
+struct FastScratch {
+  uint32_t* hdr;           // [16] zeroed per call: 0 dense-voxel counter, 1 table full
+  FastTile* tiles;         // [tiles]
+  int32_t* sample_tiles;   // [batch] first tile of every sample (-1: no points)
+  uint32_t* bsum;          // [tiles + 1] first points per tile, then their exclusive scan
+  int32_t* did;            // [n] table slot of every point, -1 out of range
+  int32_t* sd;             // [n] table slot of dense voxel d
+  int2* rec;               // [n] (tile, rank among the tile's first points) of dense voxel d
+  uint32_t* mem;           // [n * member_stride(P)] member table
+};
+
+// Tiles of the fast pipeline: every sample cut into runs of kFastThreads
+// points; at most one partial tile per sample.
+int64_t fast_tiles(const int64_t* offs, int64_t batch) {
+  int64_t t = 0;
+  for (int64_t s = 0; s < batch; ++s) t += ceil_div(offs[s + 1] - offs[s], kFastThreads);
+  return t;
+}
+int64_t fast_tiles_bound(int64_t n, int64_t batch) { return n / kFastThreads + batch; }
+
+size_t carve_fast(void* base, int64_t n, int64_t batch, int64_t P, FastScratch* v) {
+  const int64_t tiles = fast_tiles_bound(n, batch);
+  Carver c(base);
+  v->hdr = c.take<uint32_t>(16);
+  // tile descriptors and the sample -> first tile table are uploaded as one block
+  v->tiles = reinterpret_cast<FastTile*>(c.take<int64_t>(3 * (size_t)tiles + ((size_t)batch + 1) / 2));
+  v->sample_tiles = v->tiles ? reinterpret_cast<int32_t*>(reinterpret_cast<int64_t*>(v->tiles) + 3 * tiles) : nullptr;
+  v->bsum = c.take<uint32_t>((size_t)tiles + 1);
+  v->did = c.take<int32_t>((size_t)n);
+  v->sd = c.take<int32_t>((size_t)n);
+  v->rec = c.take<int2>((size_t)n);
+  v->mem = c.take<uint32_t>((size_t)n * (size_t)member_stride(P));
+  return c.bytes();
+}
+
+bool fast_path(int64_t max_points, int64_t batch) {
+  (void)batch;
+  return max_points > 0 && max_points <= kFastMaxP;
 }
 
 struct Grid {
@@ -460,6 +529,232 @@ __global__ void vox_zero_tail_kernel(const int32_t* __restrict__ voxel_num, int6
   }
 }
 
+// ---------------------------------------------------------------------------
+// fast pipeline (max_points <= kFastMaxP)
+// ---------------------------------------------------------------------------
+// A tile is up to kFastThreads consecutive points of ONE sample (the host
+// cuts every sample into tiles), so a CTA knows its sample without a search
+// and voxel numbers, which restart at 0 in each sample, are differences of
+// one global scan over the tiles.
+struct FastTile {
+  int64_t start;  // first point
+  int32_t count;  // points
+  int32_t sample;
+  int32_t head;   // tile index of the sample's first tile
+  int32_t last;   // tile index of the sample's last tile
+};
+
+template <class T>
+__global__ __launch_bounds__(kFastThreads) void vox_fast_insert_kernel(
+    const T* __restrict__ pts, int64_t f, Grid gr, const FastTile* __restrict__ tiles, TableView tb, int64_t ps,
+    int32_t* __restrict__ did, int32_t* __restrict__ sd, uint32_t* __restrict__ mem, uint32_t* hdr) {
+  const FastTile tl = tiles[blockIdx.x];
+  const int64_t p = tl.start + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool in = (int)threadIdx.x < tl.count;
+  bool valid = false;
+  uint64_t key = kEmptyKey;
+  if (in) {
+    float xyz[3];
+    load_xyz<T>(pts, p, f, xyz);
+    int32_t c[3];
+    if (cell_of(xyz, gr, c)) {
+      valid = true;
+      const uint64_t lin = ((uint64_t)c[0] * (uint64_t)gr.g[1] + (uint64_t)c[1]) * (uint64_t)gr.g[2] + (uint64_t)c[2];
+      key = ((uint64_t)tl.sample << kLinBits) | lin;
+    }
+  }
+  // a run of neighbouring lanes on the same voxel inserts once, by its first
+  // (smallest) point
+  const uint64_t prev = __shfl_up_sync(0xffffffffu, key, 1);
+  const unsigned heads = __ballot_sync(0xffffffffu, lane == 0 || prev != key);
+  const int leader = 31 - __clz(heads & (lanemask_lt() | (1u << lane)));
+  int64_t slot = -1;
+  bool created = false;
+  if (valid && lane == leader) {
+    const uint64_t mask = tb.cap - 1;
+    uint64_t h = mix64(key) & mask;
+    for (uint64_t probe = 0; probe < tb.cap; ++probe) {
+      uint64_t k = tb.slots[h].key;
+      if (k == kEmptyKey) {
+        k = atomicCAS(&tb.slots[h].key, kEmptyKey, (unsigned long long)key);
+        created = k == kEmptyKey;
+      }
+      if (k == kEmptyKey || k == key) {
+        slot = (int64_t)h;
+        break;
+      }
+      h = (h + 1) & mask;
+    }
+    if (slot >= 0)
+      atomicMin(&tb.slots[slot].first, (uint32_t)p);
+    else
+      atomicAdd(hdr + 1, 1u);  // table full: cannot happen when cap >= 2n
+  }
+  // creators take dense voxel numbers: one shared atomic per warp, one
+  // global atomic per block (a single global counter per point would serialise)
+  __shared__ uint32_t s_new, s_base;
+  if (threadIdx.x == 0) s_new = 0u;
+  __syncthreads();
+  const unsigned cm = __ballot_sync(0xffffffffu, created);
+  uint32_t wbase = 0;
+  if (lane == 0 && cm) wbase = atomicAdd(&s_new, (uint32_t)__popc(cm));
+  wbase = __shfl_sync(0xffffffffu, wbase, 0);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_new) s_base = atomicAdd(hdr, s_new);
+  __syncthreads();
+  if (created) {  // number the voxel and empty its member row
+    const uint32_t d = s_base + wbase + (uint32_t)__popc(cm & lanemask_lt());
+    tb.slots[slot].gvid = (int32_t)d;
+    sd[d] = (int32_t)slot;
+    uint4* row = reinterpret_cast<uint4*>(mem + (int64_t)d * ps);
+    for (int64_t q = 0; q < ps / 4; ++q) row[q] = make_uint4(kEmptyMember, kEmptyMember, kEmptyMember, kEmptyMember);
+  }
+  slot = __shfl_sync(0xffffffffu, slot, leader);
+  if (in) did[p] = valid ? (int32_t)slot : -1;
+}
+
+// Insert point index v into a voxel's member row (ascending, kEmptyMember
+// past the filled slots).  Slot j keeps min(held, arriving) and passes the
+// larger on, so after every insertion the row holds the P smallest indices
+// in order, whatever the order of arrival.  Row values only ever decrease, so
+// a slot whose value (read before the chain) is already below v is passed
+// without an atomic.
+__device__ __forceinline__ void insert_smallest(uint32_t* __restrict__ row, int P, uint32_t v) {
+  const uint4* row4 = reinterpret_cast<const uint4*>(row);
+  for (int q = 0; 4 * q < P; ++q) {
+    const uint4 w = __ldcg(row4 + q);  // L2, where the atomics act
+    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = 4 * q + i;
+      if (j >= P) return;
+      if (a[i] < v) continue;  // slot j keeps a smaller index
+      const uint32_t old = atomicMin(row + j, v);
+      if (old == kEmptyMember) return;
+      v = max(old, v);
+    }
+  }
+}
+
+// Per point: its voxel's dense number d; its index goes into the voxel's
+// member row (the P smallest, see insert_smallest).  The voxel's first point
+// records (tile, rank among the tile's first points) for the copy kernel.
+// Per tile: the number of first points.
+__global__ __launch_bounds__(kFastThreads) void vox_fast_members_kernel(
+    const int32_t* __restrict__ did, const VoxSlot* __restrict__ slots, uint32_t* __restrict__ mem, int64_t ps, int P,
+    const FastTile* __restrict__ tiles, uint32_t* __restrict__ bsum, int2* __restrict__ rec) {
+  __shared__ uint32_t s_ws[kFastThreads / 32];
+  const FastTile tl = tiles[blockIdx.x];
+  const int64_t p = tl.start + threadIdx.x;
+  int32_t d = -1;
+  bool first = false;
+  if ((int)threadIdx.x < tl.count) {
+    const int32_t sl = __ldg(did + p);
+    if (sl >= 0) {
+      d = slots[sl].gvid;
+      first = slots[sl].first == (uint32_t)p;
+    }
+  }
+  uint32_t total;
+  const uint32_t excl = block_exclusive_scan(first ? 1u : 0u, s_ws, &total);
+  if (first) rec[d] = make_int2((int)blockIdx.x, (int)excl);
+  if (threadIdx.x == 0) bsum[blockIdx.x] = total;
+  // at most P points of one voxel per warp can be among its P smallest
+  const unsigned peers = __match_any_sync(0xffffffffu, d);
+  if (d >= 0 && __popc(peers & lanemask_lt()) < P) insert_smallest(mem + (int64_t)d * ps, P, (uint32_t)p);
+}
+
+// One CTA: bsum -> exclusive scan over all tiles; voxel_num of every sample =
+// its tiles' first points (difference of the scan at its last and first tile),
+// capped at max_voxels.
+constexpr int kFastScanThreads = 1024;
+__global__ __launch_bounds__(kFastScanThreads) void vox_fast_scan_kernel(uint32_t* __restrict__ bsum, int64_t ntiles,
+                                                                         const FastTile* __restrict__ tiles,
+                                                                         const int32_t* __restrict__ sample_tiles,
+                                                                         int batch, int64_t max_voxels,
+                                                                         int32_t* __restrict__ voxel_num) {
+  __shared__ uint32_t ws[kFastScanThreads / 32];
+  constexpr int kItems = 8;
+  uint32_t carry = 0;
+  for (int64_t b0 = 0; b0 <= ntiles; b0 += (int64_t)kFastScanThreads * kItems) {  // bsum[ntiles] = grand total
+    uint32_t v[kItems];
+    uint32_t s = 0;
+    const int64_t q0 = b0 + (int64_t)threadIdx.x * kItems;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      v[i] = q0 + i < ntiles ? bsum[q0 + i] : 0u;
+      s += v[i];
+    }
+    uint32_t total;
+    uint32_t pre = block_exclusive_scan(s, ws, &total) + carry;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      if (q0 + i <= ntiles) bsum[q0 + i] = pre;
+      pre += v[i];
+    }
+    carry += total;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < batch; s += kFastScanThreads) {
+    const int t0 = sample_tiles[s];  // -1: a sample without points
+    int64_t c = 0;
+    if (t0 >= 0) c = (int64_t)bsum[tiles[t0].last + 1] - (int64_t)bsum[t0];
+    voxel_num[s] = (int32_t)(max_voxels < 0 ? c : min(c, max_voxels));
+  }
+}
+
+// A thread per (voxel, point slot) over the voxels' dense numbers: the voxel's
+// number within its sample comes from its first point's record and the tile
+// scan; a kept voxel's slot copies its point row through the member table
+// (zeros past the voxel's points) and slot 0 writes the coords (decoded from
+// the table key) and the count, then frees the table slot, dropped voxels
+// included.
+template <class T>
+__global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
+    const T* __restrict__ pts, int64_t f, Grid gr, const uint32_t* __restrict__ mem, int64_t ps, int P,
+    const int2* __restrict__ rec, const FastTile* __restrict__ tiles, const uint32_t* __restrict__ bsum,
+    const int32_t* __restrict__ sd, const uint32_t* __restrict__ hdr, TableView tb, int64_t max_voxels,
+    T* __restrict__ voxels, int32_t* __restrict__ coors, int32_t* __restrict__ num_points) {
+  const uint64_t items = (uint64_t)hdr[0] * (uint64_t)P;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += stride) {
+    const uint32_t d = (uint32_t)(i / (uint64_t)P);
+    const int j = (int)(i - (uint64_t)d * (uint64_t)P);
+    const int2 rc = __ldg(rec + d);
+    const FastTile& tl = tiles[rc.x];
+    const int64_t local = (int64_t)__ldg(bsum + rc.x) - (int64_t)__ldg(bsum + tl.head) + rc.y;
+    const bool kept = max_voxels < 0 || local < max_voxels;
+    const int64_t r = (int64_t)tl.sample * max_voxels + local;
+    const uint32_t* row = mem + (int64_t)d * ps;
+    if (kept) {
+      const uint32_t m = __ldg(row + j);
+      T* dst = voxels + (r * P + j) * f;
+      if (m != kEmptyMember) {
+        const T* src = pts + (int64_t)m * f;
+        for (int64_t q = 0; q < f; ++q) dst[q] = __ldg(src + q);
+      } else {
+        for (int64_t q = 0; q < f; ++q) dst[q] = from_f32<T>(0.f);
+      }
+    }
+    if (j == 0) {
+      VoxSlot& sl = tb.slots[__ldg(sd + d)];
+      if (kept) {
+        int cnt = 0;
+        for (int q = 0; q < P; ++q) cnt += __ldg(row + q) != kEmptyMember ? 1 : 0;
+        num_points[r] = cnt;
+        const uint64_t lin = sl.key & ((1ull << kLinBits) - 1ull);
+        const uint64_t yz = (uint64_t)gr.g[1] * (uint64_t)gr.g[2];
+        coors[3 * r + 0] = (int32_t)(lin / yz);
+        coors[3 * r + 1] = (int32_t)((lin % yz) / (uint64_t)gr.g[2]);
+        coors[3 * r + 2] = (int32_t)(lin % (uint64_t)gr.g[2]);
+      }
+      sl.key = kEmptyKey;  // leave the table clean for the next call
+      sl.first = kNoFirst;
+    }
+  }
+}
+
 // every slot free: key empty, no first point, count 0
 __global__ void vox_table_init_kernel(TableView tb) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -525,6 +820,58 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
   return BFB_OK;
 }
 
+template <class T>
+int hard_voxelize_fast(const void* points, int64_t n, int64_t f, const Grid& gr, const int64_t* offs_host,
+                       int64_t batch, int64_t max_points, int64_t max_voxels, void* voxels, int32_t* coors,
+                       int32_t* num_points, int32_t* voxel_num, int zero_tail, const TableView& tb,
+                       const FastScratch& fv, cudaStream_t st) {
+  const T* pts = static_cast<const T*>(points);
+  const int P = (int)max_points;
+  const int64_t ps = member_stride(P);
+  const int64_t MV = max_voxels < 0 ? n : max_voxels;
+  const int64_t tiles = fast_tiles(offs_host, batch);
+  const int64_t bound = fast_tiles_bound(n, batch);  // the scratch layout's tile capacity
+  // tile descriptors, then the first tile of every sample, in one upload
+  std::vector<int64_t> up((size_t)(3 * bound + (batch + 1) / 2), 0);
+  FastTile* tl = reinterpret_cast<FastTile*>(up.data());
+  int32_t* first_tile = reinterpret_cast<int32_t*>(up.data() + 3 * bound);
+  for (int64_t s = 0, t = 0; s < batch; ++s) {
+    const int64_t head = t;
+    const int64_t nt = ceil_div(offs_host[s + 1] - offs_host[s], kFastThreads);
+    first_tile[s] = nt > 0 ? (int32_t)head : -1;
+    for (int64_t a = offs_host[s]; a < offs_host[s + 1]; a += kFastThreads, ++t)
+      tl[t] = FastTile{a, (int32_t)std::min<int64_t>(kFastThreads, offs_host[s + 1] - a), (int32_t)s, (int32_t)head,
+                       (int32_t)(head + nt - 1)};
+  }
+  // a pageable host source: the copy is staged before the call returns
+  BFB_CUDA(cudaMemcpyAsync(fv.tiles, up.data(), sizeof(int64_t) * up.size(), cudaMemcpyHostToDevice, st));
+  BFB_CUDA(cudaMemsetAsync(fv.hdr, 0, sizeof(uint32_t) * 16, st));
+  if (tiles > 0) {
+    vox_fast_insert_kernel<T><<<(unsigned)tiles, kFastThreads, 0, st>>>(pts, f, gr, fv.tiles, tb, ps, fv.did, fv.sd,
+                                                                        fv.mem, fv.hdr);
+    BFB_CHECK_LAUNCH();
+    vox_fast_members_kernel<<<(unsigned)tiles, kFastThreads, 0, st>>>(fv.did, tb.slots, fv.mem, ps, P, fv.tiles,
+                                                                      fv.bsum, fv.rec);
+    BFB_CHECK_LAUNCH();
+  }
+  vox_fast_scan_kernel<<<1, kFastScanThreads, 0, st>>>(fv.bsum, tiles, fv.tiles, fv.sample_tiles, (int)batch, MV,
+                                                       voxel_num);
+  BFB_CHECK_LAUNCH();
+  if (tiles > 0) {
+    vox_fast_copy_kernel<T><<<148 * 16, kFastThreads, 0, st>>>(pts, f, gr, fv.mem, ps, P, fv.rec, fv.tiles, fv.bsum,
+                                                              fv.sd, fv.hdr, tb, MV, static_cast<T*>(voxels), coors,
+                                                              num_points);
+    BFB_CHECK_LAUNCH();
+  }
+  if (zero_tail) {
+    dim3 grid((unsigned)std::min<int64_t>(ceil_div(MV * max_points * f, 256), 4096), (unsigned)batch);
+    vox_zero_tail_kernel<T><<<grid, 256, 0, st>>>(voxel_num, MV, max_points * f, static_cast<T*>(voxels), coors,
+                                                  num_points);
+    BFB_CHECK_LAUNCH();
+  }
+  return BFB_OK;
+}
+
 int check_common(const void* points, int dtype, int64_t n, int64_t f) {
   if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (n < 0 || f < 3) return BFB_ERR_INVALID_ARG;
@@ -556,13 +903,23 @@ extern "C" int bfb_dynamic_voxelize(const void* points, int dtype, int64_t n, in
   return BFB_OK;
 }
 
-extern "C" int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, size_t* table_bytes, size_t* scratch_bytes) {
-  if (n < 0 || batch < 1) return BFB_ERR_INVALID_ARG;
+// Scratch of one call: the fast pipeline's layout when max_points allows it.
+size_t scratch_bytes_for(int64_t n, int64_t batch, int64_t max_points) {
+  if (fast_path(max_points, batch)) {
+    FastScratch fv;
+    return carve_fast(nullptr, n, batch, max_points, &fv);
+  }
+  VoxScratch sv;
+  return carve_scratch(nullptr, n, batch, &sv);
+}
+
+extern "C" int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, int64_t max_points, size_t* table_bytes,
+                                                 size_t* scratch_bytes) {
+  if (n < 0 || batch < 1 || max_points == 0 || max_points < -1) return BFB_ERR_INVALID_ARG;
   if (n > 0x7ffffffeLL || batch >= (1LL << (64 - kLinBits))) return BFB_ERR_TOO_LARGE;
   TableView tv;
-  VoxScratch sv;
   if (table_bytes) *table_bytes = carve_table(nullptr, table_cap_for_points(n), &tv);
-  if (scratch_bytes) *scratch_bytes = carve_scratch(nullptr, n, batch, &sv);
+  if (scratch_bytes) *scratch_bytes = scratch_bytes_for(n, batch, max_points);
   return BFB_OK;
 }
 
@@ -596,13 +953,28 @@ extern "C" int bfb_hard_voxelize_batch(const void* points, int dtype, const int6
   if (gr.g[0] > (1LL << kLinBits) / gr.g[1] / gr.g[2]) return BFB_ERR_TOO_LARGE;
   if ((max_points < 0 ? n : max_points) * f > 0x7fffffffLL) return BFB_ERR_TOO_LARGE;  // one voxel row
   const uint64_t cap = table_cap_for_bytes(table_bytes);
-  VoxScratch sv;
-  if (!table || !scratch || cap < (uint64_t)(2 * n) || carve_scratch(nullptr, n, batch, &sv) > scratch_bytes)
+  if (!table || !scratch || cap < (uint64_t)(2 * n) || scratch_bytes_for(n, batch, max_points) > scratch_bytes)
     return BFB_ERR_WORKSPACE;
   TableView tv;
   carve_table(table, cap, &tv);
-  carve_scratch(scratch, n, batch, &sv);
   cudaStream_t st = as_stream(stream);
+  if (fast_path(max_points, batch)) {
+    FastScratch fv;
+    carve_fast(scratch, n, batch, max_points, &fv);
+    switch (dtype) {
+      case BFB_F32:
+        return hard_voxelize_fast<float>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels, coors,
+                                         num_points, voxel_num, zero_tail, tv, fv, st);
+      case BFB_F16:
+        return hard_voxelize_fast<__half>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels, coors,
+                                          num_points, voxel_num, zero_tail, tv, fv, st);
+      default:
+        return hard_voxelize_fast<__nv_bfloat16>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels,
+                                                 coors, num_points, voxel_num, zero_tail, tv, fv, st);
+    }
+  }
+  VoxScratch sv;
+  carve_scratch(scratch, n, batch, &sv);
   switch (dtype) {
     case BFB_F32:
       return hard_voxelize_impl<float>(points, n, f, gr, offsets, batch, max_points, max_voxels, voxels, coors,
@@ -626,14 +998,22 @@ extern "C" int bfb_hard_voxelize(const void* points, int dtype, int64_t n, int64
                                  scratch_bytes, stream);
 }
 
-extern "C" int bfb_hard_voxelize_status(const void* scratch, int64_t n, int64_t batch, int64_t* table_full,
-                                        void* stream) {
+extern "C" int bfb_hard_voxelize_status(const void* scratch, int64_t n, int64_t batch, int64_t max_points,
+                                        int64_t* table_full, void* stream) {
   if (!scratch || !table_full || n < 0 || batch < 1) return BFB_ERR_INVALID_ARG;
-  VoxScratch sv;
-  carve_scratch(const_cast<void*>(scratch), n, batch, &sv);
+  const uint32_t* err = nullptr;
+  if (fast_path(max_points, batch)) {
+    FastScratch fv;
+    carve_fast(const_cast<void*>(scratch), n, batch, max_points, &fv);
+    err = fv.hdr + 1;  // table full
+  } else {
+    VoxScratch sv;
+    carve_scratch(const_cast<void*>(scratch), n, batch, &sv);
+    err = sv.err;
+  }
   uint32_t v = 0;
   cudaStream_t st = as_stream(stream);
-  BFB_CUDA(cudaMemcpyAsync(&v, sv.err, sizeof(v), cudaMemcpyDeviceToHost, st));
+  BFB_CUDA(cudaMemcpyAsync(&v, err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
   BFB_CUDA(cudaStreamSynchronize(st));
   *table_full = v;
   return BFB_OK;

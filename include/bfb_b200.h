@@ -266,9 +266,12 @@ int bfb_dynamic_voxelize(const void* points_dev, int points_dtype, int64_t n, in
  * bfb_hard_voxelize_table_init; every successful call leaves it clean, so it
  * can be reused call after call (re-initialise it after a failed call).  Its
  * capacity (from table_bytes) must be at least twice the point count of a
- * call.  `scratch` is only used during the call. */
-int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, size_t* table_bytes,
-                                      size_t* scratch_bytes);
+ * call.  `scratch` is only used during the call; its size depends on
+ * max_points (1 <= max_points <= 64 selects a four-launch pipeline whose
+ * member table keeps each voxel's max_points smallest point indices; other
+ * values use a general bucket pipeline). */
+int bfb_hard_voxelize_workspace_sizes(int64_t n, int64_t batch, int64_t max_points,
+                                      size_t* table_bytes, size_t* scratch_bytes);
 
 int bfb_hard_voxelize_table_init(void* table_dev, size_t table_bytes, void* stream);
 
@@ -298,7 +301,7 @@ int bfb_hard_voxelize_batch(const void* points_dev, int points_dtype, const int6
 /* Synchronously reads the device status of the last call that used this
  * scratch: *table_full = points whose insert found no free table slot
  * (always 0 when the table capacity rule above holds). */
-int bfb_hard_voxelize_status(const void* scratch_dev, int64_t n, int64_t batch,
+int bfb_hard_voxelize_status(const void* scratch_dev, int64_t n, int64_t batch, int64_t max_points,
                              int64_t* table_full, void* stream);
 
 /* ------------------------------------------------------------------------
