@@ -133,39 +133,33 @@ constexpr int kFastThreads = 256;          // one point per thread; a tile is on
 // Member-table row stride (uint32): P rounded up to whole 16-byte vectors.
 inline int64_t member_stride(int64_t P) { return (P + 3) / 4 * 4; }
 
-struct FastTile;
-
 struct FastScratch {
   uint32_t* hdr;           // [16] zeroed per call: 0 dense-voxel counter, 1 table full
-  FastTile* tiles;         // [tiles]
-  int32_t* sample_tiles;   // [batch] first tile of every sample (-1: no points)
+  int64_t* offs;           // [batch + 1] sample offsets, then
+  int64_t* tpre;           // [batch + 1] first tile of every sample (tpre[batch] = tiles): one upload
   uint32_t* bsum;          // [tiles + 1] first points per tile, then their exclusive scan
   int32_t* did;            // [n] table slot of every point, -1 out of range
   int32_t* sd;             // [n] table slot of dense voxel d
-  int2* rec;               // [n] (tile, rank among the tile's first points) of dense voxel d
+  int4* rec;               // [n] (tile, rank among the tile's first points, points) of dense voxel d
+  uint32_t* fill;          // [n] member slots claimed in a voxel of at most P points
   uint32_t* mem;           // [n * member_stride(P)] member table
 };
 
 // Tiles of the fast pipeline: every sample cut into runs of kFastThreads
-// points; at most one partial tile per sample.
-int64_t fast_tiles(const int64_t* offs, int64_t batch) {
-  int64_t t = 0;
-  for (int64_t s = 0; s < batch; ++s) t += ceil_div(offs[s + 1] - offs[s], kFastThreads);
-  return t;
-}
+// points, so at most one partial tile per sample.
 int64_t fast_tiles_bound(int64_t n, int64_t batch) { return n / kFastThreads + batch; }
 
 size_t carve_fast(void* base, int64_t n, int64_t batch, int64_t P, FastScratch* v) {
   const int64_t tiles = fast_tiles_bound(n, batch);
   Carver c(base);
   v->hdr = c.take<uint32_t>(16);
-  // tile descriptors and the sample -> first tile table are uploaded as one block
-  v->tiles = reinterpret_cast<FastTile*>(c.take<int64_t>(3 * (size_t)tiles + ((size_t)batch + 1) / 2));
-  v->sample_tiles = v->tiles ? reinterpret_cast<int32_t*>(reinterpret_cast<int64_t*>(v->tiles) + 3 * tiles) : nullptr;
+  v->offs = c.take<int64_t>(2 * ((size_t)batch + 1));
+  v->tpre = v->offs ? v->offs + batch + 1 : nullptr;
   v->bsum = c.take<uint32_t>((size_t)tiles + 1);
   v->did = c.take<int32_t>((size_t)n);
   v->sd = c.take<int32_t>((size_t)n);
-  v->rec = c.take<int2>((size_t)n);
+  v->rec = c.take<int4>((size_t)n);
+  v->fill = c.take<uint32_t>((size_t)n);
   v->mem = c.take<uint32_t>((size_t)n * (size_t)member_stride(P));
   return c.bytes();
 }
@@ -541,14 +535,31 @@ struct FastTile {
   int32_t count;  // points
   int32_t sample;
   int32_t head;   // tile index of the sample's first tile
-  int32_t last;   // tile index of the sample's last tile
 };
+
+// Tile t from the sample offsets and the first tile of every sample (the
+// sample is the last s with tpre[s] <= t; samples without points own no tile).
+__device__ __forceinline__ FastTile tile_of(int64_t t, const int64_t* __restrict__ offs,
+                                            const int64_t* __restrict__ tpre, int batch) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(tpre + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  FastTile tl;
+  tl.sample = lo;
+  tl.head = (int32_t)__ldg(tpre + lo);
+  tl.start = __ldg(offs + lo) + (t - tl.head) * kFastThreads;
+  tl.count = (int32_t)min((int64_t)kFastThreads, __ldg(offs + lo + 1) - tl.start);
+  return tl;
+}
 
 template <class T>
 __global__ __launch_bounds__(kFastThreads) void vox_fast_insert_kernel(
-    const T* __restrict__ pts, int64_t f, Grid gr, const FastTile* __restrict__ tiles, TableView tb, int64_t ps,
-    int32_t* __restrict__ did, int32_t* __restrict__ sd, uint32_t* __restrict__ mem, uint32_t* hdr) {
-  const FastTile tl = tiles[blockIdx.x];
+    const T* __restrict__ pts, int64_t f, Grid gr, const int64_t* __restrict__ offs, const int64_t* __restrict__ tpre,
+    int batch, TableView tb, int64_t ps, int32_t* __restrict__ did, int32_t* __restrict__ sd, uint32_t* __restrict__ mem,
+    uint32_t* __restrict__ fill, uint32_t* hdr) {
+  const FastTile tl = tile_of(blockIdx.x, offs, tpre, batch);
   const int64_t p = tl.start + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const bool in = (int)threadIdx.x < tl.count;
@@ -586,10 +597,14 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_insert_kernel(
       }
       h = (h + 1) & mask;
     }
-    if (slot >= 0)
+    if (slot >= 0) {
       atomicMin(&tb.slots[slot].first, (uint32_t)p);
-    else
+      const unsigned later = lane < 31 ? heads >> (lane + 1) : 0u;
+      const uint32_t run = later ? (uint32_t)__ffs(later) : (uint32_t)(32 - lane);
+      atomicAdd(&tb.slots[slot].cnt, run);  // points of the voxel
+    } else {
       atomicAdd(hdr + 1, 1u);  // table full: cannot happen when cap >= 2n
+    }
   }
   // creators take dense voxel numbers: one shared atomic per warp, one
   // global atomic per block (a single global counter per point would serialise)
@@ -609,6 +624,7 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_insert_kernel(
     sd[d] = (int32_t)slot;
     uint4* row = reinterpret_cast<uint4*>(mem + (int64_t)d * ps);
     for (int64_t q = 0; q < ps / 4; ++q) row[q] = make_uint4(kEmptyMember, kEmptyMember, kEmptyMember, kEmptyMember);
+    fill[d] = 0u;
   }
   slot = __shfl_sync(0xffffffffu, slot, leader);
   if (in) did[p] = valid ? (int32_t)slot : -1;
@@ -622,12 +638,16 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_insert_kernel(
 // without an atomic.
 __device__ __forceinline__ void insert_smallest(uint32_t* __restrict__ row, int P, uint32_t v) {
   const uint4* row4 = reinterpret_cast<const uint4*>(row);
-  for (int q = 0; 4 * q < P; ++q) {
-    const uint4 w = __ldcg(row4 + q);  // L2, where the atomics act
-    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+  for (int q0 = 0; 4 * q0 < P; q0 += 4) {
+    uint32_t a[16];  // up to four row vectors read together (L2, where the atomics act)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int j = 4 * q + i;
+    for (int u = 0; u < 4; ++u) {
+      const uint4 w = 4 * (q0 + u) < P ? __ldcg(row4 + q0 + u) : make_uint4(0u, 0u, 0u, 0u);
+      a[4 * u] = w.x; a[4 * u + 1] = w.y; a[4 * u + 2] = w.z; a[4 * u + 3] = w.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = 4 * q0 + i;
       if (j >= P) return;
       if (a[i] < v) continue;  // slot j keeps a smaller index
       const uint32_t old = atomicMin(row + j, v);
@@ -637,32 +657,43 @@ __device__ __forceinline__ void insert_smallest(uint32_t* __restrict__ row, int 
   }
 }
 
-// Per point: its voxel's dense number d; its index goes into the voxel's
-// member row (the P smallest, see insert_smallest).  The voxel's first point
-// records (tile, rank among the tile's first points) for the copy kernel.
-// Per tile: the number of first points.
+// Per point: its voxel's dense number d.  A voxel with at most P points
+// keeps all of them: each point claims a member slot with one atomicAdd, in
+// any order (the copy kernel ranks them).  A larger voxel keeps its P
+// smallest point indices, in order (insert_smallest).  The voxel's first
+// point records (tile, rank among the tile's first points, point count, sample) for
+// the copy kernel.  Per tile: the number of first points.
 __global__ __launch_bounds__(kFastThreads) void vox_fast_members_kernel(
-    const int32_t* __restrict__ did, const VoxSlot* __restrict__ slots, uint32_t* __restrict__ mem, int64_t ps, int P,
-    const FastTile* __restrict__ tiles, uint32_t* __restrict__ bsum, int2* __restrict__ rec) {
+    const int32_t* __restrict__ did, const VoxSlot* __restrict__ slots, uint32_t* __restrict__ mem,
+    uint32_t* __restrict__ fill, int64_t ps, int P, const int64_t* __restrict__ offs, const int64_t* __restrict__ tpre,
+    int batch, uint32_t* __restrict__ bsum, int4* __restrict__ rec) {
   __shared__ uint32_t s_ws[kFastThreads / 32];
-  const FastTile tl = tiles[blockIdx.x];
+  const FastTile tl = tile_of(blockIdx.x, offs, tpre, batch);
   const int64_t p = tl.start + threadIdx.x;
   int32_t d = -1;
+  uint32_t cnt = 0;
   bool first = false;
   if ((int)threadIdx.x < tl.count) {
     const int32_t sl = __ldg(did + p);
     if (sl >= 0) {
-      d = slots[sl].gvid;
-      first = slots[sl].first == (uint32_t)p;
+      const VoxSlot v = slots[sl];
+      d = v.gvid;
+      cnt = v.cnt;
+      first = v.first == (uint32_t)p;
     }
   }
   uint32_t total;
   const uint32_t excl = block_exclusive_scan(first ? 1u : 0u, s_ws, &total);
-  if (first) rec[d] = make_int2((int)blockIdx.x, (int)excl);
+  if (first) rec[d] = make_int4((int)blockIdx.x, (int)excl, (int)cnt, tl.sample);
   if (threadIdx.x == 0) bsum[blockIdx.x] = total;
-  // at most P points of one voxel per warp can be among its P smallest
-  const unsigned peers = __match_any_sync(0xffffffffu, d);
-  if (d >= 0 && __popc(peers & lanemask_lt()) < P) insert_smallest(mem + (int64_t)d * ps, P, (uint32_t)p);
+  uint32_t* row = mem + (int64_t)d * ps;
+  if (d >= 0 && cnt <= (uint32_t)P) {
+    row[atomicAdd(fill + d, 1u)] = (uint32_t)p;
+  }
+  // a larger voxel: at most P points of it per warp can be among its P smallest
+  const int32_t big = (d >= 0 && cnt > (uint32_t)P) ? d : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, big);
+  if (big >= 0 && __popc(peers & lanemask_lt()) < P) insert_smallest(row, P, (uint32_t)p);
 }
 
 // One CTA: bsum -> exclusive scan over all tiles; voxel_num of every sample =
@@ -670,8 +701,7 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_members_kernel(
 // capped at max_voxels.
 constexpr int kFastScanThreads = 1024;
 __global__ __launch_bounds__(kFastScanThreads) void vox_fast_scan_kernel(uint32_t* __restrict__ bsum, int64_t ntiles,
-                                                                         const FastTile* __restrict__ tiles,
-                                                                         const int32_t* __restrict__ sample_tiles,
+                                                                         const int64_t* __restrict__ tpre,
                                                                          int batch, int64_t max_voxels,
                                                                          int32_t* __restrict__ voxel_num) {
   __shared__ uint32_t ws[kFastScanThreads / 32];
@@ -697,23 +727,23 @@ __global__ __launch_bounds__(kFastScanThreads) void vox_fast_scan_kernel(uint32_
   }
   __syncthreads();
   for (int s = threadIdx.x; s < batch; s += kFastScanThreads) {
-    const int t0 = sample_tiles[s];  // -1: a sample without points
-    int64_t c = 0;
-    if (t0 >= 0) c = (int64_t)bsum[tiles[t0].last + 1] - (int64_t)bsum[t0];
+    const int64_t c = (int64_t)bsum[tpre[s + 1]] - (int64_t)bsum[tpre[s]];
     voxel_num[s] = (int32_t)(max_voxels < 0 ? c : min(c, max_voxels));
   }
 }
 
 // A thread per (voxel, point slot) over the voxels' dense numbers: the voxel's
 // number within its sample comes from its first point's record and the tile
-// scan; a kept voxel's slot copies its point row through the member table
-// (zeros past the voxel's points) and slot 0 writes the coords (decoded from
-// the table key) and the count, then frees the table slot, dropped voxels
-// included.
+// scan.  For a kept voxel, slot j's thread takes member j: in a voxel of at
+// most P points the members are unordered, so it moves to position = number of
+// smaller members; a larger voxel's members are already the P smallest in
+// order.  Positions past the voxel's points are zero.  Slot 0 writes the
+// coords (decoded from the table key) and the count, then frees the table
+// slot, dropped voxels included.
 template <class T>
 __global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
     const T* __restrict__ pts, int64_t f, Grid gr, const uint32_t* __restrict__ mem, int64_t ps, int P,
-    const int2* __restrict__ rec, const FastTile* __restrict__ tiles, const uint32_t* __restrict__ bsum,
+    const int4* __restrict__ rec, const int64_t* __restrict__ tpre, const uint32_t* __restrict__ bsum,
     const int32_t* __restrict__ sd, const uint32_t* __restrict__ hdr, TableView tb, int64_t max_voxels,
     T* __restrict__ voxels, int32_t* __restrict__ coors, int32_t* __restrict__ num_points) {
   const uint64_t items = (uint64_t)hdr[0] * (uint64_t)P;
@@ -721,27 +751,30 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += stride) {
     const uint32_t d = (uint32_t)(i / (uint64_t)P);
     const int j = (int)(i - (uint64_t)d * (uint64_t)P);
-    const int2 rc = __ldg(rec + d);
-    const FastTile& tl = tiles[rc.x];
-    const int64_t local = (int64_t)__ldg(bsum + rc.x) - (int64_t)__ldg(bsum + tl.head) + rc.y;
+    const int4 rc = __ldg(rec + d);
+    const int64_t local = (int64_t)__ldg(bsum + rc.x) - (int64_t)__ldg(bsum + __ldg(tpre + rc.w)) + rc.y;
     const bool kept = max_voxels < 0 || local < max_voxels;
-    const int64_t r = (int64_t)tl.sample * max_voxels + local;
+    const int64_t r = (int64_t)rc.w * max_voxels + local;
     const uint32_t* row = mem + (int64_t)d * ps;
+    const int cnt = min(rc.z, P);
     if (kept) {
-      const uint32_t m = __ldg(row + j);
-      T* dst = voxels + (r * P + j) * f;
-      if (m != kEmptyMember) {
+      T* dst = voxels + r * P * f;
+      if (j < cnt) {
+        const uint32_t m = __ldg(row + j);
+        int pos = j;
+        if (rc.z <= P) {  // unordered members: rank among them
+          pos = 0;
+          for (int q = 0; q < cnt; ++q) pos += __ldg(row + q) < m ? 1 : 0;
+        }
         const T* src = pts + (int64_t)m * f;
-        for (int64_t q = 0; q < f; ++q) dst[q] = __ldg(src + q);
+        for (int64_t q = 0; q < f; ++q) dst[pos * f + q] = __ldg(src + q);
       } else {
-        for (int64_t q = 0; q < f; ++q) dst[q] = from_f32<T>(0.f);
+        for (int64_t q = 0; q < f; ++q) dst[j * f + q] = from_f32<T>(0.f);
       }
     }
     if (j == 0) {
       VoxSlot& sl = tb.slots[__ldg(sd + d)];
       if (kept) {
-        int cnt = 0;
-        for (int q = 0; q < P; ++q) cnt += __ldg(row + q) != kEmptyMember ? 1 : 0;
         num_points[r] = cnt;
         const uint64_t lin = sl.key & ((1ull << kLinBits) - 1ull);
         const uint64_t yz = (uint64_t)gr.g[1] * (uint64_t)gr.g[2];
@@ -751,6 +784,7 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
       }
       sl.key = kEmptyKey;  // leave the table clean for the next call
       sl.first = kNoFirst;
+      sl.cnt = 0u;
     }
   }
 }
@@ -829,36 +863,29 @@ int hard_voxelize_fast(const void* points, int64_t n, int64_t f, const Grid& gr,
   const int P = (int)max_points;
   const int64_t ps = member_stride(P);
   const int64_t MV = max_voxels < 0 ? n : max_voxels;
-  const int64_t tiles = fast_tiles(offs_host, batch);
-  const int64_t bound = fast_tiles_bound(n, batch);  // the scratch layout's tile capacity
-  // tile descriptors, then the first tile of every sample, in one upload
-  std::vector<int64_t> up((size_t)(3 * bound + (batch + 1) / 2), 0);
-  FastTile* tl = reinterpret_cast<FastTile*>(up.data());
-  int32_t* first_tile = reinterpret_cast<int32_t*>(up.data() + 3 * bound);
-  for (int64_t s = 0, t = 0; s < batch; ++s) {
-    const int64_t head = t;
-    const int64_t nt = ceil_div(offs_host[s + 1] - offs_host[s], kFastThreads);
-    first_tile[s] = nt > 0 ? (int32_t)head : -1;
-    for (int64_t a = offs_host[s]; a < offs_host[s + 1]; a += kFastThreads, ++t)
-      tl[t] = FastTile{a, (int32_t)std::min<int64_t>(kFastThreads, offs_host[s + 1] - a), (int32_t)s, (int32_t)head,
-                       (int32_t)(head + nt - 1)};
+  // sample offsets and the first tile of every sample, in one small upload
+  std::vector<int64_t> up((size_t)(2 * (batch + 1)));
+  int64_t tiles = 0;
+  for (int64_t s = 0; s <= batch; ++s) {
+    up[(size_t)s] = offs_host[s];
+    up[(size_t)(batch + 1 + s)] = tiles;
+    if (s < batch) tiles += ceil_div(offs_host[s + 1] - offs_host[s], kFastThreads);
   }
   // a pageable host source: the copy is staged before the call returns
-  BFB_CUDA(cudaMemcpyAsync(fv.tiles, up.data(), sizeof(int64_t) * up.size(), cudaMemcpyHostToDevice, st));
+  BFB_CUDA(cudaMemcpyAsync(fv.offs, up.data(), sizeof(int64_t) * up.size(), cudaMemcpyHostToDevice, st));
   BFB_CUDA(cudaMemsetAsync(fv.hdr, 0, sizeof(uint32_t) * 16, st));
   if (tiles > 0) {
-    vox_fast_insert_kernel<T><<<(unsigned)tiles, kFastThreads, 0, st>>>(pts, f, gr, fv.tiles, tb, ps, fv.did, fv.sd,
-                                                                        fv.mem, fv.hdr);
+    vox_fast_insert_kernel<T><<<(unsigned)tiles, kFastThreads, 0, st>>>(pts, f, gr, fv.offs, fv.tpre, (int)batch, tb, ps,
+                                                                        fv.did, fv.sd, fv.mem, fv.fill, fv.hdr);
     BFB_CHECK_LAUNCH();
-    vox_fast_members_kernel<<<(unsigned)tiles, kFastThreads, 0, st>>>(fv.did, tb.slots, fv.mem, ps, P, fv.tiles,
-                                                                      fv.bsum, fv.rec);
+    vox_fast_members_kernel<<<(unsigned)tiles, kFastThreads, 0, st>>>(fv.did, tb.slots, fv.mem, fv.fill, ps, P,
+                                                                      fv.offs, fv.tpre, (int)batch, fv.bsum, fv.rec);
     BFB_CHECK_LAUNCH();
   }
-  vox_fast_scan_kernel<<<1, kFastScanThreads, 0, st>>>(fv.bsum, tiles, fv.tiles, fv.sample_tiles, (int)batch, MV,
-                                                       voxel_num);
+  vox_fast_scan_kernel<<<1, kFastScanThreads, 0, st>>>(fv.bsum, tiles, fv.tpre, (int)batch, MV, voxel_num);
   BFB_CHECK_LAUNCH();
   if (tiles > 0) {
-    vox_fast_copy_kernel<T><<<148 * 16, kFastThreads, 0, st>>>(pts, f, gr, fv.mem, ps, P, fv.rec, fv.tiles, fv.bsum,
+    vox_fast_copy_kernel<T><<<148 * 16, kFastThreads, 0, st>>>(pts, f, gr, fv.mem, ps, P, fv.rec, fv.tpre, fv.bsum,
                                                               fv.sd, fv.hdr, tb, MV, static_cast<T*>(voxels), coors,
                                                               num_points);
     BFB_CHECK_LAUNCH();
