@@ -163,20 +163,41 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ inputs
+def upstream_grad(sample: int, case, device):
+    """N(0, 1) upstream gradient of one det sample, seeded by the sample's
+    index in the global batch (any shard reproduces it)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(1000 + sample)
+    return torch.randn((1, C, case.D, case.H, case.W), generator=g, device=device)
+
+
+def checksum(*ts) -> int:
+    """Order-sensitive integer checksum of tensors' bytes (bit-exact results
+    give equal checksums on any GPU)."""
+    acc = 0
+    for t in ts:
+        w = t.detach().contiguous().view(-1).view(torch.int32).to(torch.int64)
+        k = torch.arange(1, w.numel() + 1, device=w.device, dtype=torch.int64) % 65521
+        acc = (acc * 1000003 + int((w * k).sum().item())) % (1 << 61)
+    return acc
+
+
 class Workload:
     """The rank's shard: det bev_pool batch + LiDAR batch, resident on the GPU."""
 
-    def __init__(self, rank: int, samples: int, device, world: int = 1):
+    def __init__(self, rank: int, samples: int, device, world: int = 1, sample_offset=None):
         self.S = samples
-        first, count = shard.shard_samples(samples * world, world, rank)
-        assert count == samples
+        if sample_offset is None:
+            first, count = shard.shard_samples(samples * world, world, rank)
+            assert count == samples
+        else:
+            first = sample_offset
         case = synth.det_bev_pool_case(samples, device=device, sample_offset=first)
         self.feats, self.coords = case.feats, case.coords
         self.shape = (case.B, case.D, case.H, case.W)
         self.n = self.feats.size(0)
-        g = torch.Generator(device=device)
-        g.manual_seed(1000 + rank)
-        self.up = torch.randn((case.B, C, case.D, case.H, case.W), generator=g, device=device)
+        self.first = first
+        self.up = torch.cat([upstream_grad(first + i, case, device) for i in range(samples)])
         dhw = case.D * case.H * case.W
         r = (self.coords[:, 3] * dhw + (self.coords[:, 2] * case.H + self.coords[:, 0]) * case.W + self.coords[:, 1])
         self.nonempty = int(torch.unique(r).numel())
@@ -251,7 +272,7 @@ def run_ours(args, ws, rank, local):
     barrier(ws)
     t0.record(stream)
     for k in range(args.steps):
-        step(evs[k])
+        out_last, g_last = step(evs[k])
     t1.record(stream)
     torch.cuda.synchronize()
     barrier(ws)
@@ -301,6 +322,7 @@ def run_ours(args, ws, rank, local):
                                   'bev_bwd': round(phase[2], 4), 'voxelize': round(phase[3], 4)},
         'roofline': roofline, 'gpu_launches': launches, 'clocks': clocks,
     }
+    line['shard_check'] = shard_check(O, wl, out_last, g_last, ws, rank)
     if not args.no_e2e:
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
     if not args.no_rulebook:
@@ -311,22 +333,71 @@ def run_ours(args, ws, rank, local):
         del wl
         torch.cuda.empty_cache()
         line['fused_camera_branch'] = run_fused(args, rank, ws)
+    if not args.no_extra:
+        torch.cuda.empty_cache()
+        line['other_configs'] = run_extra_configs(args, rank, ws)
     if not args.no_cpu_baseline and ws == 1 and rank == 0:
         line['cpu_baseline'] = cpu_baseline(args)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
 
+def sample_checksums(O, feats_out, grad, wl_vox, n1):
+    """Checksum of every sample's outputs: bev_pool forward plane, the
+    sample's gradient rows, and its voxel rows / coords / counts."""
+    voxels, vcoors, vnum, vn = wl_vox
+    res = []
+    for i in range(feats_out.size(0)):
+        m = int(vn[i])
+        res.append(checksum(feats_out[i], grad[i * n1:(i + 1) * n1], voxels[i, :m], vcoors[i, :m], vnum[i, :m]))
+    return res
+
+
+def shard_check(O, wl, out, g, ws, rank):
+    """Multi-GPU parity of the sharded step: every rank checksums each of its
+    samples' outputs; rank 0 gathers them and recomputes the first sample of
+    every other rank's shard on its own GPU from the same seeds (outside the
+    timed region).  At N = 1 the checksums are reported for comparison with
+    the N > 1 lines (sample i gives the same checksum on any rank)."""
+    n1 = wl.n // wl.S
+    mine = sample_checksums(O, out, g, (wl.voxels, wl.vcoors, wl.vnum, wl.vn.tolist()), n1)
+    if ws == 1:
+        return {'sample_checksums': mine, 'recomputed': 0, 'match': True}
+    import torch.distributed as dist
+    allc = [None] * ws
+    dist.all_gather_object(allc, mine)
+    res = None
+    if rank == 0:
+        ok = True
+        for r in range(1, ws):
+            one = Workload(r, 1, wl.feats.device, ws, sample_offset=r * wl.S)
+            B, D, H, W = one.shape
+            plan = O.bev_pool_plan(one.coords, B, D, H, W)
+            o1 = O.bev_pool_forward_planned(one.feats, plan, B, D, H, W)
+            g1 = O.bev_pool_backward(one.up, plan, one.n, B, D, H, W)
+            O.hard_voxelize_batch(one.points, one.offs, one.voxels, one.vcoors, one.vnum, one.vn, one.vsize,
+                                  one.crange, one.mp, one.mv, False)
+            c1 = sample_checksums(O, o1, g1, (one.voxels, one.vcoors, one.vnum, one.vn.tolist()), one.n)[0]
+            ok = ok and c1 == allc[r][0]
+            del one
+        res = {'sample_checksums': [c for cs in allc for c in cs], 'recomputed': ws - 1, 'match': ok}
+    dist.barrier()
+    return res
+
+
 def run_e2e(args, wl, ws, samples_total):
     """Public API, host buffers: pinned H2D of the step's inputs, bev_pool
-    forward + backward through autograd, hard voxelisation, D2H of every
-    output, all inside the timed region.  The step is pipelined by sample
-    over three streams (copy in, compute, copy out), so both PCIe directions
-    and the kernels overlap, also across consecutive steps; device inputs are
-    double-buffered.  The timed region starts with idle streams and ends when
-    the last step's outputs are in host memory."""
+    forward + backward through autograd per det sample, the batched LiDAR
+    voxelisation (voxelize_batch, unreduced: packed [M, P, F] rows, one host
+    read of M), and D2H of every output (the valid voxel rows only), all
+    inside the timed region.  Det samples are pipelined over three streams
+    (copy in, compute, copy out), so both PCIe directions and the kernels
+    overlap, also across consecutive steps; device inputs are double-buffered.
+
+    The same copies with no kernels (same bytes, streams and ordering) give
+    the host-link ceiling the end-to-end number is held against."""
     from bevfusion_triton_b200.ops.bev_pool import bev_pool
-    from bevfusion_triton_b200.ops.voxel.voxel_layer import hard_voxelize_batch
+    from bevfusion_triton_b200.ops.voxel import voxelize_batch
     S = wl.S
     n1 = wl.n // S  # every det sample has the rig's kept points
     B, D, H, W = wl.shape
@@ -338,77 +409,112 @@ def run_e2e(args, wl, ws, samples_total):
     pts_h = wl.points_cpu.pin_memory()
     out_h = torch.empty(wl.up.shape, dtype=torch.float32).pin_memory()
     grad_h = torch.empty(wl.feats.shape, dtype=torch.float32).pin_memory()
-    vox_h = torch.empty(wl.voxels.shape, dtype=torch.float32).pin_memory()
-    vc_h = torch.empty(wl.vcoors.shape, dtype=torch.int32).pin_memory()
-    vnum_h = torch.empty(wl.vnum.shape, dtype=torch.int32).pin_memory()
-    vn_h = torch.empty(wl.vn.shape, dtype=torch.int32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (feats_h, coords_h, up_h, pts_h))
-    d2h = sum(t.numel() * t.element_size() for t in (out_h, grad_h, vox_h, vc_h, vnum_h, vn_h))
     dev = torch.device('cuda', torch.cuda.current_device())
+    clouds_d = torch.empty(pts_h.shape, device=dev)
+    clouds = [clouds_d[a:b] for a, b in zip(wl.offs, wl.offs[1:])]
+    M = int(wl.vn.sum())  # voxels of the step (deterministic)
+    F = pts_h.size(1)
+    vox_h = torch.empty((M, wl.mp, F), dtype=torch.float32).pin_memory()
+    vc_h = torch.empty((M, 4), dtype=torch.int32).pin_memory()
+    vs_h = torch.empty((M,), dtype=torch.int32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (feats_h, coords_h, up_h, pts_h))
+    d2h = sum(t.numel() * t.element_size() for t in (out_h, grad_h, vox_h, vc_h, vs_h))
     s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
     slots = [dict(feats=torch.empty((n1, C), device=dev), coords=torch.empty((n1, 4), dtype=torch.int64, device=dev),
-                  up=torch.empty((1, C, D, H, W), device=dev),
-                  pts=torch.empty((max(b - a for a, b in zip(wl.offs, wl.offs[1:])), pts_h.size(1)), device=dev))
-             for _ in range(2)]
+                  up=torch.empty((1, C, D, H, W), device=dev)) for _ in range(2)]
     free = [torch.cuda.Event(), torch.cuda.Event()]  # compute finished reading slot
+    outs = dict(out=torch.empty((1, C, D, H, W), device=dev), grad=torch.empty((n1, C), device=dev),
+                vox=torch.empty((M, wl.mp, F), device=dev), vc=torch.empty((M, 4), dtype=torch.int32, device=dev),
+                vs=torch.empty((M,), dtype=torch.int32, device=dev))
+    got = {}
 
-    def step():
+    def lidar(compute: bool):
+        with torch.cuda.stream(s_in):
+            clouds_d.copy_(pts_h, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ready)
+            if compute:
+                v, c, n = voxelize_batch(clouds, wl.vsize, wl.crange, wl.mp, wl.mv, reduce_mean=False)
+                got['M'] = v.size(0)
+            else:
+                v, c, n = outs['vox'], outs['vc'], outs['vs']
+            done = torch.cuda.Event()
+            done.record(s_cmp)
+            for t in (v, c, n):
+                t.record_stream(s_out)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            vox_h.copy_(v, non_blocking=True)
+            vc_h.copy_(c, non_blocking=True)
+            vs_h.copy_(n, non_blocking=True)
+
+    def step(compute=True):
         # no wait on the previous step here: its D2H drains while this step's
         # H2D starts (slot reuse is ordered by the `free` events)
         main = torch.cuda.current_stream()
+        lidar(compute)
         for s in range(S):
             k = s % 2
             sl = slots[k]
-            a, b = wl.offs[s], wl.offs[s + 1]
             with torch.cuda.stream(s_in):
                 s_in.wait_event(free[k])
                 sl['feats'].copy_(feats_h[s * n1:(s + 1) * n1], non_blocking=True)
                 sl['coords'].copy_(coords_h[s * n1:(s + 1) * n1], non_blocking=True)
                 sl['up'].copy_(up_h[s:s + 1], non_blocking=True)
-                pts = sl['pts'][: b - a]
-                pts.copy_(pts_h[a:b], non_blocking=True)
                 ready = torch.cuda.Event()
                 ready.record(s_in)
             with torch.cuda.stream(s_cmp):
                 s_cmp.wait_event(ready)
-                x = sl['feats'].detach().requires_grad_(True)
-                out = bev_pool(x, sl['coords'], 1, D, H, W)
-                out.backward(sl['up'])
-                V, Cc, N, VN = hard_voxelize_batch(pts, [0, b - a], wl.vsize, wl.crange, wl.mp, wl.mv)
+                if compute:
+                    x = sl['feats'].detach().requires_grad_(True)
+                    out = bev_pool(x, sl['coords'], 1, D, H, W)
+                    out.backward(sl['up'])
+                    out, grad = out.detach(), x.grad
+                else:
+                    out, grad = outs['out'], outs['grad']
                 free[k].record(s_cmp)
                 done = torch.cuda.Event()
                 done.record(s_cmp)
-                for t in (out, x.grad, V, Cc, N, VN):
+                for t in (out, grad):
                     t.record_stream(s_out)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done)
-                out_h[s:s + 1].copy_(out.detach(), non_blocking=True)
-                grad_h[s * n1:(s + 1) * n1].copy_(x.grad, non_blocking=True)
-                vox_h[s:s + 1].copy_(V, non_blocking=True)
-                vc_h[s:s + 1].copy_(Cc, non_blocking=True)
-                vnum_h[s:s + 1].copy_(N, non_blocking=True)
-                vn_h[s:s + 1].copy_(VN, non_blocking=True)
+                out_h[s:s + 1].copy_(out, non_blocking=True)
+                grad_h[s * n1:(s + 1) * n1].copy_(grad, non_blocking=True)
         main.wait_stream(s_out)
         main.wait_stream(s_cmp)
 
-    steps = max(2, min(args.steps, args.e2e_steps))
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize()
-    barrier(ws)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    barrier(ws)
-    ms = max_over_ranks(s.elapsed_time(e), ws) / steps
-    # the pipelined step must return what the batched device step computes
-    ok = bool(torch.equal(vn_h.to(wl.vn.device), wl.vn))
+    def timed(compute):
+        steps = max(2, min(args.steps, args.e2e_steps))
+        for _ in range(2):
+            step(compute)
+        torch.cuda.synchronize()
+        barrier(ws)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            step(compute)
+        e.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        return max_over_ranks(s.elapsed_time(e), ws) / steps, steps
+
+    ms, steps = timed(True)
+    ok = got.get('M') == M  # the pipelined step returns what the batched device step computed
+    copy_ms, _ = timed(False)
+    agg = lambda b, t: round(sum_over_ranks(b, ws) / (t * 1e-3) / 1e9, 1)  # noqa: E731
     return {'value': round(ms / samples_total, 4), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
             'd2h_bytes_per_step': d2h, 'steps': steps, 'ms_per_step': round(ms, 3),
-            'pipeline': 'per sample over 3 streams (H2D / compute / D2H), consecutive steps overlap', 'voxel_counts_match_device_step': ok}
+            'pipeline': 'per det sample over 3 streams (H2D / compute / D2H), consecutive steps overlap; '
+                        'LiDAR batch voxelised at once, valid voxel rows copied back',
+            'voxel_count_matches_device_step': ok,
+            'copy_ceiling': {'ms_per_step': round(copy_ms, 3), 'value': round(copy_ms / samples_total, 4),
+                             'unit': UNIT, 'h2d_gbs_all_ranks': agg(h2d, copy_ms),
+                             'd2h_gbs_all_ranks': agg(d2h, copy_ms),
+                             'note': 'same pinned copies, streams and ordering, no kernels'},
+            'frac_of_copy_ceiling': round(copy_ms / ms, 4)}
 
 
 def run_triton_reference(args, wl, ws):
@@ -470,6 +576,55 @@ def run_triton_reference(args, wl, ws):
     res['note'] = ('reference Triton kernels (bev_pool_triton.py, voxelization_triton.py, unmodified) vs this '
                    'library, both through their public Python calls on the same device-resident inputs; '
                    'bev_pool over the det batch with autograd, hard_voxelize one cloud per call (deterministic)')
+    return res
+
+
+def run_extra_configs(args, rank, ws):
+    """The other bev_pool configurations of BASELINE.json, device-resident,
+    plan + forward + backward per step (CUDA events, same warm-up rule):
+    config 4 (segmentation grid 256 x 256, batch 4, fp32) and config 2's
+    fp16-feature variant (det grid, batch 8, fp16 features and gradients)."""
+    O = torch.ops.bfb_b200
+    peak, _ = measured_peak()
+    res = {}
+    for name, mk, S, dt in (('seg_batch4_fp32', synth.seg_bev_pool_case, 4, torch.float32),
+                            ('det_batch8_fp16', synth.det_bev_pool_case, 8, torch.float16)):
+        first, _ = shard.shard_samples(S * ws, ws, rank)
+        case = mk(S, device='cuda', sample_offset=first, dtype=dt)
+        B, D, H, W = case.B, case.D, case.H, case.W
+        up = torch.cat([upstream_grad(first + i, case, 'cuda') for i in range(S)]).to(dt)
+        n = case.feats.size(0)
+        es = torch.empty((), dtype=dt).element_size()
+        dhw = D * H * W
+        r = case.coords[:, 3] * dhw + (case.coords[:, 2] * H + case.coords[:, 0]) * W + case.coords[:, 1]
+        U = int(torch.unique(r).numel())
+        alg = (n * C * es + n * 32 + B * C * dhw * es) + (n * C * es + n * 32 + U * C * es)
+
+        def step():
+            plan = O.bev_pool_plan(case.coords, B, D, H, W)
+            O.bev_pool_forward_planned(case.feats, plan, B, D, H, W)
+            O.bev_pool_backward(up, plan, n, B, D, H, W)
+
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        barrier(ws)
+        k = max(3, min(args.steps, 20))
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        ms = max_over_ranks(s0.elapsed_time(s1), ws) / k
+        res[name] = {'ms_per_sample': round(ms / (S * ws), 5), 'ms_per_step': round(ms, 4), 'samples_per_gpu': S,
+                     'points_per_sample': n // S, 'gbs_per_gpu': round(alg / (ms * 1e-3) / 1e9, 1),
+                     'hbm_frac': round(alg / (ms * 1e-3) / 1e9 / peak, 4)}
+        del case, up
+        torch.cuda.empty_cache()
+    res['note'] = ('plan + forward + backward of bev_pool per step, inputs resident in HBM; bytes are the '
+                   'path-level algorithmic bytes (feats, int64 coords, output, gradient rows)')
     return res
 
 
@@ -657,6 +812,7 @@ def main():
     ap.add_argument('--no-fused', action='store_true')
     ap.add_argument('--no-rulebook', action='store_true')
     ap.add_argument('--no-triton', action='store_true', help='skip timing the reference Triton GPU path')
+    ap.add_argument('--no-extra', action='store_true', help='skip the config-4 and fp16 bev_pool timings')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3  # timing rule: at least 3 warm-up steps

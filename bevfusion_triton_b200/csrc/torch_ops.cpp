@@ -406,6 +406,35 @@ void hard_voxelize_batch(const at::Tensor& points_in, c10::ArrayRef<int64_t> off
   check(rc, "hard_voxelize");
 }
 
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> voxelize_mean_epilogue(const at::Tensor& voxels,
+                                                                                  const at::Tensor& coors,
+                                                                                  const at::Tensor& num_points,
+                                                                                  const at::Tensor& voxel_num) {
+  require_cuda(voxels, "voxels");
+  c10::cuda::CUDAGuard guard(voxels.device());
+  TORCH_CHECK_VALUE(voxels.dim() == 4, "voxels must be [batch, max_voxels, max_points, F]");
+  const int64_t B = voxels.size(0), MV = voxels.size(1), P = voxels.size(2), F = voxels.size(3);
+  TORCH_CHECK_VALUE(coors.dim() == 3 && coors.size(0) == B && coors.size(1) == MV && coors.size(2) == 3,
+                    "coors must be [batch, max_voxels, 3]");
+  TORCH_CHECK_VALUE(num_points.dim() == 2 && num_points.size(0) == B && num_points.size(1) == MV,
+                    "num_points must be [batch, max_voxels]");
+  TORCH_CHECK_VALUE(voxel_num.numel() == B, "voxel_num must hold batch counts");
+  for (auto* t : {&voxels, &coors, &num_points, &voxel_num}) require_contig(*t, "epilogue inputs");
+  TORCH_CHECK_TYPE(coors.scalar_type() == at::kInt && num_points.scalar_type() == at::kInt &&
+                       voxel_num.scalar_type() == at::kInt,
+                   "coors, num_points and voxel_num must be int32");
+  auto feats = at::empty({B * MV, F}, voxels.options());
+  auto coords = at::empty({B * MV, 4}, coors.options());
+  auto sizes = at::empty({B * MV}, coors.options());
+  auto total = at::empty({1}, coors.options());
+  check(bfb_voxelize_mean_epilogue(voxels.data_ptr(), dtype_code(voxels), coors.data_ptr<int32_t>(),
+                                   num_points.data_ptr<int32_t>(), voxel_num.data_ptr<int32_t>(), B, MV, P, F,
+                                   feats.data_ptr(), coords.data_ptr<int32_t>(), sizes.data_ptr<int32_t>(),
+                                   total.data_ptr<int32_t>(), stream_of(voxels)),
+        "voxelize mean epilogue");
+  return {feats, coords, sizes, total};
+}
+
 int64_t hard_voxelize(const at::Tensor& points, at::Tensor& voxels, at::Tensor& coors, at::Tensor& num_points,
                       c10::ArrayRef<double> voxel_size, c10::ArrayRef<double> coors_range, int64_t max_points,
                       int64_t max_voxels, bool zero_tail) {
@@ -547,6 +576,9 @@ TORCH_LIBRARY(bfb_b200, m) {
       "Tensor(c!) num_points, Tensor(d!) voxel_num, float[] voxel_size, float[] coors_range, int max_points, "
       "int max_voxels, bool zero_tail) -> ()");
   m.def(
+      "voxelize_mean_epilogue(Tensor voxels, Tensor coors, Tensor num_points, Tensor voxel_num) -> (Tensor, Tensor, "
+      "Tensor, Tensor)");
+  m.def(
       "get_indice_pairs(Tensor indices, int batch, int[] out_shape, int[] ksize, int[] stride, int[] padding, "
       "int[] dilation, bool subm, bool transpose) -> (Tensor, Tensor, Tensor)");
   m.def(
@@ -572,6 +604,7 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("dynamic_voxelize", &dynamic_voxelize);
   m.impl("hard_voxelize", &hard_voxelize);
   m.impl("hard_voxelize_batch", &hard_voxelize_batch);
+  m.impl("voxelize_mean_epilogue", &voxelize_mean_epilogue);
   m.impl("dynamic_scatter_forward", &dynamic_scatter_forward);
   m.impl("get_indice_pairs", &get_indice_pairs);
   m.impl("dynamic_scatter_backward", &dynamic_scatter_backward);

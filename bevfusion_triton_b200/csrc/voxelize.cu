@@ -789,6 +789,60 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// mean epilogue: voxel rows of every sample -> packed [M, F] means,
+// (b, x, y, z) coords and counts
+// ---------------------------------------------------------------------------
+constexpr int kEpiMaxBatch = 4096;  // prefix of voxel_num kept in shared memory
+
+// A thread per (voxel row, feature) over batch * max_voxels rows; row `local`
+// of sample s (local < voxel_num[s]) lands at packed row prefix(s) + local.
+// The mean sums the row's P point slots in slot order in fp32 (unused slots
+// hold zeros) and divides once by the count.
+template <class T>
+__global__ __launch_bounds__(256) void vox_mean_epilogue_kernel(
+    const T* __restrict__ voxels, const int32_t* __restrict__ coors, const int32_t* __restrict__ num_points,
+    const int32_t* __restrict__ voxel_num, int batch, int64_t max_voxels, int64_t P, int64_t f,
+    T* __restrict__ out_feats, int32_t* __restrict__ out_coords, int32_t* __restrict__ out_sizes,
+    int32_t* __restrict__ total_dev) {
+  __shared__ uint32_t s_pre[kEpiMaxBatch + 1];
+  __shared__ uint32_t s_ws[8];
+  uint32_t carry = 0;
+  for (int b0 = 0; b0 < batch; b0 += 256) {
+    const int sidx = b0 + threadIdx.x;
+    const uint32_t c = sidx < batch ? (uint32_t)voxel_num[sidx] : 0u;
+    uint32_t tot;
+    const uint32_t pre = block_exclusive_scan(c, s_ws, &tot) + carry;
+    if (sidx < batch) s_pre[sidx] = pre;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) s_pre[batch] = carry;
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && total_dev) *total_dev = (int32_t)carry;
+  const uint64_t items = (uint64_t)batch * (uint64_t)max_voxels * (uint64_t)f;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += stride) {
+    const uint64_t row = i / (uint64_t)f;
+    const int64_t q = (int64_t)(i - row * (uint64_t)f);
+    const int s = (int)(row / (uint64_t)max_voxels);
+    const int64_t local = (int64_t)(row - (uint64_t)s * (uint64_t)max_voxels);
+    if (local >= (int64_t)(s_pre[s + 1] - s_pre[s])) continue;
+    const int64_t k = (int64_t)s_pre[s] + local;
+    const T* src = voxels + (int64_t)row * P * f + q;
+    float acc = 0.f;
+    for (int64_t j = 0; j < P; ++j) acc = __fadd_rn(acc, to_f32<T>(__ldg(src + j * f)));
+    const int32_t cnt = __ldg(num_points + row);
+    out_feats[k * f + q] = from_f32<T>(__fdiv_rn(acc, (float)cnt));
+    if (q == 0) {
+      out_coords[4 * k + 0] = s;
+      out_coords[4 * k + 1] = __ldg(coors + 3 * row + 0);
+      out_coords[4 * k + 2] = __ldg(coors + 3 * row + 1);
+      out_coords[4 * k + 3] = __ldg(coors + 3 * row + 2);
+      out_sizes[k] = cnt;
+    }
+  }
+}
+
 // every slot free: key empty, no first point, count 0
 __global__ void vox_table_init_kernel(TableView tb) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -1046,3 +1100,37 @@ extern "C" int bfb_hard_voxelize_status(const void* scratch, int64_t n, int64_t 
   return BFB_OK;
 }
 
+
+extern "C" int bfb_voxelize_mean_epilogue(const void* voxels, int dtype, const int32_t* coors,
+                                          const int32_t* num_points, const int32_t* voxel_num, int64_t batch,
+                                          int64_t max_voxels, int64_t max_points, int64_t f, void* out_feats,
+                                          int32_t* out_coords, int32_t* out_sizes, int32_t* total_dev,
+                                          void* stream) {
+  if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 1 || max_voxels < 1 || max_points < 1 || f < 1) return BFB_ERR_INVALID_ARG;
+  if (batch > kEpiMaxBatch) return BFB_ERR_TOO_LARGE;
+  if ((uint64_t)batch * (uint64_t)max_voxels > 0x7fffffffull) return BFB_ERR_TOO_LARGE;
+  if (!voxels || !coors || !num_points || !voxel_num || !out_feats || !out_coords || !out_sizes)
+    return BFB_ERR_INVALID_ARG;
+  cudaStream_t st = as_stream(stream);
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(batch * max_voxels * f, 256), 148 * 16);
+  switch (dtype) {
+    case BFB_F32:
+      vox_mean_epilogue_kernel<float><<<grid, 256, 0, st>>>(
+          static_cast<const float*>(voxels), coors, num_points, voxel_num, (int)batch, max_voxels, max_points, f,
+          static_cast<float*>(out_feats), out_coords, out_sizes, total_dev);
+      break;
+    case BFB_F16:
+      vox_mean_epilogue_kernel<__half><<<grid, 256, 0, st>>>(
+          static_cast<const __half*>(voxels), coors, num_points, voxel_num, (int)batch, max_voxels, max_points, f,
+          static_cast<__half*>(out_feats), out_coords, out_sizes, total_dev);
+      break;
+    default:
+      vox_mean_epilogue_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(voxels), coors, num_points, voxel_num, (int)batch, max_voxels,
+          max_points, f, static_cast<__nv_bfloat16*>(out_feats), out_coords, out_sizes, total_dev);
+      break;
+  }
+  BFB_CHECK_LAUNCH();
+  return BFB_OK;
+}

@@ -127,6 +127,12 @@ def _register_fakes() -> None:
           zero_tail):
         return None
 
+    @reg(lib + 'voxelize_mean_epilogue')
+    def _(voxels, coors, num_points, voxel_num):
+        B, MV, _, F = voxels.shape
+        return (voxels.new_empty((B * MV, F)), coors.new_empty((B * MV, 4)), coors.new_empty((B * MV,)),
+                coors.new_empty((1,)))
+
     @reg(lib + 'get_indice_pairs')
     def _(indices, batch, out_shape, ksize, stride, padding, dilation, subm, transpose):
         n, k1 = indices.shape

@@ -71,24 +71,24 @@ class Voxelization(nn.Module):
 def voxelize_batch(points_list, voxel_size, point_cloud_range, max_num_points, max_voxels, reduce_mean=True):
     """Batched replacement of ``BEVFusion.voxelize`` (models/fusion_models/
     bevfusion.py:269-296): one set of launches for all samples instead of a
-    Python loop.  Returns ``(feats, coords, sizes)`` exactly as that method
+    Python loop over them.  Returns ``(feats, coords, sizes)`` as that method
     does: feats [M, F] (mean over each voxel's points when ``reduce_mean``,
-    else [M, P, F]), coords [M, 4] int32 = (sample, x, y, z), sizes [M]."""
+    else [M, P, F]), coords [M, 4] int32 = (sample, x, y, z), sizes [M].
+
+    With ``reduce_mean`` the packing and the mean are one epilogue launch
+    (``bfb_voxelize_mean_epilogue``); the only host read is the voxel total M
+    that sizes the returned tensors."""
     pts = torch.cat([p for p in points_list], 0) if len(points_list) > 1 else points_list[0]
     offs = [0]
     for p in points_list:
         offs.append(offs[-1] + int(p.size(0)))
     voxels, coors, num, vn = hard_voxelize_batch(pts, offs, voxel_size, point_cloud_range, max_num_points,
                                                  max_voxels)
-    counts = vn.tolist()
-    feats, coords, sizes = [], [], []
-    for s, m in enumerate(counts):
-        feats.append(voxels[s, :m])
-        coords.append(torch.nn.functional.pad(coors[s, :m], (1, 0), mode='constant', value=s))
-        sizes.append(num[s, :m])
-    feats = torch.cat(feats, 0)
-    coords = torch.cat(coords, 0)
-    sizes = torch.cat(sizes, 0)
+    feats, coords, sizes, total = ops().voxelize_mean_epilogue(voxels, coors, num, vn)
+    m = int(total.item())
     if reduce_mean:
-        feats = (feats.sum(dim=1) / sizes.to(feats.dtype).unsqueeze(1)).contiguous()
-    return feats, coords, sizes
+        return feats[:m], coords[:m], sizes[:m]
+    # the unreduced [M, P, F] rows: gather the packed rows (no per-sample loop)
+    rows = coords[:m, 0].long() * voxels.size(1) + torch.arange(m, device=pts.device) - \
+        torch.repeat_interleave(torch.cumsum(vn.long(), 0) - vn.long(), vn.long(), output_size=m)
+    return voxels.flatten(0, 1)[rows], coords[:m], sizes[:m]

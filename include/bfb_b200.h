@@ -298,6 +298,23 @@ int bfb_hard_voxelize_batch(const void* points_dev, int points_dtype, const int6
                             size_t table_bytes, void* scratch_dev, size_t scratch_bytes,
                             void* stream);
 
+/* Mean epilogue of a batched voxelisation, one launch.  Replaces the loop of
+ * models/fusion_models/bevfusion.py:269-296 after the per-sample
+ * voxelisation: the rows [0, voxel_num[s]) of every sample s of the outputs
+ * of bfb_hard_voxelize_batch (voxels [batch, max_voxels, max_points, f],
+ * coors [batch, max_voxels, 3], num_points [batch, max_voxels], voxel_num
+ * [batch], all device) are packed sample after sample into out_feats [M, f]
+ * (mean over the voxel's point slots: the slots are summed in slot order in
+ * fp32, unused slots hold zeros, then divided by the count), out_coords
+ * [M, 4] int32 = (sample, x, y, z) and out_sizes [M] int32, with M =
+ * sum(voxel_num) <= batch * max_voxels (size the outputs for that); the
+ * device int32 *total_dev receives M (may be NULL).  batch <= 4096. */
+int bfb_voxelize_mean_epilogue(const void* voxels_dev, int dtype, const int32_t* coors_dev,
+                               const int32_t* num_points_dev, const int32_t* voxel_num_dev,
+                               int64_t batch, int64_t max_voxels, int64_t max_points, int64_t f,
+                               void* out_feats_dev, int32_t* out_coords_dev, int32_t* out_sizes_dev,
+                               int32_t* total_dev, void* stream);
+
 /* Synchronously reads the device status of the last call that used this
  * scratch: *table_full = points whose insert found no free table slot
  * (always 0 when the table capacity rule above holds). */

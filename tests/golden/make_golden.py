@@ -14,8 +14,11 @@ package modules:
 * ops/voxel/src/scatter_points_triton.py         ``dynamic_point_to_voxel_forward/backward``
 * ops/spconv/src/spconv_triton.py                ``_get_indice_pairs_impl`` (rulebooks, with the
                                                  GPU path's output order: cuda_ordering=True)
+* models/vtransforms/base.py                     ``BaseTransform.get_geometry`` and the quantise +
+                                                 in-grid filter of ``BaseTransform.bev_pool``
+                                                 (with models/helper/amp.py ``force_fp32``)
 
-``--only spconv`` regenerates only the rulebook fixture.
+``--only spconv`` / ``--only geometry`` regenerate only that fixture.
 
 Cases mirror the reference tests (tests/test_ops/test_bev_pool.py:24-84,
 tests/test_ops/test_voxel.py:27-79) plus seeded larger cases and full-size
@@ -70,6 +73,83 @@ SPCONV_CASES = [
     ([4, 3, 3, 5], [3, 1, 3, 2], [1, 1, 1, 1], [1, 0, 1, 0], [1, 1, 1, 1], False, False),
     ([20, 20, 6], [3, 3, 3], [2, 2, 2], [1, 1, 1], [1, 1, 1], False, False),
 ]
+
+
+def import_base_transform(ref: Path):
+    """models/vtransforms/base.py with stub ``models`` / ``models.helper``
+    packages (only helper/amp.py is executed) and ``ops.bev_pool`` bound to
+    the reference bev_pool module (CPU path)."""
+    import importlib.util
+    for name, sub in [('models', 'models'), ('models.helper', 'models/helper'),
+                      ('models.vtransforms', 'models/vtransforms')]:
+        m = types.ModuleType(name)
+        m.__path__ = [str(ref / sub)]
+        sys.modules[name] = m
+    spec = importlib.util.spec_from_file_location('models.helper.amp', ref / 'models/helper/amp.py')
+    amp = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(amp)
+    sys.modules['models.helper'].force_fp32 = amp.force_fp32
+    import ops.bev_pool.src.bev_pool_triton as bpt
+    sys.modules['ops.bev_pool'].bev_pool = bpt.bev_pool
+    import models.vtransforms.base as base
+    return base
+
+
+EDGE = 1e-4  # cells: a point this close to a cell edge may round either way
+
+
+def geometry_cases(base):
+    """Per frustum point, the cell rank ((b*D + z)*H + x)*W + y the reference
+    gives it (get_geometry, then the trunc quantise and in-grid filter of
+    BaseTransform.bev_pool, base.py:82-158), -1 when filtered out.  The
+    points whose quantiser input lies within EDGE cells of an integer are
+    listed with their reference cells (the GPU producer's fp32 association
+    may round them either way); all other points are pinned by a digest of
+    the cell array with the listed points set to -2."""
+    out, dig = {}, {}
+    cases = [('det_plain', synth.DET_GRID, 1, False), ('det_aug', synth.DET_GRID, 2, True),
+             ('seg_plain', synth.SEG_GRID, 1, False), ('seg_aug', synth.SEG_GRID, 1, True)]
+    for name, grid, batch, augment in cases:
+        rig = synth.camera_rig(batch, augment=augment, seed=5)
+        bt = base.BaseTransform(80, 80, synth.IMAGE_SIZE, synth.FEATURE_SIZE, grid['xbound'], grid['ybound'],
+                                grid['zbound'], synth.DBOUND)
+        bt.frustum.data.copy_(rig['frustum'])
+        extra = {k: rig[k] for k in ('extra_rots', 'extra_trans') if k in rig}
+        geom = bt.get_geometry(rig['camera2lidar_rots'], rig['camera2lidar_trans'], rig['intrins'],
+                               rig['post_rots'], rig['post_trans'], **extra)
+        B, N, D, H, W, _ = geom.shape
+        n = B * N * D * H * W
+        captured = {}
+
+        def capture(x, g, b_, d_, h_, w_):
+            captured['idx'] = x[:, 0].long()
+            captured['coords'] = g.clone()
+            captured['grid'] = (b_, int(d_), int(h_), int(w_))
+            return torch.zeros((b_, x.size(1), int(d_), int(h_), int(w_)))
+
+        saved = base.bev_pool
+        base.bev_pool = capture
+        try:  # the point index rides through the filter as the one feature channel
+            x = torch.arange(n, dtype=torch.float32).view(B, N, D, H, W, 1)
+            bt.bev_pool(geom, x)
+        finally:
+            base.bev_pool = saved
+        Bg, Dg, Hg, Wg = captured['grid']
+        c = captured['coords']
+        cells = torch.full((n,), -1, dtype=torch.int64)
+        cells[captured['idx']] = ((c[:, 3] * Dg + c[:, 2]) * Hg + c[:, 0]) * Wg + c[:, 1]
+        q = (geom - (bt.bx - bt.dx / 2.0)) / bt.dx  # the quantiser input, as base.py:139 forms it
+        q = q.reshape(-1, 3).double()
+        near = torch.nonzero(((q - q.round()).abs() < EDGE).any(1)).squeeze(1)
+        masked = cells.clone()
+        masked[near] = -2
+        out[f'{name}_near_idx'] = near.numpy().astype(np.int32)
+        out[f'{name}_near_cells'] = cells[near].numpy()
+        out[f'{name}_grid'] = np.array([Bg, Dg, Hg, Wg], dtype=np.int64)
+        dig[f'geometry_{name}_masked_cells'] = sha(masked.numpy())
+        dig[f'geometry_{name}_kept'] = int((cells >= 0).sum())
+    save('geometry_cells', **out)
+    return dig
 
 
 def spconv_cases(sct):
@@ -243,8 +323,14 @@ def main():
         raise SystemExit('usage: make_golden.py <path to the bevfusion-triton checkout>')
     ref = Path(sys.argv[1]).resolve()
     bpt, vt, spt = import_reference(ref)
-    if '--only' in sys.argv and sys.argv[sys.argv.index('--only') + 1] == 'spconv':
+    only = sys.argv[sys.argv.index('--only') + 1] if '--only' in sys.argv else None
+    if only == 'spconv':
         spconv_cases(import_spconv())
+        return
+    if only == 'geometry':
+        digests = json.loads((HERE / 'digests.json').read_text())
+        digests.update(geometry_cases(import_base_transform(ref)))
+        (HERE / 'digests.json').write_text(json.dumps(digests, indent=1, sort_keys=True) + '\n')
         return
     torch.set_num_threads(8)
     digests = {}
@@ -252,6 +338,7 @@ def main():
     digests.update(voxel_cases(vt))
     scatter_cases(spt)
     spconv_cases(import_spconv())
+    digests.update(geometry_cases(import_base_transform(ref)))
     (HERE / 'digests.json').write_text(json.dumps(digests, indent=1, sort_keys=True) + '\n')
     print(json.dumps(digests, indent=1))
 

@@ -54,3 +54,32 @@ def test_fused_forward_vs_oracle_small(cuda):
     ref, bad = oracle.bev_pool(feats.numpy(), coords.numpy(), B, D, H, W)
     assert bad > 0
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_fused_forward_vs_oracle_det_sample(cuda):
+    """One full det sample (6 cameras x 118 bins x 32 x 88, C = 80, the
+    config-1 grid) through the fused op against the C oracle's sequential sum
+    of the materialised product (unfiltered: the oracle drops the out-of-grid
+    points as the caller's filter does), bit for bit; and the gradients
+    against the oracle's backward gather contracted on the CPU in fp64."""
+    case = synth.depth_context_case(1, synth.DET_GRID, device='cuda')
+    shape = (case.B, case.D, case.H, case.W)
+    d = case.depth.clone().requires_grad_(True)
+    c = case.context.clone().requires_grad_(True)
+    out = bev_pool_depth_context(d, c, case.coords, *shape)
+    C = case.context.size(2)
+    feats = (case.depth.unsqueeze(2) * case.context.unsqueeze(3)).permute(0, 1, 3, 4, 5, 2).reshape(-1, C)
+    ref, bad = oracle.bev_pool(feats.cpu().numpy(), case.coords.cpu().numpy(), *shape)
+    assert bad == int((~case.kept).sum())
+    np.testing.assert_array_equal(out.detach().cpu().numpy(), ref)
+    up = torch.randn(out.shape, device='cuda', generator=torch.Generator(device='cuda').manual_seed(3))
+    out.backward(up)
+    # d feats[n] = up[cell(n)] (oracle gather), then the product rule in fp64
+    gf = torch.from_numpy(oracle.bev_pool_backward(up.cpu().numpy(), case.coords.cpu().numpy(), *shape))
+    gf = gf.double().view(1, 6, -1, 32, 88, C)                     # (b n d h w) c
+    dep = case.depth.double().cpu()
+    ctx = case.context.double().cpu()                              # [1, 6, C, fH, fW]
+    want_d = (gf * ctx.permute(0, 1, 3, 4, 2).unsqueeze(2)).sum(-1)
+    want_c = (gf * dep.unsqueeze(-1)).sum(2).permute(0, 1, 4, 2, 3)
+    torch.testing.assert_close(d.grad.double().cpu(), want_d, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(c.grad.double().cpu(), want_c, rtol=1e-5, atol=1e-5)

@@ -10,10 +10,12 @@ points differ from the reference's cells, and every one of them is within
 1e-3 of a cell edge in the reference's own fp32 coordinates.  Everything
 downstream of the cells is compared bit for bit.
 """
+import numpy as np
 import pytest
 import torch
 
 from tests import synth
+from tests._util import sha
 from bevfusion_triton_b200.ops.bev_pool import (bev_grid, bev_pool, bev_pool_depth_context, bev_pool_geometry_plan,
                                                 bev_pool_planned)
 from bevfusion_triton_b200.ops.bev_pool.bev_pool import invalid_count, plan_cells
@@ -66,6 +68,52 @@ def test_geometry_plan_cells_match_reference(cuda, augment, grid):
     got = plan_cells(plan, n, *shape)
     check_cells(got, want, v)
     assert invalid_count(plan) == int((got < 0).sum())
+
+
+FIXTURE_CASES = {'det_plain': ('det', 1, False), 'det_aug': ('det', 2, True), 'seg_plain': ('seg', 1, False),
+                 'seg_aug': ('seg', 1, True)}
+
+
+@pytest.mark.parametrize('name', sorted(FIXTURE_CASES))
+def test_geometry_plan_cells_match_reference_fixture(cuda, golden, digests, name):
+    """Pinned to the reference itself: tests/golden/make_golden.py ran the
+    reference's BaseTransform.get_geometry and the quantise + filter of its
+    bev_pool (models/vtransforms/base.py:82-158) on this rig on the CPU.  Every
+    point whose quantiser input is more than 1e-4 cells from a cell edge has
+    exactly the reference's cell (digest of the whole cell array with the
+    near-edge points masked); a near-edge point is in the reference's cell or
+    a neighbour of it (one axis, one step, or across the grid border)."""
+    grid, batch, augment = FIXTURE_CASES[name]
+    grid_d = synth.DET_GRID if grid == 'det' else synth.SEG_GRID
+    rig = synth.camera_rig(batch, augment=augment, seed=5, device='cuda')
+    plan, shape = bev_pool_geometry_plan(xbound=grid_d['xbound'], ybound=grid_d['ybound'], zbound=grid_d['zbound'],
+                                         **rig)
+    g = golden('geometry_cells')
+    assert list(shape) == g[f'{name}_grid'].tolist()
+    n = batch * 6 * rig['frustum'][..., 0].numel()
+    got = plan_cells(plan, n, *shape).cpu()
+    near = torch.from_numpy(g[f'{name}_near_idx'].astype(np.int64))
+    masked = got.clone()
+    masked[near] = -2
+    assert sha(masked) == digests[f'geometry_{name}_masked_cells']
+    B, D, H, W = shape
+    want = torch.from_numpy(g[f'{name}_near_cells'])
+    ours = got[near]
+
+    def split(c):
+        return torch.stack((c // (D * H * W), (c // (H * W)) % D, (c // W) % H, c % W), 1)
+
+    both = (want >= 0) & (ours >= 0)
+    step = (split(ours[both]) - split(want[both])).abs().sum(1)
+    assert bool((step <= 1).all())
+    # a point dropped on one side only sits on the grid border
+    one = (want >= 0) ^ (ours >= 0)
+    kept = want[one].clamp_min(0) * (want[one] >= 0) + ours[one].clamp_min(0) * (ours[one] >= 0)
+    k = split(kept)
+    border = (k[:, 1] == 0) | (k[:, 1] == D - 1) | (k[:, 2] == 0) | (k[:, 2] == H - 1) | (k[:, 3] == 0) | (
+        k[:, 3] == W - 1)
+    assert bool(border.all())
+    assert int((ours != want).sum()) <= max(1, near.numel() // 10)
 
 
 def test_geometry_plan_pools_unfiltered_features(cuda):

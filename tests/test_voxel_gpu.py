@@ -154,19 +154,51 @@ def test_hard_voxelize_batch_matches_single(cuda):
 
 
 def test_voxelize_batch_mean_features(cuda):
-    clouds = [synth.lidar_sweeps(s)[:30000].cuda() for s in range(2)]
+    """The one-launch epilogue against the reference composition
+    (models/fusion_models/bevfusion.py:269-296: per-sample voxelisation, batch
+    index padded on, concatenated, feats.sum(1) / num_points): coords and
+    sizes bit-exact; the mean equals a sequential fp32 sum over the point slots
+    divided once by the count bit for bit, and the torch composition within
+    1e-6 (its reduction may associate the slot sum differently)."""
+    clouds = [synth.lidar_sweeps(s)[:30000].cuda() for s in range(3)]
     vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
     feats, coords, sizes = voxelize_batch(clouds, vs, cr, 10, 12000)
     rf, rc, rs = [], [], []
-    for b, c in enumerate(clouds):  # models/fusion_models/bevfusion.py:269-296
+    for b, c in enumerate(clouds):
         v, cc, nn = voxelization(c, vs, cr, 10, 12000, True)
         rf.append(v)
         rc.append(torch.nn.functional.pad(cc, (1, 0), mode='constant', value=b))
         rs.append(nn)
     rs = torch.cat(rs)
-    ref = torch.cat(rf).sum(1) / rs.to(torch.float32).unsqueeze(1)
+    rv = torch.cat(rf)
     assert torch.equal(coords, torch.cat(rc)) and torch.equal(sizes, rs)
-    assert torch.equal(feats, ref)
+    seq = np.zeros((rv.size(0), rv.size(2)), dtype=np.float32)
+    rvn = rv.cpu().numpy()
+    for j in range(rv.size(1)):
+        seq = (seq + rvn[:, j]).astype(np.float32)
+    seq = seq / rs.cpu().numpy().astype(np.float32)[:, None]
+    np.testing.assert_array_equal(feats.cpu().numpy(), seq)
+    ref = rv.sum(1) / rs.to(torch.float32).unsqueeze(1)
+    torch.testing.assert_close(feats, ref, rtol=1e-6, atol=1e-6)
+    # unreduced rows
+    f2, c2, s2 = voxelize_batch(clouds, vs, cr, 10, 12000, reduce_mean=False)
+    assert torch.equal(f2, rv) and torch.equal(c2, coords) and torch.equal(s2, sizes)
+
+
+def test_voxelize_batch_empty_sample_and_cap(cuda):
+    """A sample without points, and max_voxels reached: packing stays right."""
+    clouds = [synth.lidar_sweeps(0)[:20000].cuda(), torch.empty((0, 5), device='cuda'),
+              synth.lidar_sweeps(1)[:20000].cuda()]
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    feats, coords, sizes = voxelize_batch(clouds, vs, cr, 5, 3000)
+    rc = []
+    for b, c in enumerate(clouds):
+        if c.size(0) == 0:
+            continue
+        _, cc, _ = voxelization(c, vs, cr, 5, 3000, True)
+        rc.append(torch.nn.functional.pad(cc, (1, 0), mode='constant', value=b))
+    assert torch.equal(coords, torch.cat(rc))
+    assert coords.size(0) == 6000 and int(sizes.max()) <= 5
 
 
 # ----------------------------------------------------------------- scatter
