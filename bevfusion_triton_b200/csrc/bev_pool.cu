@@ -557,8 +557,10 @@ struct DepthContextRows {
 
 // Sum of one cell's rows in ascending point order, software-pipelined: the
 // loads of the next U rows are in flight while the current U are added.
+// `steps` bounds the loop for the whole warp, `cnt` is this lane's count
+// (lane groups summing different cells keep one loop and stay converged).
 template <int VE, int U, class Src>
-__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, uint32_t pos0, int cnt,
+__device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ pids, uint32_t pos0, int steps, int cnt,
                                                    const Src& src, bool active, float (&acc)[VE]) {
   float va[U][VE], vb[U][VE];
   auto load = [&](int k, float (&v)[U][VE]) {
@@ -581,19 +583,49 @@ __device__ __forceinline__ void sum_cell_pipelined(const uint32_t* __restrict__ 
       }
   };
   load(0, va);
-  for (int k = 0; k < cnt; k += 2 * U) {
-    if (k + U < cnt) load(k + U, vb);
+  for (int k = 0; k < steps; k += 2 * U) {
+    if (k + U < steps) load(k + U, vb);
     add(k, va);
-    if (k + U >= cnt) break;
-    if (k + 2 * U < cnt) load(k + 2 * U, va);
+    if (k + U >= steps) break;
+    if (k + 2 * U < steps) load(k + 2 * U, va);
     add(k + U, vb);
+  }
+}
+
+// Sum of a cell larger than a piece: its permutation slice is streamed from
+// global memory by the whole warp (PermStream), PU rows at a time.
+template <int VE, int PU, class Src>
+__device__ __forceinline__ void sum_cell_streamed(const uint32_t* __restrict__ perm, int a, int cnt, int lane,
+                                                  const Src& src, bool active, float (&acc)[VE]) {
+  PermStream ps;
+  ps.init(perm, a, a + cnt, lane);
+  for (int k = 0; k < cnt; k += PU) {
+    float v[PU][VE];
+#pragma unroll
+    for (int u = 0; u < PU; ++u) {
+      const uint32_t pid = ps.at(a + k + u, lane);
+      if (k + u < cnt && active) {
+        src.load(pid, (uint32_t)(a + k + u), v[u]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
+      }
+    }
+    // ascending point order, one fp32 add per element per point
+#pragma unroll
+    for (int u = 0; u < PU; ++u) {
+      if (k + u < cnt) {
+#pragma unroll
+        for (int q = 0; q < VE; ++q) acc[q] = __fadd_rn(acc[q], v[u][q]);
+      }
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // 6. forward: one CTA per (piece, channel slice of 32 vectors)
 // ---------------------------------------------------------------------------
-template <class T, int VE, int PU, class Src>
+template <class T, int VE, int PU, class Src, bool kGroups>
 __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
     Src src, int64_t C, int nvec, int64_t dhw, int64_t tpb,
     const uint32_t* __restrict__ perm, const int2* __restrict__ cell_se,
@@ -630,54 +662,65 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
   if (threadIdx.x == 0) s_next = 0;
   __syncthreads();
 
-  const bool active = lane < nvs;
-  src.bind(v0, lane);
-  const int m = s_m;
-  for (;;) {
-    int i = 0;
-    if (lane == 0) i = atomicAdd(&s_next, 1);
-    i = __shfl_sync(0xffffffffu, i, 0);
-    if (i >= m) break;
-    const int cell = s_cell[i], beg = s_beg[i], cnt = s_cnt[i];
-    float acc[VE];
+  if constexpr (kGroups) {
+    // Narrow rows (at most 16 vectors, e.g. 80 fp16 channels = 10 lanes) are
+    // summed by lane groups of nvs lanes, each group on its own cell, so most
+    // lanes stay busy; a cell is still summed by one group in ascending point
+    // order.  The warp takes ngrp consecutive cells of the largest-first
+    // list: their counts are close, so one loop bound (the first, largest
+    // count) keeps the groups converged.  A piece that is one cell larger
+    // than a piece (not staged) is summed by the whole warp.
+    const int L = staged ? nvs : 32;  // lanes per group
+    const int grp = lane / L, gl = lane - grp * L;
+    const int ngrp = 32 / L;
+    const bool active = grp < ngrp && gl < nvs;  // lanes past the last group only follow the loop
+    src.bind(v0, gl);
+    const int m = s_m;
+    for (;;) {
+      int i0 = 0;
+      if (lane == 0) i0 = atomicAdd(&s_next, ngrp);
+      i0 = __shfl_sync(0xffffffffu, i0, 0);
+      if (i0 >= m) break;
+      const int i = i0 + grp;
+      const bool has = i < m;
+      const int cell = has ? s_cell[i] : 0, beg = has ? s_beg[i] : 0, cnt = has ? s_cnt[i] : 0;
+      float acc[VE];
 #pragma unroll
-    for (int q = 0; q < VE; ++q) acc[q] = 0.f;
-    if (staged) {
-      sum_cell_pipelined<VE, PU>(s_perm + beg, (uint32_t)(pa + beg), cnt, src, active, acc);
-    } else {
-      PermStream ps;
-      if (!staged) ps.init(perm, pa + beg, pa + beg + cnt, lane);
-      for (int k = 0; k < cnt; k += PU) {
-        float v[PU][VE];
+      for (int q = 0; q < VE; ++q) acc[q] = 0.f;
+      if (staged) {
+        sum_cell_pipelined<VE, PU>(s_perm + beg, (uint32_t)(pa + beg), s_cnt[i0], cnt, src, active, acc);
+      } else {
+        sum_cell_streamed<VE, PU>(perm, pa + beg, cnt, lane, src, active, acc);
+      }
+      if (active && has) {
+        float* dst = acc_s + cell * row_f + gl * VE;
 #pragma unroll
-        for (int u = 0; u < PU; ++u) {
-          uint32_t pid = 0;
-          if (staged) {
-            if (k + u < cnt) pid = s_perm[beg + k + u];
-          } else {
-            pid = ps.at(pa + beg + k + u, lane);
-          }
-          if (k + u < cnt && active) {
-            src.load(pid, (uint32_t)(pa + beg + k + u), v[u]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < VE; ++q) v[u][q] = 0.f;
-          }
-        }
-        // ascending point order, one fp32 add per element per point
-#pragma unroll
-        for (int u = 0; u < PU; ++u) {
-          if (k + u < cnt) {
-#pragma unroll
-            for (int q = 0; q < VE; ++q) acc[q] = __fadd_rn(acc[q], v[u][q]);
-          }
-        }
+        for (int q = 0; q < VE; ++q) dst[q] = acc[q];
       }
     }
-    if (active) {
-      float* dst = acc_s + cell * row_f + lane * VE;
+  } else {
+    const bool active = lane < nvs;
+    src.bind(v0, lane);
+    const int m = s_m;
+    for (;;) {
+      int i = 0;
+      if (lane == 0) i = atomicAdd(&s_next, 1);
+      i = __shfl_sync(0xffffffffu, i, 0);
+      if (i >= m) break;
+      const int cell = s_cell[i], beg = s_beg[i], cnt = s_cnt[i];
+      float acc[VE];
 #pragma unroll
-      for (int q = 0; q < VE; ++q) dst[q] = acc[q];
+      for (int q = 0; q < VE; ++q) acc[q] = 0.f;
+      if (staged) {
+        sum_cell_pipelined<VE, PU>(s_perm + beg, (uint32_t)(pa + beg), cnt, cnt, src, active, acc);
+      } else {
+        sum_cell_streamed<VE, PU>(perm, pa + beg, cnt, lane, src, active, acc);
+      }
+      if (active) {
+        float* dst = acc_s + cell * row_f + lane * VE;
+#pragma unroll
+        for (int q = 0; q < VE; ++q) dst[q] = acc[q];
+      }
     }
   }
   __syncthreads();
@@ -956,21 +999,29 @@ __global__ __launch_bounds__(kGatherThreads) void bev_gather_kernel(const T* __r
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <class T, int VE, int PU, class Src>
-int launch_fwd_v(const Src& src, int64_t C, const Geometry& g, const PlanView& pv, void* out,
-               cudaStream_t st) {
+template <class T, int VE, int PU, class Src, bool G>
+int launch_fwd_g(const Src& src, int64_t C, const Geometry& g, const PlanView& pv, void* out, cudaStream_t st) {
   const int nvec = (int)(C / VE);
   const int slices = (nvec + 31) / 32;
   const int chs_full = (nvec < 32 ? nvec : 32) * VE;
   const size_t smem = (size_t)kTileCells * tile_row_bytes(chs_full, 4) + kPiecePoints * sizeof(uint32_t);
   if (smem > 48 * 1024)
-    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    BFB_CUDA(cudaFuncSetAttribute(bev_fwd_kernel<T, VE, PU, Src, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
   dim3 grid((unsigned)g.max_pieces, (unsigned)slices);
-  bev_fwd_kernel<T, VE, PU, Src><<<grid, kPoolThreads, smem, st>>>(
-      src, C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr, g.geo(),
-      static_cast<T*>(out));
+  bev_fwd_kernel<T, VE, PU, Src, G><<<grid, kPoolThreads, smem, st>>>(
+      src, C, nvec, g.dhw, g.tpb, pv.perm, pv.cell_se, pv.pieces, pv.hdr, g.geo(), static_cast<T*>(out));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
+}
+
+// Rows of at most 16 channel vectors are summed by lane groups (several cells
+// per warp at once); wider rows by whole warps.
+template <class T, int VE, int PU, class Src>
+int launch_fwd_v(const Src& src, int64_t C, const Geometry& g, const PlanView& pv, void* out,
+               cudaStream_t st) {
+  if (C / VE <= 16) return launch_fwd_g<T, VE, PU, Src, true>(src, C, g, pv, out, st);
+  return launch_fwd_g<T, VE, PU, Src, false>(src, C, g, pv, out, st);
 }
 
 // Pipeline depth of the forward gather: 8 rows for 4-byte features (96
