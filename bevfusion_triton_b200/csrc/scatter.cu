@@ -225,42 +225,46 @@ __global__ __launch_bounds__(kThreads) void seg_reduce_kernel(const T* __restric
   }
 }
 
+// Element kernels over n * c < 2^31 elements: 32-bit indices, the channel
+// split by a precomputed divisor (no 64-bit division per element).
 template <class T>
 __global__ void grad_sum_kernel(const T* __restrict__ gout, const int32_t* __restrict__ map,
-                                const int32_t* __restrict__ counts, int64_t n, int64_t c, int mean,
+                                const int32_t* __restrict__ counts, uint32_t total, FastDiv cdiv, int mean,
                                 T* __restrict__ gfeat) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n * c) return;
-  const int64_t i = idx / c, ch = idx - i * c;
-  const int32_t m = map[i];
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const uint32_t i = cdiv.div(idx), ch = idx - i * cdiv.d;
+  const int32_t m = __ldg(map + i);
   if (m < 0) {
     gfeat[idx] = from_f32<T>(0.f);
     return;
   }
-  float g = to_f32<T>(gout[(int64_t)m * c + ch]);
-  if (mean) g = __fdiv_rn(g, (float)counts[m]);
+  float g = to_f32<T>(__ldg(gout + (int64_t)m * cdiv.d + ch));
+  if (mean) g = __fdiv_rn(g, (float)__ldg(counts + m));
   gfeat[idx] = from_f32<T>(g);
 }
 
 template <class T>
 __global__ void grad_argmax_kernel(const T* __restrict__ feats, const T* __restrict__ reduced,
-                                   const int32_t* __restrict__ map, int64_t n, int64_t c, int32_t* __restrict__ from) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n * c) return;
-  const int64_t i = idx / c, ch = idx - i * c;
-  const int32_t m = map[i];
+                                   const int32_t* __restrict__ map, uint32_t total, FastDiv cdiv,
+                                   int32_t* __restrict__ from) {
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const uint32_t i = cdiv.div(idx), ch = idx - i * cdiv.d;
+  const int32_t m = __ldg(map + i);
   if (m < 0) return;
-  if (to_f32<T>(feats[idx]) == to_f32<T>(reduced[(int64_t)m * c + ch])) atomicMin(&from[(int64_t)m * c + ch], (int32_t)i);
+  const int64_t o = (int64_t)m * cdiv.d + ch;
+  if (to_f32<T>(__ldg(feats + idx)) == to_f32<T>(__ldg(reduced + o))) atomicMin(&from[o], (int32_t)i);
 }
 
 template <class T>
-__global__ void grad_max_scatter_kernel(const T* __restrict__ gout, const int32_t* __restrict__ from, int64_t m_total,
-                                        int64_t c, int64_t n, T* __restrict__ gfeat) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= m_total * c) return;
-  const int32_t src = from[idx];
-  const int64_t ch = idx % c;
-  if (src < n) gfeat[(int64_t)src * c + ch] = gout[idx];
+__global__ void grad_max_scatter_kernel(const T* __restrict__ gout, const int32_t* __restrict__ from, uint32_t total,
+                                        FastDiv cdiv, int64_t n, T* __restrict__ gfeat) {
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int32_t src = __ldg(from + idx);
+  const uint32_t ch = idx - cdiv.div(idx) * cdiv.d;
+  if (src < n) gfeat[(int64_t)src * cdiv.d + ch] = __ldg(gout + idx);
 }
 
 int width_of(int64_t max_value) {
@@ -367,8 +371,8 @@ int scatter_backward_t(void* gfeat, const void* gout, const void* feats, const v
   if (n == 0) return BFB_OK;
   const unsigned nb = (unsigned)ceil_div(n * c, kThreads);
   if (reduce != 2) {
-    grad_sum_kernel<T><<<nb, kThreads, 0, st>>>(static_cast<const T*>(gout), map, counts, n, c, reduce == 1,
-                                                static_cast<T*>(gfeat));
+    grad_sum_kernel<T><<<nb, kThreads, 0, st>>>(static_cast<const T*>(gout), map, counts, (uint32_t)(n * c),
+                                                FastDiv((uint32_t)c), reduce == 1, static_cast<T*>(gfeat));
     BFB_CHECK_LAUNCH();
     return BFB_OK;
   }
@@ -376,11 +380,11 @@ int scatter_backward_t(void* gfeat, const void* gout, const void* feats, const v
   if (m == 0) return BFB_OK;
   // from[] = n (no source) for every voxel channel
   BFB_CUDA(cudaMemsetAsync(from, 0x7f, sizeof(int32_t) * (size_t)(m * c), st));
-  grad_argmax_kernel<T><<<nb, kThreads, 0, st>>>(static_cast<const T*>(feats), static_cast<const T*>(reduced), map, n,
-                                                 c, from);
+  grad_argmax_kernel<T><<<nb, kThreads, 0, st>>>(static_cast<const T*>(feats), static_cast<const T*>(reduced), map,
+                                                 (uint32_t)(n * c), FastDiv((uint32_t)c), from);
   BFB_CHECK_LAUNCH();
   grad_max_scatter_kernel<T><<<(unsigned)ceil_div(m * c, kThreads), kThreads, 0, st>>>(
-      static_cast<const T*>(gout), from, m, c, n, static_cast<T*>(gfeat));
+      static_cast<const T*>(gout), from, (uint32_t)(m * c), FastDiv((uint32_t)c), n, static_cast<T*>(gfeat));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
