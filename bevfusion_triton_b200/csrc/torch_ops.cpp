@@ -13,9 +13,18 @@
 #include <utility>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "bfb_b200.h"
 
 namespace {
+
+// An NVTX range around every op (header-only NVTX3; inert unless a profiler
+// such as Nsight Systems is attached), named bfb_b200::<op>.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
 
 void check(int status, const char* what) {
   if (status == BFB_OK) return;
@@ -62,6 +71,7 @@ void check_plan(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t
 
 std::tuple<at::Tensor, at::Tensor> bev_pool_forward(const at::Tensor& feats_in, const at::Tensor& coords_in,
                                                      int64_t B, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_forward");
   require_cuda(feats_in, "feats");
   require_cuda(coords_in, "coords");
   TORCH_CHECK(feats_in.device() == coords_in.device(), "feats and coords must be on one device");
@@ -84,6 +94,7 @@ std::tuple<at::Tensor, at::Tensor> bev_pool_forward(const at::Tensor& feats_in, 
 }
 
 at::Tensor bev_pool_plan(const at::Tensor& coords_in, int64_t B, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_plan");
   require_cuda(coords_in, "coords");
   c10::cuda::CUDAGuard guard(coords_in.device());
   auto coords = coords_in.contiguous();
@@ -102,6 +113,7 @@ at::Tensor bev_pool_plan(const at::Tensor& coords_in, int64_t B, int64_t D, int6
 
 at::Tensor bev_pool_forward_planned(const at::Tensor& feats_in, const at::Tensor& plan, int64_t B, int64_t D,
                                     int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_forward_planned");
   require_cuda(feats_in, "feats");
   c10::cuda::CUDAGuard guard(feats_in.device());
   auto feats = feats_in.contiguous();
@@ -116,6 +128,7 @@ at::Tensor bev_pool_forward_planned(const at::Tensor& feats_in, const at::Tensor
 
 at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, int64_t n, int64_t B, int64_t D,
                              int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_backward");
   require_cuda(grad_in, "grad_out");
   c10::cuda::CUDAGuard guard(grad_in.device());
   auto grad = grad_in.contiguous();
@@ -144,6 +157,7 @@ at::Tensor bev_pool_backward(const at::Tensor& grad_in, const at::Tensor& plan, 
 }
 
 at::Tensor bev_pool_plan_cells(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_plan_cells");
   require_cuda(plan, "plan");
   c10::cuda::CUDAGuard guard(plan.device());
   check_plan(plan, n, B, D, H, W);
@@ -155,6 +169,7 @@ at::Tensor bev_pool_plan_cells(const at::Tensor& plan, int64_t n, int64_t B, int
 }
 
 bool bev_pool_plan_check(const at::Tensor& plan, int64_t n, int64_t B, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_plan_check");
   require_cuda(plan, "plan");
   c10::cuda::CUDAGuard guard(plan.device());
   const int s = bfb_bev_pool_plan_check(plan.data_ptr(), n, B, D, H, W, stream_of(plan));
@@ -164,6 +179,7 @@ bool bev_pool_plan_check(const at::Tensor& plan, int64_t n, int64_t B, int64_t D
 }
 
 int64_t bev_pool_invalid_count(const at::Tensor& plan) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_invalid_count");
   c10::cuda::CUDAGuard guard(plan.device());
   int64_t v = 0;
   check(bfb_bev_pool_invalid_count(plan.data_ptr(), &v, stream_of(plan)), "bev_pool invalid count");
@@ -174,6 +190,7 @@ int64_t bev_pool_invalid_count(const at::Tensor& plan) {
 std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward(const at::Tensor& depth_in, const at::Tensor& ctx_in,
                                                        const at::Tensor& coords_in, int64_t B, int64_t D, int64_t H,
                                                        int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_dc_forward");
   require_cuda(depth_in, "depth");
   require_cuda(ctx_in, "context");
   require_cuda(coords_in, "coords");
@@ -207,6 +224,7 @@ std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward(const at::Tensor& depth_i
 std::tuple<at::Tensor, at::Tensor> bev_pool_dc_forward_planned(const at::Tensor& depth_in, const at::Tensor& ctx_in,
                                                                const at::Tensor& plan, int64_t B, int64_t D, int64_t H,
                                                                int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_dc_forward_planned");
   require_cuda(depth_in, "depth");
   require_cuda(ctx_in, "context");
   require_cuda(plan, "plan");
@@ -238,6 +256,7 @@ at::Tensor bev_pool_geometry_plan(const at::Tensor& frustum_in, const at::Tensor
                                   const at::Tensor& trans_in, const std::optional<at::Tensor>& extra_rots_in,
                                   const std::optional<at::Tensor>& extra_trans_in, at::ArrayRef<double> lower,
                                   at::ArrayRef<double> dx, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_geometry_plan");
   require_cuda(frustum_in, "frustum");
   c10::cuda::CUDAGuard guard(frustum_in.device());
   auto f32 = [](const at::Tensor& t) { return t.contiguous().to(at::kFloat); };
@@ -284,6 +303,7 @@ at::Tensor bev_pool_geometry_plan(const at::Tensor& frustum_in, const at::Tensor
 std::tuple<at::Tensor, at::Tensor> bev_pool_dc_backward(const at::Tensor& grad_in, const at::Tensor& depth_in,
                                                         const at::Tensor& coords_in, const at::Tensor& aux,
                                                         int64_t c, int64_t B, int64_t D, int64_t H, int64_t W) {
+  NvtxRange nvtx_("bfb_b200::bev_pool_dc_backward");
   require_cuda(grad_in, "grad_out");
   c10::cuda::CUDAGuard guard(grad_in.device());
   auto grad = grad_in.contiguous().to(at::kFloat);
@@ -348,6 +368,7 @@ void require_contig(const at::Tensor& t, const char* name) {
 
 void dynamic_voxelize(const at::Tensor& points_in, at::Tensor& coors, c10::ArrayRef<double> voxel_size,
                       c10::ArrayRef<double> coors_range) {
+  NvtxRange nvtx_("bfb_b200::dynamic_voxelize");
   require_cuda(points_in, "points");
   require_cuda(coors, "coors");
   c10::cuda::CUDAGuard guard(points_in.device());
@@ -369,6 +390,7 @@ void hard_voxelize_batch(const at::Tensor& points_in, c10::ArrayRef<int64_t> off
                          at::Tensor& coors, at::Tensor& num_points, at::Tensor& voxel_num,
                          c10::ArrayRef<double> voxel_size, c10::ArrayRef<double> coors_range, int64_t max_points,
                          int64_t max_voxels, bool zero_tail) {
+  NvtxRange nvtx_("bfb_b200::hard_voxelize_batch");
   require_cuda(points_in, "points");
   c10::cuda::CUDAGuard guard(points_in.device());
   auto points = points_in.contiguous();
@@ -410,6 +432,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> voxelize_mean_epilogu
                                                                                   const at::Tensor& coors,
                                                                                   const at::Tensor& num_points,
                                                                                   const at::Tensor& voxel_num) {
+  NvtxRange nvtx_("bfb_b200::voxelize_mean_epilogue");
   require_cuda(voxels, "voxels");
   c10::cuda::CUDAGuard guard(voxels.device());
   TORCH_CHECK_VALUE(voxels.dim() == 4, "voxels must be [batch, max_voxels, max_points, F]");
@@ -438,6 +461,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> voxelize_mean_epilogu
 int64_t hard_voxelize(const at::Tensor& points, at::Tensor& voxels, at::Tensor& coors, at::Tensor& num_points,
                       c10::ArrayRef<double> voxel_size, c10::ArrayRef<double> coors_range, int64_t max_points,
                       int64_t max_voxels, bool zero_tail) {
+  NvtxRange nvtx_("bfb_b200::hard_voxelize");
   require_cuda(points, "points");
   c10::cuda::CUDAGuard guard(points.device());
   auto vn = at::empty({1}, points.options().dtype(at::kInt));
@@ -460,6 +484,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> dynamic_scatter_forwa
                                                                                    const at::Tensor& coors_in,
                                                                                    c10::string_view reduce,
                                                                                    at::OptionalIntArrayRef extents) {
+  NvtxRange nvtx_("bfb_b200::dynamic_scatter_forward");
   require_cuda(feats_in, "feats");
   require_cuda(coors_in, "coors");
   c10::cuda::CUDAGuard guard(feats_in.device());
@@ -489,6 +514,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> dynamic_scatter_forwa
 void dynamic_scatter_backward(at::Tensor& grad_feats, const at::Tensor& grad_out_in, const at::Tensor& feats_in,
                               const at::Tensor& reduced_in, const at::Tensor& map_in, const at::Tensor& counts_in,
                               c10::string_view reduce) {
+  NvtxRange nvtx_("bfb_b200::dynamic_scatter_backward");
   require_cuda(grad_feats, "grad_feats");
   c10::cuda::CUDAGuard guard(grad_feats.device());
   require_contig(grad_feats, "grad_feats");
@@ -517,6 +543,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> get_indice_pairs(const at::Tensor
                                                                 at::IntArrayRef out_shape, at::IntArrayRef ksize,
                                                                 at::IntArrayRef stride, at::IntArrayRef padding,
                                                                 at::IntArrayRef dilation, bool subm, bool transpose) {
+  NvtxRange nvtx_("bfb_b200::get_indice_pairs");
   require_cuda(indices_in, "indices");
   c10::cuda::CUDAGuard guard(indices_in.device());
   auto indices = indices_in.contiguous().to(at::kInt);
