@@ -322,7 +322,10 @@ def run_ours(args, ws, rank, local):
                                   'bev_bwd': round(phase[2], 4), 'voxelize': round(phase[3], 4)},
         'roofline': roofline, 'gpu_launches': launches, 'clocks': clocks,
     }
-    line['shard_check'] = shard_check(O, wl, out_last, g_last, ws, rank)
+    try:
+        line['shard_check'] = shard_check(O, wl, out_last, g_last, ws, rank)
+    except Exception as e:  # the parity check must not cost the benchmark line
+        line['shard_check'] = {'error': repr(e)[:300]}
     if not args.no_e2e:
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
     if not args.no_rulebook:
@@ -368,19 +371,22 @@ def shard_check(O, wl, out, g, ws, rank):
     dist.all_gather_object(allc, mine)
     res = None
     if rank == 0:
-        ok = True
-        for r in range(1, ws):
-            one = Workload(r, 1, wl.feats.device, ws, sample_offset=r * wl.S)
-            B, D, H, W = one.shape
-            plan = O.bev_pool_plan(one.coords, B, D, H, W)
-            o1 = O.bev_pool_forward_planned(one.feats, plan, B, D, H, W)
-            g1 = O.bev_pool_backward(one.up, plan, one.n, B, D, H, W)
-            O.hard_voxelize_batch(one.points, one.offs, one.voxels, one.vcoors, one.vnum, one.vn, one.vsize,
-                                  one.crange, one.mp, one.mv, False)
-            c1 = sample_checksums(O, o1, g1, (one.voxels, one.vcoors, one.vnum, one.vn.tolist()), one.n)[0]
-            ok = ok and c1 == allc[r][0]
-            del one
-        res = {'sample_checksums': [c for cs in allc for c in cs], 'recomputed': ws - 1, 'match': ok}
+        try:
+            ok = True
+            for r in range(1, ws):
+                one = Workload(r, 1, wl.feats.device, ws, sample_offset=r * wl.S)
+                B, D, H, W = one.shape
+                plan = O.bev_pool_plan(one.coords, B, D, H, W)
+                o1 = O.bev_pool_forward_planned(one.feats, plan, B, D, H, W)
+                g1 = O.bev_pool_backward(one.up, plan, one.n, B, D, H, W)
+                O.hard_voxelize_batch(one.points, one.offs, one.voxels, one.vcoors, one.vnum, one.vn, one.vsize,
+                                      one.crange, one.mp, one.mv, False)
+                c1 = sample_checksums(O, o1, g1, (one.voxels, one.vcoors, one.vnum, one.vn.tolist()), one.n)[0]
+                ok = ok and c1 == allc[r][0]
+                del one
+            res = {'sample_checksums': [c for cs in allc for c in cs], 'recomputed': ws - 1, 'match': ok}
+        except Exception as e:  # report, and still meet the other ranks at the barrier
+            res = {'sample_checksums': [c for cs in allc for c in cs], 'error': repr(e)[:300]}
     dist.barrier()
     return res
 
