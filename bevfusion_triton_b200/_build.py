@@ -47,26 +47,34 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f'build step failed: {cmd[0]} (exit {r.returncode})')
 
 
-def build_cuda_lib(verbose: bool = False) -> Path:
-    OBJ.mkdir(exist_ok=True)
+DEBUG_DIR = PKG / 'debug'
+
+
+def build_cuda_lib(verbose: bool = False, debug_checks: bool = False) -> Path:
+    """libbfb_b200.so; with ``debug_checks`` the debug variant (device index
+    checks counted into an error word, -DBFB_DEBUG_CHECKS) in ``debug/``."""
+    obj = OBJ / 'debug' if debug_checks else OBJ
+    lib = DEBUG_DIR / LIB.name if debug_checks else LIB
+    obj.mkdir(parents=True, exist_ok=True)
+    lib.parent.mkdir(exist_ok=True)
     hdrs = _headers()
     objs = []
     for src in CU_SOURCES:
         s = CSRC / src
         if not s.exists():
             continue
-        o = OBJ / (s.stem + '.o')
+        o = obj / (s.stem + '.o')
         objs.append(o)
         if _stale(o, [s] + hdrs):
             cmd = [NVCC, '-std=c++17', *GENCODE, '-lineinfo', '-O3', '-Xcompiler', '-fPIC',
-                   f'-I{INCLUDE}', '-c', str(s), '-o', str(o)]
+                   f'-I{INCLUDE}', '-c', str(s), '-o', str(o)] + (['-DBFB_DEBUG_CHECKS'] if debug_checks else [])
             if verbose:
                 cmd.insert(1, '-Xptxas=-v')
                 print(' '.join(cmd))
             _run(cmd)
-    if _stale(LIB, objs):
-        _run([NVCC, '-shared', *GENCODE, '-o', str(LIB), *map(str, objs), '-lcudart'])
-    return LIB
+    if _stale(lib, objs):
+        _run([NVCC, '-shared', *GENCODE, '-o', str(lib), *map(str, objs), '-lcudart'])
+    return lib
 
 
 def build_torch_ops() -> Path:
@@ -97,5 +105,8 @@ def build(verbose: bool = False) -> None:
 
 
 if __name__ == '__main__':
-    build(verbose='-v' in sys.argv)
-    print('built', LIB, TORCH_LIB)
+    if '--debug-checks' in sys.argv:
+        print('built', build_cuda_lib('-v' in sys.argv, debug_checks=True))
+    else:
+        build(verbose='-v' in sys.argv)
+        print('built', LIB, TORCH_LIB)

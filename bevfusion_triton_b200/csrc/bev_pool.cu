@@ -33,6 +33,9 @@
 #include "scan.cuh"
 
 namespace bfb {
+
+BFB_DEBUG_COUNTER();
+BFB_DEBUG_READER(debug_violations_bev)
 namespace {
 
 constexpr int kTileCells = 32;
@@ -657,7 +660,11 @@ __global__ __launch_bounds__(kPoolThreads) void bev_fwd_kernel(
   for (int i = threadIdx.x; i < kTileCells * row_f / 4; i += kPoolThreads)
     reinterpret_cast<float4*>(acc_s)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (staged)
-    for (int i = threadIdx.x; i < np; i += kPoolThreads) s_perm[i] = __ldg(perm + pa + i);
+    for (int i = threadIdx.x; i < np; i += kPoolThreads) {
+      uint32_t v = __ldg(perm + pa + i);
+      if (BFB_BAD(v < geo.n)) v = 0u;  // a corrupt plan: read row 0 instead of out of bounds
+      s_perm[i] = v;
+    }
   if (warp == 0) order_piece_cells(cell_se, r0, ca, cb, pa, s_cell, s_beg, s_cnt, &s_m);
   if (threadIdx.x == 0) s_next = 0;
   __syncthreads();
@@ -974,7 +981,8 @@ __global__ __launch_bounds__(kGatherThreads) void bev_gather_kernel(const T* __r
       if (l < total) {
         const uint32_t p = dv.div(l);
         const uint32_t ch = l - p * (uint32_t)nvec;
-        const uint32_t k = s_key[p];
+        uint32_t k = s_key[p];
+        if (BFB_BAD(k <= sentinel)) k = sentinel;  // a corrupt plan: zero row instead of out of bounds
         if (k != sentinel) {
           q[u] = load_vec<T, VE>(rv + (int64_t)k * nvec + ch);
         } else {
@@ -1165,6 +1173,7 @@ extern "C" int bfb_bev_pool_workspace_sizes(int64_t n, int64_t c, int64_t B, int
 extern "C" int bfb_bev_pool_plan(const void* coords, int itype, int64_t n, int64_t B, int64_t D,
                                  int64_t H, int64_t W, void* plan, size_t plan_bytes, void* scratch,
                                  size_t scratch_bytes, void* stream) {
+  BFB_INJECT_POINT();
   Geometry g;
   BFB_TRY(make_geometry(n, B, D, H, W, &g));
   if (itype != BFB_I32 && itype != BFB_I64) return BFB_ERR_UNSUPPORTED_DTYPE;
@@ -1205,6 +1214,7 @@ extern "C" int bfb_bev_pool_geometry_plan(const float* frustum, int64_t nd, int6
                                           int64_t B, int64_t ncam, const float* lower, const float* dx, int64_t D,
                                           int64_t H, int64_t W, void* plan, size_t plan_bytes, void* scratch,
                                           size_t scratch_bytes, void* stream) {
+  BFB_INJECT_POINT();
   if (nd <= 0 || fh <= 0 || fw <= 0 || ncam <= 0 || B <= 0) return BFB_ERR_INVALID_ARG;
   if (nd > 0x7fffffffLL / fh / fw || B > 0x7fffffffLL / ncam) return BFB_ERR_TOO_LARGE;
   const int64_t fpts = nd * fh * fw;
@@ -1239,6 +1249,7 @@ extern "C" int bfb_bev_pool_forward_planned(const void* feats, int dtype, int64_
                                             int64_t B, int64_t D, int64_t H, int64_t W,
                                             const void* plan, size_t plan_bytes, void* out,
                                             void* stream) {
+  BFB_INJECT_POINT();
   Geometry g;
   BFB_TRY(make_geometry(n, B, D, H, W, &g));
   BFB_TRY(check_channels(c));
@@ -1264,6 +1275,7 @@ extern "C" int bfb_bev_pool_forward(const void* feats, int dtype, const void* co
 extern "C" int bfb_bev_pool_backward(const void* gout, int dtype, int64_t n, int64_t c, int64_t B,
                                      int64_t D, int64_t H, int64_t W, const void* plan,
                                      size_t plan_bytes, void* gfeat, void* stream) {
+  BFB_INJECT_POINT();
   Geometry g;
   BFB_TRY(make_geometry(n, B, D, H, W, &g));
   BFB_TRY(check_channels(c));
@@ -1293,6 +1305,7 @@ extern "C" int bfb_bev_pool_backward_gather(const void* gout, int dtype, int64_t
                                             int64_t D, int64_t H, int64_t W, const void* plan,
                                             size_t plan_bytes, void* gfeat, void* workspace,
                                             size_t workspace_bytes, void* stream) {
+  BFB_INJECT_POINT();
   Geometry g;
   BFB_TRY(make_geometry(n, B, D, H, W, &g));
   BFB_TRY(check_channels(c));
@@ -1583,6 +1596,7 @@ extern "C" int bfb_bev_pool_dc_forward_planned(const float* depth, const float* 
                                                int64_t W, const void* plan, size_t plan_bytes, float* out,
                                                void* scratch, size_t scratch_bytes, void* aux, size_t aux_bytes,
                                                void* stream) {
+  BFB_INJECT_POINT();
   const DcDims dm{cams, nd, fh * fw, c};
   Geometry g;
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));
@@ -1640,6 +1654,7 @@ extern "C" int bfb_bev_pool_dc_backward(const float* grad_out, const float* dept
                                         int64_t D, int64_t H, int64_t W, const void* aux, size_t aux_bytes,
                                         void* ws, size_t ws_bytes, float* grad_depth, float* grad_context,
                                         void* stream) {
+  BFB_INJECT_POINT();
   const DcDims dm{cams, nd, fh * fw, c};
   Geometry g;
   BFB_TRY(make_geometry(dm.n(), B, D, H, W, &g));

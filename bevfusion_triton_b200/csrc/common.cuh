@@ -35,6 +35,48 @@ struct Carver {
   size_t bytes() const { return align_up(off); }
 };
 
+// Debug builds (-DBFB_DEBUG_CHECKS, `python -m bevfusion_triton_b200._build
+// --debug-checks`): device-side index checks count violations into a
+// per-file error word instead of trapping; BFB_BAD(ok) is true (and counted)
+// when `ok` fails, so the guarded access is skipped.  In release builds it
+// is the constant false and compiles away.
+#ifdef BFB_DEBUG_CHECKS
+#define BFB_DEBUG_COUNTER() static __device__ unsigned long long bfb_violations_ = 0ull
+#define BFB_BAD(ok) (!(ok) ? (atomicAdd(&bfb_violations_, 1ull), true) : false)
+#define BFB_DEBUG_READER(fn)                                                               \
+  int fn(uint64_t* v, int reset) {                                                         \
+    unsigned long long x = 0ull;                                                           \
+    BFB_CUDA(cudaMemcpyFromSymbol(&x, bfb_violations_, sizeof(x)));                        \
+    if (reset) {                                                                           \
+      const unsigned long long z = 0ull;                                                   \
+      BFB_CUDA(cudaMemcpyToSymbol(bfb_violations_, &z, sizeof(z)));                        \
+    }                                                                                      \
+    *v += x;                                                                               \
+    return BFB_OK;                                                                         \
+  }
+#else
+#define BFB_DEBUG_COUNTER() static_assert(true, "")
+#define BFB_BAD(ok) false
+#define BFB_DEBUG_READER(fn) \
+  int fn(uint64_t*, int) { return BFB_OK; }
+#endif
+
+// The error words of the kernel files (summed by bfb_debug_violations).
+int debug_violations_bev(uint64_t* v, int reset);
+int debug_violations_vox(uint64_t* v, int reset);
+int debug_violations_scatter(uint64_t* v, int reset);
+int debug_violations_spconv(uint64_t* v, int reset);
+int debug_violations_capi(uint64_t* v, int reset);
+
+// A status armed by bfb_debug_inject_status for the next calls of the main
+// entry points (host-side fault injection for tests), else BFB_OK.
+int injected_status();
+#define BFB_INJECT_POINT()                         \
+  do {                                             \
+    const int bfb_i_ = ::bfb::injected_status();   \
+    if (bfb_i_ != BFB_OK) return bfb_i_;           \
+  } while (0)
+
 // Records the CUDA error text for bfb_last_cuda_error() and maps it to a status.
 int record_cuda_error(cudaError_t e);
 // Counts one kernel launch of this library (bfb_kernel_launches()).

@@ -26,6 +26,9 @@
 #include "scan.cuh"
 
 namespace bfb {
+
+BFB_DEBUG_COUNTER();
+BFB_DEBUG_READER(debug_violations_scatter)
 namespace {
 
 constexpr int kThreads = 256;
@@ -157,6 +160,7 @@ __global__ void seg_assign_kernel(SortedKeys sk, const uint32_t* __restrict__ pe
     return;
   }
   const uint32_t m = vid[i + 1] - 1;  // inclusive count of heads up to i, minus one
+  if (BFB_BAD(m < (uint64_t)n)) return;
   map[p] = (int32_t)m;
   if (i == 0 || !sk.same(i, i - 1)) {
     seg[m] = (uint32_t)i;
@@ -406,6 +410,7 @@ extern "C" int bfb_dynamic_scatter_forward(const void* feats, int dtype, const i
                                            int64_t ndim, int reduce, const int64_t* extents, void* out_feats,
                                            int32_t* out_coors, int32_t* point2voxel, int32_t* counts,
                                            int64_t* num_voxels, void* ws, size_t ws_bytes, void* stream) {
+  BFB_INJECT_POINT();
   if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (n < 0 || c <= 0 || ndim < 1 || ndim > 4 || reduce < 0 || reduce > 2 || !num_voxels) return BFB_ERR_INVALID_ARG;
   if (n > 0x7ffffffeLL) return BFB_ERR_TOO_LARGE;
@@ -433,6 +438,7 @@ extern "C" int bfb_dynamic_scatter_backward(void* grad_feats, const void* grad_o
                                             const void* reduced, const int32_t* point2voxel, const int32_t* counts,
                                             int dtype, int64_t n, int64_t m, int64_t c, int reduce, int32_t* argmax_ws,
                                             size_t argmax_ws_bytes, void* stream) {
+  BFB_INJECT_POINT();
   if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (n < 0 || m < 0 || c <= 0 || reduce < 0 || reduce > 2) return BFB_ERR_INVALID_ARG;
   if (n * c > 0x7ffffffeLL || m * c > 0x7ffffffeLL) return BFB_ERR_TOO_LARGE;

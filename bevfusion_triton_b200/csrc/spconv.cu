@@ -31,6 +31,9 @@
 #include "scan.cuh"
 
 namespace bfb {
+
+BFB_DEBUG_COUNTER();
+BFB_DEBUG_READER(debug_violations_spconv)
 namespace {
 
 constexpr uint32_t kSpEmpty = 0xffffffffu;
@@ -215,6 +218,7 @@ __global__ void spc_pack_kernel(const uint32_t* __restrict__ pos, int64_t n, con
     const uint32_t p = pos[t];
     if (pos[t + 1] == p) continue;  // flag was 0
     const int64_t slot = (int64_t)(p - base);
+    if (BFB_BAD(slot < n)) continue;
     pairs[(k * 2 + 0) * n + slot] = (int32_t)j;
     pairs[(k * 2 + 1) * n + slot] = out_of[t];
   }
@@ -336,6 +340,7 @@ extern "C" int bfb_get_indice_pairs(const int32_t* indices, int64_t n, int ndim,
                                     const int64_t* padding, const int64_t* dilation, int subm, int transpose,
                                     int32_t* indice_pairs, int32_t* indice_num, int32_t* num_out_dev,
                                     void* workspace, size_t workspace_bytes, void* stream) {
+  BFB_INJECT_POINT();
   SpGeom g;
   BFB_TRY(make_sp_geom(ndim, batch, out_shape, ksize, stride, padding, dilation, transpose, &g));
   if (n < 0 || (n > 0 && (!indices || !indice_pairs)) || !indice_num || !num_out_dev) return BFB_ERR_INVALID_ARG;

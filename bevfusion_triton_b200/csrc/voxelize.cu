@@ -53,6 +53,9 @@
 #include "scan.cuh"
 
 namespace bfb {
+
+BFB_DEBUG_COUNTER();
+BFB_DEBUG_READER(debug_violations_vox)
 namespace {
 
 constexpr uint64_t kEmptyKey = ~0ull;
@@ -688,7 +691,8 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_members_kernel(
   if (threadIdx.x == 0) bsum[blockIdx.x] = total;
   uint32_t* row = mem + (int64_t)d * ps;
   if (d >= 0 && cnt <= (uint32_t)P) {
-    row[atomicAdd(fill + d, 1u)] = (uint32_t)p;
+    const uint32_t slot = atomicAdd(fill + d, 1u);
+    if (!BFB_BAD(slot < (uint32_t)P)) row[slot] = (uint32_t)p;  // more claims than the count said
   }
   // a larger voxel: at most P points of it per warp can be among its P smallest
   const int32_t big = (d >= 0 && cnt > (uint32_t)P) ? d : -1;
@@ -766,6 +770,7 @@ __global__ __launch_bounds__(kFastThreads) void vox_fast_copy_kernel(
           pos = 0;
           for (int q = 0; q < cnt; ++q) pos += __ldg(row + q) < m ? 1 : 0;
         }
+        if (BFB_BAD(pos < P)) pos = j;
         const T* src = pts + (int64_t)m * f;
         for (int64_t q = 0; q < f; ++q) dst[pos * f + q] = __ldg(src + q);
       } else {
@@ -968,6 +973,7 @@ using namespace bfb;
 
 extern "C" int bfb_dynamic_voxelize(const void* points, int dtype, int64_t n, int64_t f, const float* voxel_size,
                                     const float* coors_range, int32_t* coors, void* stream) {
+  BFB_INJECT_POINT();
   BFB_TRY(check_common(points, dtype, n, f));
   Grid gr;
   BFB_TRY(make_grid(voxel_size, coors_range, &gr));
@@ -1019,6 +1025,7 @@ extern "C" int bfb_hard_voxelize_batch(const void* points, int dtype, const int6
                                        int64_t max_points, int64_t max_voxels, void* voxels, int32_t* coors,
                                        int32_t* num_points, int32_t* voxel_num, int zero_tail, void* table,
                                        size_t table_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+  BFB_INJECT_POINT();
   BFB_TRY(check_common(points, dtype, n, f));
   if (batch < 1 || !offsets || !voxel_num) return BFB_ERR_INVALID_ARG;
   if (batch >= (1LL << (64 - kLinBits))) return BFB_ERR_TOO_LARGE;
@@ -1106,6 +1113,7 @@ extern "C" int bfb_voxelize_mean_epilogue(const void* voxels, int dtype, const i
                                           int64_t max_voxels, int64_t max_points, int64_t f, void* out_feats,
                                           int32_t* out_coords, int32_t* out_sizes, int32_t* total_dev,
                                           void* stream) {
+  BFB_INJECT_POINT();
   if (dtype_size(dtype) == 0) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (batch < 1 || max_voxels < 1 || max_points < 1 || f < 1) return BFB_ERR_INVALID_ARG;
   if (batch > kEpiMaxBatch) return BFB_ERR_TOO_LARGE;

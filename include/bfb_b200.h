@@ -61,6 +61,28 @@ const char* bfb_last_cuda_error(void);
 /* Number of kernels this library has launched in this process (all threads). */
 uint64_t bfb_kernel_launches(void);
 
+/* Debugging aids (no reference counterpart; the reference has no
+ * diagnostics on this path).
+ *
+ * A debug build (`python -m bevfusion_triton_b200._build --debug-checks`,
+ * which compiles with -DBFB_DEBUG_CHECKS into bevfusion_triton_b200/debug/)
+ * checks indices the kernels take from plans and workspaces (permutation
+ * entries, cell ranks, member slots, voxel and pair slots) and counts each
+ * violation into a device error word instead of trapping, skipping the
+ * access.  bfb_debug_checks_enabled() says which build is loaded;
+ * bfb_debug_violations() reads (and optionally clears) the summed error word
+ * of the current device, synchronously; bfb_debug_selftest(k) counts k
+ * synthetic violations (0 in a release build).
+ *
+ * bfb_debug_inject_status(status, calls): the next `calls` calls of the main
+ * entry points (plans, forwards, backwards, voxelisation, scatter, rulebook)
+ * return `status` at once, without touching their arguments -- host-side
+ * fault injection for testing error paths; status 0 disarms. */
+int bfb_debug_checks_enabled(void);
+int bfb_debug_violations(uint64_t* count, int reset);
+int bfb_debug_selftest(int k, void* stream);
+int bfb_debug_inject_status(int status, int calls);
+
 /* ------------------------------------------------------------------------
  * bev_pool: out[b, c, z, x, y] = sum_{n : coords[n] = (x, y, z, b)} feats[n, c]
  *

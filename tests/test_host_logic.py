@@ -159,3 +159,25 @@ def test_plan_of_another_geometry_is_refused():
 def test_plan_mismatch_status_string(cabi):
     cabi.bfb_status_string.restype = ctypes.c_char_p
     assert b'another geometry' in cabi.bfb_status_string(-7)
+
+
+def test_status_injection_returns_before_touching_arguments(cabi):
+    """Host-side fault injection: an armed status is returned by the next
+    entry-point calls without reading their (here invalid) pointers; then the
+    entry point validates its arguments as usual."""
+    i64 = ctypes.c_int64
+    assert cabi.bfb_debug_inject_status(-5, 2) == 0
+    args = (None, 1, i64(10), i64(1), i64(1), i64(2), i64(2), None, ctypes.c_size_t(0), None, ctypes.c_size_t(0),
+            None)
+    assert cabi.bfb_bev_pool_plan(*args) == -5
+    assert cabi.bfb_bev_pool_plan(*args) == -5
+    assert cabi.bfb_bev_pool_plan(*args) == -3  # disarmed: the missing workspace is reported
+    assert cabi.bfb_debug_inject_status(-1, 5) == 0
+    assert cabi.bfb_debug_inject_status(0, 0) == 0  # disarm
+    assert cabi.bfb_bev_pool_plan(*args) == -3
+    assert cabi.bfb_debug_inject_status(3, 1) == -1  # a positive status is not a status
+
+
+def test_release_build_has_no_debug_checks(cabi):
+    cabi.bfb_debug_checks_enabled.restype = ctypes.c_int
+    assert cabi.bfb_debug_checks_enabled() == 0
