@@ -48,6 +48,7 @@
 // (bfb_hard_voxelize_table_init) and every successful call leaves it clean.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 #include "scan.cuh"
@@ -222,6 +223,45 @@ __device__ __forceinline__ int sample_of(const int64_t* offs, int batch, int64_t
     if (__ldg(offs + mid) <= p) lo = mid; else hi = mid - 1;
   }
   return lo;
+}
+
+// Host -> device upload of the small per-call tables (sample offsets, tile
+// prefix) through kernel parameters: no pageable cudaMemcpyAsync, which may
+// wait for the stream before it returns and so stalls the launching thread
+// behind earlier work on the stream (and is not capturable into a graph).
+// The first launch also zeroes `nzero` words at `zero` (the call's
+// counters), which saves a memset.
+template <int W>
+struct UploadChunk {
+  int64_t v[W];
+};
+
+template <int W>
+__global__ void upload_words_kernel(const UploadChunk<W> c, int64_t* __restrict__ dst, int count,
+                                    uint32_t* __restrict__ zero, int nzero) {
+  for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = c.v[i];
+  for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
+}
+
+// W = 128 (1 KB of parameters) covers batches up to 63; larger tables go
+// in chunks of 2048 words (16 KB of the 32 KB parameter space).
+template <int W>
+int upload_chunks(int64_t* dst, const int64_t* src, size_t count, uint32_t* zero, int nzero, cudaStream_t st) {
+  UploadChunk<W> c;
+  size_t base = 0;
+  do {
+    const int m = (int)std::min<size_t>(W, count - base);
+    std::memcpy(c.v, src + base, sizeof(int64_t) * (size_t)m);
+    upload_words_kernel<W><<<1, 256, 0, st>>>(c, dst + base, m, base == 0 ? zero : nullptr, base == 0 ? nzero : 0);
+    BFB_CHECK_LAUNCH();
+    base += (size_t)m;
+  } while (base < count);
+  return BFB_OK;
+}
+
+int upload_words(int64_t* dst, const int64_t* src, size_t count, uint32_t* zero, int nzero, cudaStream_t st) {
+  return count <= 128 ? upload_chunks<128>(dst, src, count, zero, nzero, st)
+                      : upload_chunks<2048>(dst, src, count, zero, nzero, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -870,8 +910,7 @@ int hard_voxelize_impl(const void* points, int64_t n, int64_t f, const Grid& gr,
   const T* pts = static_cast<const T*>(points);
   const int64_t P = max_points < 0 ? n : max_points;
   const int64_t MV = max_voxels < 0 ? n : max_voxels;
-  BFB_CUDA(cudaMemcpyAsync(sv.offs, offs_host, sizeof(int64_t) * (size_t)(batch + 1), cudaMemcpyHostToDevice, st));
-  BFB_CUDA(cudaMemsetAsync(sv.err, 0, 4 * sizeof(uint32_t), st));
+  if (int rc = upload_words(sv.offs, offs_host, (size_t)(batch + 1), sv.err, 4, st)) return rc;
   const unsigned nb = (unsigned)ceil_div(n > 0 ? n : 1, kVoxThreads);
   if (n > 0) {
     vox_insert_kernel<T><<<nb, kVoxThreads, 0, st>>>(pts, n, f, gr, sv.offs, (int)batch, tb, sv.slot_of, sv.err);
@@ -930,9 +969,7 @@ int hard_voxelize_fast(const void* points, int64_t n, int64_t f, const Grid& gr,
     up[(size_t)(batch + 1 + s)] = tiles;
     if (s < batch) tiles += ceil_div(offs_host[s + 1] - offs_host[s], kFastThreads);
   }
-  // a pageable host source: the copy is staged before the call returns
-  BFB_CUDA(cudaMemcpyAsync(fv.offs, up.data(), sizeof(int64_t) * up.size(), cudaMemcpyHostToDevice, st));
-  BFB_CUDA(cudaMemsetAsync(fv.hdr, 0, sizeof(uint32_t) * 16, st));
+  if (int rc = upload_words(fv.offs, up.data(), up.size(), fv.hdr, 16, st)) return rc;
   if (tiles > 0) {
     vox_fast_insert_kernel<T><<<(unsigned)tiles, kFastThreads, 0, st>>>(pts, f, gr, fv.offs, fv.tpre, (int)batch, tb, ps,
                                                                         fv.did, fv.sd, fv.mem, fv.fill, fv.hdr);

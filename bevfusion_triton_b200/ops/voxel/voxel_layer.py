@@ -76,7 +76,8 @@ def hard_voxelize_batch(points: torch.Tensor, offsets: Sequence[int], voxel_size
     ``(voxels [B, max_voxels, max_points, F], coors [B, max_voxels, 3],
     num_points [B, max_voxels], voxel_num [B])`` on the device; rows past a
     sample's ``voxel_num`` are left unwritten unless ``zero_tail``.  No host
-    synchronisation."""
+    copy or synchronisation: the sample offsets travel as kernel parameters,
+    so the call can be captured into a CUDA graph."""
     voxel_size, coors_range, _ = _voxel_meta(voxel_size, coors_range, 3)
     _require_cuda(points)
     offsets = [int(o) for o in offsets]

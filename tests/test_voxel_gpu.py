@@ -153,6 +153,54 @@ def test_hard_voxelize_batch_matches_single(cuda):
         assert torch.equal(N[s, :vn].cpu(), n[:vn])
 
 
+def test_hard_voxelize_batch_many_samples(cuda):
+    """70 samples: the per-call offset and tile tables (2 x 71 words) go to
+    the device in more than one parameter upload; every sample still matches
+    its single-sample result."""
+    clouds = [synth.lidar_sweeps(s % 5)[: 300 + 97 * s] for s in range(70)]
+    offs = [0]
+    for c in clouds:
+        offs.append(offs[-1] + c.size(0))
+    pts = torch.cat(clouds).cuda()
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    V, C, N, VN = hard_voxelize_batch(pts, offs, vs, cr, 10, 2000)
+    for s in (0, 1, 63, 64, 69):
+        v, c, n, vn = run_hard(clouds[s], vs, cr, 10, 2000)
+        assert int(VN[s]) == vn
+        assert torch.equal(V[s, :vn].cpu(), v[:vn]) and torch.equal(C[s, :vn].cpu(), c[:vn])
+        assert torch.equal(N[s, :vn].cpu(), n[:vn])
+
+
+def test_hard_voxelize_batch_graph_capture(cuda):
+    """The batched call issues no host copy or synchronisation, so it can be
+    captured into a CUDA graph; replays over new points in the same buffers
+    give the eager results."""
+    from bevfusion_triton_b200._lib import ops
+    vs, cr = list(synth.LIDAR_VOXEL_SIZE), list(synth.LIDAR_RANGE)
+    sizes = [40000, 0, 35000]
+    offs = [0, 40000, 40000, 75000]
+    pts = torch.empty((75000, 5), device='cuda')
+    outs = (torch.empty((3, 8000, 10, 5), device='cuda'), torch.empty((3, 8000, 3), dtype=torch.int32, device='cuda'),
+            torch.empty((3, 8000), dtype=torch.int32, device='cuda'), torch.empty((3,), dtype=torch.int32, device='cuda'))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):  # warm-up on the capture stream: its hash table is made here
+            ops().hard_voxelize_batch(pts.zero_(), offs, *outs, vs, cr, 10, 8000, True)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        ops().hard_voxelize_batch(pts, offs, *outs, vs, cr, 10, 8000, True)
+    for seed in (3, 4):
+        pts.copy_(torch.cat([synth.lidar_sweeps(seed)[:40000], synth.lidar_sweeps(seed + 1)[:35000]]).cuda())
+        g.replay()
+        torch.cuda.synchronize()
+        V, C, N, VN = hard_voxelize_batch(pts, offs, vs, cr, 10, 8000, True)
+        assert torch.equal(VN, outs[3]) and torch.equal(C, outs[1]) and torch.equal(N, outs[2])
+        assert torch.equal(V, outs[0])
+    assert int(outs[3][1]) == 0 and sizes[1] == 0
+
+
 def test_voxelize_batch_mean_features(cuda):
     """The one-launch epilogue against the reference composition
     (models/fusion_models/bevfusion.py:269-296: per-sample voxelisation, batch
