@@ -10,6 +10,8 @@ box) together with a SHA-256 manifest:
 * ``ops/voxel/src/``     -> ``voxelization_triton.hard_voxelize`` (:674-710),
   ``dynamic_voxelize`` (:428-463), ``scatter_points_triton.dynamic_point_to_voxel_forward``
   / ``_backward`` (:253-424)
+* ``ops/spconv/src/``    -> ``spconv_triton.get_indice_pairs`` (:918-957), ``indice_conv``
+  (:981-1007), ``indice_conv_backward`` (:1035-1061), ``indice_maxpool`` (:1064-1082)
 
 The reference project has no installable package layout (``pip install``
 fails on setuptools' flat-layout discovery), and importing its ``ops``
@@ -30,7 +32,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / '_ref'
 MANIFEST = REF_DIR / 'manifest.json'
-PACKAGES = {'bev_pool_src': 'ops/bev_pool/src', 'voxel_src': 'ops/voxel/src'}
+PACKAGES = {'bev_pool_src': 'ops/bev_pool/src', 'voxel_src': 'ops/voxel/src', 'spconv_src': 'ops/spconv/src'}
 SOURCE_ROOT = Path('/root/reference')
 
 
@@ -97,6 +99,20 @@ def load():
     _mods['vox'] = sys.modules['_bfbref_voxel_src.voxelization_triton']
     _mods['scatter'] = sys.modules['_bfbref_voxel_src.scatter_points_triton']
     return _mods['bev'], _mods['vox'], _mods['scatter']
+
+
+def load_spconv():
+    """The installed reference's ``spconv_triton`` module."""
+    if 'spconv' in _mods:
+        return _mods['spconv']
+    why = available()
+    if why:
+        raise RuntimeError(why)
+    if 'ops/spconv/src/spconv_triton.py' not in json.loads(MANIFEST.read_text())['files']:
+        raise RuntimeError('the installed reference copy predates the spconv package: rerun baseline/ref_triton.py')
+    _load_package('_bfbref_spconv_src', PACKAGES['spconv_src'])
+    _mods['spconv'] = sys.modules['_bfbref_spconv_src.spconv_triton']
+    return _mods['spconv']
 
 
 if __name__ == '__main__':

@@ -353,6 +353,11 @@ def run_ours(args, ws, rank, local):
         line['e2e'] = run_e2e(args, wl, ws, samples_total)
     if not args.no_rulebook:
         line['sparse_rulebook'] = run_rulebook(args, wl, ws)
+    if not args.no_spconv:
+        try:
+            line['sparse_conv'] = run_spconv(args, wl, ws)
+        except Exception as e:  # an extra leg must not cost the benchmark line
+            line['sparse_conv'] = {'error': repr(e)[:300]}
     if not args.no_triton:
         line['triton_reference'] = run_triton_reference(args, wl, ws)
     if not args.no_fused:
@@ -669,6 +674,83 @@ def run_extra_configs(args, rank, ws):
     return res
 
 
+def lidar_sites(wl):
+    """(b, x, y, z) int32 rows of the rank's voxelised LiDAR samples."""
+    vn = wl.vn.tolist()
+    return torch.cat([torch.cat((torch.full((int(vn[b]), 1), b, dtype=torch.int32, device=wl.vcoors.device),
+                                 wl.vcoors[b, :int(vn[b])]), 1) for b in range(wl.S)]).contiguous()
+
+
+SPCONV_LAYERS = [
+    # name, rulebook, cin, cout, dtype
+    ('subm_k3_16x16_f16', 'subm', 16, 16, torch.float16),
+    ('subm_k3_64x64_f16', 'subm', 64, 64, torch.float16),
+    ('subm_k3_64x64_bf16', 'subm', 64, 64, torch.bfloat16),
+    ('subm_k3_64x64_f32', 'subm', 64, 64, torch.float32),
+    ('down_k3_s2_32x64_f16', 'down', 32, 64, torch.float16),
+]
+
+
+def run_spconv(args, wl, ws):
+    """Sparse convolution over the rank's voxelised LiDAR samples (the sparse
+    encoder's submanifold and strided 3x3x3 layers at full resolution),
+    device-resident, forward and backward (input + filter gradients), ours
+    beside the reference's own GPU path (Triton gather, one matmul per rule,
+    Triton atomic scatter; installed unmodified under baseline/_ref).  ms per
+    call of all S samples, max over ranks; useful TFLOP/s = 2 * pairs * Cin *
+    Cout per pass (forward; the backward does twice that)."""
+    from bevfusion_triton_b200.ops.spconv import get_indice_pairs, indice_conv, indice_conv_backward
+    sys.path.insert(0, str(ROOT / 'baseline'))
+    import ref_triton
+    try:
+        rsc = ref_triton.load_spconv()
+    except Exception as e:  # the reference copy is optional for this leg
+        rsc, why = None, str(e)
+    idx = lidar_sites(wl)
+    shape = [1440, 1440, 41]
+    books = {'subm': get_indice_pairs(idx, wl.S, shape, ksize=3, padding=1, subm=True),
+             'down': get_indice_pairs(idx, wl.S, shape, ksize=3, stride=2, padding=1)}
+    g = torch.Generator(device='cuda').manual_seed(7)
+    k = max(3, min(args.steps, 10))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(ws)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        return max_over_ranks(s0.elapsed_time(s1), ws) / k
+
+    res = {'sites': int(idx.size(0)), 'reference': 'triton (baseline/_ref)' if rsc else f'unavailable: {why}'}
+    for name, book, cin, cout, dt in SPCONV_LAYERS:
+        outids, pairs, num = books[book]
+        n_in, n_out = idx.size(0), outids.size(0)
+        x = torch.randn(n_in, cin, device='cuda', generator=g).to(dt)
+        w = (torch.randn(27, cin, cout, device='cuda', generator=g) / (27 * cin) ** 0.5).to(dt)
+        gy = torch.randn(n_out, cout, device='cuda', generator=g).to(dt)
+        npairs = int(num.sum())
+        flop = 2.0 * npairs * cin * cout
+        fwd = timed(lambda: indice_conv(x, w, pairs, num, n_out))
+        bwd = timed(lambda: indice_conv_backward(x, w, gy, pairs, num))
+        r = {'pairs': npairs, 'out_sites': n_out, 'fwd_ms': round(fwd, 4), 'bwd_ms': round(bwd, 4),
+             'fwd_tflops': round(flop / fwd / 1e9, 2), 'bwd_tflops': round(2 * flop / bwd / 1e9, 2)}
+        if rsc is not None:
+            rf = timed(lambda: rsc.indice_conv(x, w, pairs, num, n_out))
+            rb = timed(lambda: rsc.indice_conv_backward(x, w, gy, pairs, num))
+            y, yr = indice_conv(x, w, pairs, num, n_out).float(), rsc.indice_conv(x, w, pairs, num, n_out).float()
+            r.update({'ref_fwd_ms': round(rf, 4), 'ref_bwd_ms': round(rb, 4),
+                      'fwd_speedup': round(rf / fwd, 2), 'bwd_speedup': round(rb / bwd, 2),
+                      'max_rel_diff_vs_ref': float(((y - yr).abs() / yr.abs().clamp(min=1.0)).max())})
+        res[name] = r
+    return res
+
+
 def run_rulebook(args, wl, ws):
     """Sparse-convolution rulebooks of the sparse encoder's layer kinds over
     the rank's voxelised LiDAR samples (the voxel sites of the step above,
@@ -677,9 +759,7 @@ def run_rulebook(args, wl, ws):
     count as in the reference."""
     from bevfusion_triton_b200.ops.spconv import get_indice_pairs
     S = wl.S
-    vn = wl.vn.tolist()
-    idx = torch.cat([torch.cat((torch.full((int(vn[b]), 1), b, dtype=torch.int32, device=wl.vcoors.device),
-                                wl.vcoors[b, :int(vn[b])]), 1) for b in range(S)]).contiguous()
+    idx = lidar_sites(wl)
     shape = [1440, 1440, 41]
     layers = {'subm_k3': dict(ksize=3, stride=1, padding=1, subm=True),
               'down_k3_s2': dict(ksize=3, stride=2, padding=1),
@@ -852,6 +932,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-fused', action='store_true')
     ap.add_argument('--no-rulebook', action='store_true')
+    ap.add_argument('--no-spconv', action='store_true', help='skip the sparse-convolution timings')
     ap.add_argument('--no-triton', action='store_true', help='skip timing the reference Triton GPU path')
     ap.add_argument('--no-extra', action='store_true', help='skip the config-4 and fp16 bev_pool timings')
     ap.add_argument('--serial', action='store_true', help='run the LiDAR voxelisation after the camera branch on one stream')

@@ -26,7 +26,8 @@ TORCH_LIB = PKG / '_bfb_torch.so'
 CUDA_HOME = os.environ.get('CUDA_HOME', '/usr/local/cuda')
 NVCC = os.path.join(CUDA_HOME, 'bin', 'nvcc')
 GENCODE = ['-gencode', 'arch=compute_100a,code=sm_100a']
-CU_SOURCES = ['capi.cu', 'scan.cu', 'radix.cu', 'bev_pool.cu', 'voxelize.cu', 'scatter.cu', 'spconv.cu']
+CU_SOURCES = ['capi.cu', 'scan.cu', 'radix.cu', 'bev_pool.cu', 'voxelize.cu', 'scatter.cu', 'spconv.cu',
+              'spconv_conv.cu']
 
 
 def _headers() -> list[Path]:

@@ -73,6 +73,7 @@ extern "C" int bfb_debug_violations(uint64_t* count, int reset) {
   BFB_TRY(bfb::debug_violations_vox(count, reset));
   BFB_TRY(bfb::debug_violations_scatter(count, reset));
   BFB_TRY(bfb::debug_violations_spconv(count, reset));
+  BFB_TRY(bfb::debug_violations_spconv_conv(count, reset));
   BFB_TRY(bfb::debug_violations_capi(count, reset));
   return BFB_OK;
 }

@@ -66,6 +66,7 @@ int debug_violations_bev(uint64_t* v, int reset);
 int debug_violations_vox(uint64_t* v, int reset);
 int debug_violations_scatter(uint64_t* v, int reset);
 int debug_violations_spconv(uint64_t* v, int reset);
+int debug_violations_spconv_conv(uint64_t* v, int reset);
 int debug_violations_capi(uint64_t* v, int reset);
 
 // A status armed by bfb_debug_inject_status for the next calls of the main

@@ -578,6 +578,146 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> get_indice_pairs(const at::Tensor
   return {outids, pairs, num};
 }
 
+// ------------------------------------------------------ sparse convolution
+namespace {
+
+struct Rulebook {
+  at::Tensor pairs, num;
+  int64_t K, cap;
+};
+
+Rulebook rulebook_of(const at::Tensor& pairs_in, const at::Tensor& num_in, const at::Tensor& like) {
+  require_cuda(pairs_in, "indice_pairs");
+  require_cuda(num_in, "indice_pair_num");
+  TORCH_CHECK_VALUE(pairs_in.dim() == 3 && pairs_in.size(1) == 2, "indice_pairs must be [K, 2, N]");
+  TORCH_CHECK_VALUE(num_in.numel() == pairs_in.size(0), "indice_pair_num must hold K counts");
+  TORCH_CHECK(pairs_in.device() == like.device() && num_in.device() == like.device(),
+              "features and the rulebook must be on one device");
+  return {pairs_in.to(at::kInt).contiguous(), num_in.to(at::kInt).contiguous(), pairs_in.size(0), pairs_in.size(2)};
+}
+
+// filters [*ksize, Cin, Cout] viewed [K, Cin, Cout]
+at::Tensor filters_of(const at::Tensor& filters, const at::Tensor& feats, int64_t* K, int64_t* cout) {
+  require_cuda(filters, "filters");
+  TORCH_CHECK_VALUE(filters.dim() >= 2 && filters.size(-2) == feats.size(1),
+                    "filters must be [..., Cin, Cout] with Cin = features.size(1)");
+  TORCH_CHECK_TYPE(filters.scalar_type() == feats.scalar_type(), "filters must have the dtype of features");
+  *cout = filters.size(-1);
+  *K = filters.numel() / std::max<int64_t>(1, feats.size(1) * *cout);
+  return filters.contiguous();
+}
+
+}  // namespace
+
+at::Tensor indice_conv(const at::Tensor& features_in, const at::Tensor& filters_in, const at::Tensor& indice_pairs,
+                       const at::Tensor& indice_pair_num, int64_t num_activate_out, bool inverse,
+                       const c10::optional<at::Tensor>& bias_in) {
+  NvtxRange nvtx_("bfb_b200::indice_conv");
+  require_cuda(features_in, "features");
+  c10::cuda::CUDAGuard guard(features_in.device());
+  TORCH_CHECK_VALUE(features_in.dim() == 2, "features must be [N, Cin]");
+  auto feats = features_in.contiguous();
+  int64_t K = 0, cout = 0;
+  auto filters = filters_of(filters_in, feats, &K, &cout);
+  auto rb = rulebook_of(indice_pairs, indice_pair_num, feats);
+  TORCH_CHECK_VALUE(rb.K == K, "indice_pairs has ", rb.K, " rules, the filters ", K, " offsets");
+  at::Tensor bias;
+  if (bias_in.has_value() && bias_in->defined()) {
+    bias = bias_in->to(feats.scalar_type()).contiguous();
+    require_cuda(bias, "bias");
+    TORCH_CHECK_VALUE(bias.numel() == cout, "bias must hold Cout values");
+  }
+  const int dt = dtype_code(feats);
+  size_t ws_b = 0;
+  check(bfb_indice_conv_workspace_size(feats.size(0), num_activate_out, K, feats.size(1), cout, rb.cap, dt, 0, &ws_b),
+        "indice_conv workspace query");
+  auto ws = at::empty({(int64_t)ws_b}, feats.options().dtype(at::kByte));
+  auto out = at::empty({num_activate_out, cout}, feats.options());
+  check(bfb_indice_conv(feats.data_ptr(), dt, feats.size(0), feats.size(1), filters.data_ptr(), K, cout,
+                        rb.pairs.data_ptr<int32_t>(), rb.cap, rb.num.data_ptr<int32_t>(), num_activate_out,
+                        inverse ? 1 : 0, bias.defined() ? bias.data_ptr() : nullptr, out.data_ptr(), ws.data_ptr(),
+                        ws_b, stream_of(feats)),
+        "indice_conv");
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor> indice_conv_backward(const at::Tensor& features_in, const at::Tensor& filters_in,
+                                                        const at::Tensor& out_bp_in, const at::Tensor& indice_pairs,
+                                                        const at::Tensor& indice_pair_num, bool inverse) {
+  NvtxRange nvtx_("bfb_b200::indice_conv_backward");
+  require_cuda(features_in, "features");
+  require_cuda(out_bp_in, "out_bp");
+  c10::cuda::CUDAGuard guard(features_in.device());
+  TORCH_CHECK_VALUE(features_in.dim() == 2 && out_bp_in.dim() == 2, "features and out_bp must be 2-D");
+  auto feats = features_in.contiguous();
+  int64_t K = 0, cout = 0;
+  auto filters = filters_of(filters_in, feats, &K, &cout);
+  auto gout = out_bp_in.to(feats.scalar_type()).contiguous();
+  TORCH_CHECK_VALUE(gout.size(1) == cout, "out_bp must be [num_out, Cout]");
+  auto rb = rulebook_of(indice_pairs, indice_pair_num, feats);
+  TORCH_CHECK_VALUE(rb.K == K, "indice_pairs has ", rb.K, " rules, the filters ", K, " offsets");
+  const int dt = dtype_code(feats);
+  size_t ws_b = 0;
+  check(bfb_indice_conv_workspace_size(feats.size(0), gout.size(0), K, feats.size(1), cout, rb.cap, dt, 1, &ws_b),
+        "indice_conv_backward workspace query");
+  auto ws = at::empty({(int64_t)ws_b}, feats.options().dtype(at::kByte));
+  auto gin = at::empty_like(feats);
+  auto gw = at::empty_like(filters);
+  check(bfb_indice_conv_backward(feats.data_ptr(), dt, feats.size(0), feats.size(1), filters.data_ptr(), K, cout,
+                                 gout.data_ptr(), gout.size(0), rb.pairs.data_ptr<int32_t>(), rb.cap,
+                                 rb.num.data_ptr<int32_t>(), inverse ? 1 : 0, gin.data_ptr(), gw.data_ptr(),
+                                 ws.data_ptr(), ws_b, stream_of(feats)),
+        "indice_conv_backward");
+  return {gin, gw};
+}
+
+at::Tensor indice_maxpool(const at::Tensor& features_in, const at::Tensor& indice_pairs,
+                          const at::Tensor& indice_pair_num, int64_t num_activate_out) {
+  NvtxRange nvtx_("bfb_b200::indice_maxpool");
+  require_cuda(features_in, "features");
+  c10::cuda::CUDAGuard guard(features_in.device());
+  TORCH_CHECK_VALUE(features_in.dim() == 2, "features must be [N, C]");
+  auto feats = features_in.contiguous();
+  auto rb = rulebook_of(indice_pairs, indice_pair_num, feats);
+  size_t ws_b = 0;
+  check(bfb_indice_maxpool_workspace_size(feats.size(0), num_activate_out, rb.K, 0, &ws_b),
+        "indice_maxpool workspace query");
+  auto ws = at::empty({std::max<int64_t>((int64_t)ws_b, 1)}, feats.options().dtype(at::kByte));
+  auto out = at::empty({num_activate_out, feats.size(1)}, feats.options());
+  check(bfb_indice_maxpool(feats.data_ptr(), dtype_code(feats), feats.size(0), feats.size(1),
+                           rb.pairs.data_ptr<int32_t>(), rb.K, rb.cap, rb.num.data_ptr<int32_t>(), num_activate_out,
+                           out.data_ptr(), ws.data_ptr(), ws_b, stream_of(feats)),
+        "indice_maxpool");
+  return out;
+}
+
+at::Tensor indice_maxpool_backward(const at::Tensor& features_in, const at::Tensor& out_features_in,
+                                   const at::Tensor& out_bp_in, const at::Tensor& indice_pairs,
+                                   const at::Tensor& indice_pair_num) {
+  NvtxRange nvtx_("bfb_b200::indice_maxpool_backward");
+  require_cuda(features_in, "features");
+  require_cuda(out_features_in, "out_features");
+  require_cuda(out_bp_in, "out_bp");
+  c10::cuda::CUDAGuard guard(features_in.device());
+  auto feats = features_in.contiguous();
+  auto y = out_features_in.to(feats.scalar_type()).contiguous();
+  auto gy = out_bp_in.to(feats.scalar_type()).contiguous();
+  TORCH_CHECK_VALUE(feats.dim() == 2 && y.dim() == 2 && y.sizes() == gy.sizes() && y.size(1) == feats.size(1),
+                    "features [N, C], out_features and out_bp [M, C]");
+  auto rb = rulebook_of(indice_pairs, indice_pair_num, feats);
+  size_t ws_b = 0;
+  check(bfb_indice_maxpool_workspace_size(feats.size(0), y.size(0), rb.K, 1, &ws_b),
+        "indice_maxpool_backward workspace query");
+  auto ws = at::empty({std::max<int64_t>((int64_t)ws_b, 1)}, feats.options().dtype(at::kByte));
+  auto gx = at::empty_like(feats);
+  check(bfb_indice_maxpool_backward(feats.data_ptr(), y.data_ptr(), gy.data_ptr(), dtype_code(feats), feats.size(0),
+                                    y.size(0), feats.size(1), rb.pairs.data_ptr<int32_t>(), rb.K, rb.cap,
+                                    rb.num.data_ptr<int32_t>(), gx.data_ptr(), ws.data_ptr(), ws_b,
+                                    stream_of(feats)),
+        "indice_maxpool_backward");
+  return gx;
+}
+
 TORCH_LIBRARY(bfb_b200, m) {
   m.def("bev_pool_forward(Tensor feats, Tensor coords, int B, int D, int H, int W) -> (Tensor, Tensor)");
   m.def("bev_pool_plan(Tensor coords, int B, int D, int H, int W) -> Tensor");
@@ -614,6 +754,16 @@ TORCH_LIBRARY(bfb_b200, m) {
   m.def(
       "dynamic_scatter_backward(Tensor(a!) grad_feats, Tensor grad_out, Tensor feats, Tensor reduced, Tensor map, "
       "Tensor counts, str reduce) -> ()");
+  m.def(
+      "indice_conv(Tensor features, Tensor filters, Tensor indice_pairs, Tensor indice_pair_num, "
+      "int num_activate_out, bool inverse=False, Tensor? bias=None) -> Tensor");
+  m.def(
+      "indice_conv_backward(Tensor features, Tensor filters, Tensor out_bp, Tensor indice_pairs, "
+      "Tensor indice_pair_num, bool inverse=False) -> (Tensor, Tensor)");
+  m.def("indice_maxpool(Tensor features, Tensor indice_pairs, Tensor indice_pair_num, int num_activate_out) -> Tensor");
+  m.def(
+      "indice_maxpool_backward(Tensor features, Tensor out_features, Tensor out_bp, Tensor indice_pairs, "
+      "Tensor indice_pair_num) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
@@ -635,4 +785,8 @@ TORCH_LIBRARY_IMPL(bfb_b200, CUDA, m) {
   m.impl("dynamic_scatter_forward", &dynamic_scatter_forward);
   m.impl("get_indice_pairs", &get_indice_pairs);
   m.impl("dynamic_scatter_backward", &dynamic_scatter_backward);
+  m.impl("indice_conv", &indice_conv);
+  m.impl("indice_conv_backward", &indice_conv_backward);
+  m.impl("indice_maxpool", &indice_maxpool);
+  m.impl("indice_maxpool_backward", &indice_maxpool_backward);
 }

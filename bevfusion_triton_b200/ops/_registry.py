@@ -12,7 +12,9 @@ and registers the backward of the differentiable ones
   (the reference's autograd pair, ops/bev_pool/src/bev_pool_triton.py:153-216);
 * ``bev_pool_dc_forward`` / ``bev_pool_dc_forward_planned`` -> ``bev_pool_dc_backward``;
 * ``dynamic_scatter_forward`` -> ``dynamic_scatter_backward``
-  (ops/voxel/scatter_points.py:8-50, scatter_points_triton.py:348-424).
+  (ops/voxel/scatter_points.py:8-50, scatter_points_triton.py:348-424);
+* ``indice_conv`` -> ``indice_conv_backward`` and ``indice_maxpool`` ->
+  ``indice_maxpool_backward`` (ops/spconv/functional.py:21-110).
 
 Workspace sizes in the fake kernels come from the library's host-only size
 queries, so a traced plan tensor has exactly the size the real op returns.
@@ -156,6 +158,22 @@ def _register_fakes() -> None:
     def _(grad_feats, grad_out, feats, reduced, map, counts, reduce):
         return None
 
+    @reg(lib + 'indice_conv')
+    def _(features, filters, indice_pairs, indice_pair_num, num_activate_out, inverse=False, bias=None):
+        return features.new_empty((num_activate_out, filters.size(-1)))
+
+    @reg(lib + 'indice_conv_backward')
+    def _(features, filters, out_bp, indice_pairs, indice_pair_num, inverse=False):
+        return torch.empty_like(features), torch.empty_like(filters, memory_format=torch.contiguous_format)
+
+    @reg(lib + 'indice_maxpool')
+    def _(features, indice_pairs, indice_pair_num, num_activate_out):
+        return features.new_empty((num_activate_out, features.size(1)))
+
+    @reg(lib + 'indice_maxpool_backward')
+    def _(features, out_features, out_bp, indice_pairs, indice_pair_num):
+        return torch.empty_like(features)
+
 
 def _register_autograd() -> None:
     O = torch.ops.bfb_b200
@@ -214,6 +232,31 @@ def _register_autograd() -> None:
 
     torch.library.register_autograd('bfb_b200::dynamic_scatter_forward', scatter_backward,
                                     setup_context=scatter_setup)
+
+    # sparse convolution: gradients w.r.t. features, filters and the bias
+    def conv_setup(ctx, inputs, output):
+        features, filters, pairs, num, _, inverse, bias = inputs
+        ctx.save_for_backward(features, filters, pairs, num)
+        ctx.inverse = inverse
+        ctx.has_bias = bias is not None
+
+    def conv_backward(ctx, grad):
+        features, filters, pairs, num = ctx.saved_tensors
+        gin, gw = O.indice_conv_backward(features, filters, grad.contiguous(), pairs, num, ctx.inverse)
+        gb = grad.sum(0) if ctx.has_bias else None
+        return gin, gw.view_as(filters), None, None, None, None, gb
+
+    torch.library.register_autograd('bfb_b200::indice_conv', conv_backward, setup_context=conv_setup)
+
+    def pool_setup(ctx, inputs, output):
+        features, pairs, num, _ = inputs
+        ctx.save_for_backward(features, output, pairs, num)
+
+    def pool_backward(ctx, grad):
+        features, out, pairs, num = ctx.saved_tensors
+        return O.indice_maxpool_backward(features, out, grad.contiguous(), pairs, num), None, None, None
+
+    torch.library.register_autograd('bfb_b200::indice_maxpool', pool_backward, setup_context=pool_setup)
 
 
 def register() -> None:

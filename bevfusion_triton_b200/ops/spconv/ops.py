@@ -1,4 +1,7 @@
-"""Sparse-convolution rulebook (``get_indice_pairs``) on the sm_100a kernels.
+"""Sparse-convolution rulebook (``get_indice_pairs``) and the convolution /
+max-pooling over it (``indice_conv``, ``fused_indice_conv``,
+``indice_conv_backward``, ``indice_maxpool``, ``indice_maxpool_backward``,
+ops/spconv/ops.py:95-188) on the sm_100a kernels.
 
 Reference: ops/spconv/ops.py:25-93 (output-size helpers, ``get_indice_pairs``)
 and ops/spconv/src/spconv_triton.py:608-652 (argument checks), :792-915 (the
@@ -80,3 +83,60 @@ def get_indice_pairs(indices: torch.Tensor, batch_size: int, spatial_shape, ksiz
         outids = indices
     dt = indices.dtype
     return outids.to(dt), pairs.to(dt), num.to(dt)
+
+
+# --------------------------------------------------------------- convolution
+def _require_cuda(*ts) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
+
+
+def indice_conv(features: torch.Tensor, filters: torch.Tensor, indice_pairs: torch.Tensor,
+                indice_pair_num: torch.Tensor, num_activate_out: int, inverse: bool = False,
+                subm: bool = False) -> torch.Tensor:
+    """[num_activate_out, Cout]: every output row sums, over the kernel
+    offsets k in ascending order, features[in] @ filters[k] for the rule-k
+    pair (in, out) that names it (ops/spconv/ops.py:95-114 ->
+    spconv_triton.py:981-1007).  ``inverse`` swaps the two pair slots;
+    ``subm`` changes nothing here, as in the reference.  One launch over all
+    rules, no host read of the rule counts; differentiable w.r.t. features and
+    filters."""
+    del subm
+    _require_cuda(features, filters, indice_pairs, indice_pair_num)
+    return ops().indice_conv(features, filters, indice_pairs, indice_pair_num, int(num_activate_out),
+                             bool(inverse), None)
+
+
+def fused_indice_conv(features, filters, bias, indice_pairs, indice_pair_num, num_activate_out, inverse, subm):
+    """indice_conv + bias, the bias added in the kernel's epilogue; as in the
+    reference (spconv_triton.py:1010-1032) a submanifold convolution adds no
+    bias here."""
+    _require_cuda(features, filters, indice_pairs, indice_pair_num)
+    return ops().indice_conv(features, filters, indice_pairs, indice_pair_num, int(num_activate_out),
+                             bool(inverse), None if subm else bias)
+
+
+def indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_num, inverse: bool = False,
+                         subm: bool = False):
+    """(input_grad [N, Cin], filters_grad shaped like filters)
+    (spconv_triton.py:1035-1061); the filter gradient is summed in a fixed
+    order, so it is deterministic."""
+    del subm
+    _require_cuda(features, filters, out_bp, indice_pairs, indice_pair_num)
+    gin, gw = ops().indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_num, bool(inverse))
+    return gin, gw.view_as(filters)
+
+
+def indice_maxpool(features, indice_pairs, indice_pair_num, num_activate_out):
+    """[num_activate_out, C]: max over each output's inputs, never below 0
+    (the reference pools into zeros, spconv_triton.py:1064-1082)."""
+    _require_cuda(features, indice_pairs, indice_pair_num)
+    return ops().indice_maxpool(features, indice_pairs, indice_pair_num, int(num_activate_out))
+
+
+def indice_maxpool_backward(features, out_features, out_bp, indice_pairs, indice_pair_num):
+    """input_grad [N, C]: every input equal to its output's pooled value
+    receives that output's gradient (spconv_triton.py:1085-1111)."""
+    _require_cuda(features, out_features, out_bp, indice_pairs, indice_pair_num)
+    return ops().indice_maxpool_backward(features, out_features, out_bp, indice_pairs, indice_pair_num)

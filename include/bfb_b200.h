@@ -411,6 +411,69 @@ int bfb_indice_pairs_outids(int64_t n, int ndim, int64_t batch, const int64_t* o
                             const int64_t* ksize, const void* workspace_dev, size_t workspace_bytes,
                             int32_t* outids_dev, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Sparse convolution and sparse max-pooling over a rulebook.  Replace
+ * indice_conv / fused_indice_conv / indice_conv_backward / indice_maxpool /
+ * indice_maxpool_backward (ops/spconv/ops.py:95-188 ->
+ * ops/spconv/src/spconv_triton.py:981-1111).
+ *
+ * features [n_in, cin]; filters [K, cin, cout] (the reference's
+ * [*ksize, Cin, Cout] viewed flat), same dtype; indice_pairs [K, 2, pair_cap]
+ * int32 and indice_num [K] int32 on the device, as bfb_get_indice_pairs
+ * writes them: rule k's pair i joins input indice_pairs[k, s, i] to output
+ * indice_pairs[k, 1 - s, i], s = inverse ? 1 : 0, for i < indice_num[k].
+ * A rulebook holds at most one pair per (output, k) and per (input, k);
+ * pairs naming rows outside [0, n_in) x [0, n_out) are ignored.
+ *
+ * out [n_out, cout] is fully written: out[o] = sum over k ascending of
+ * features[in(o, k)] @ filters[k], accumulated in fp32 and rounded once, then
+ * + bias (nullable; the reference's fused form rounds the sum and the biased
+ * value separately, and so does this).  fp16 / bf16 with cin and cout
+ * multiples of 16 (cout <= 256) run on the tensor cores; everything else
+ * (fp32 included) on fp32 FMA.  K <= 125, cin, cout <= 256.  The workspace
+ * (bfb_indice_conv_workspace_size, backward = 0 or 1) holds the neighbour
+ * table and the filters in the kernels' layout.
+ * ---------------------------------------------------------------------- */
+int bfb_indice_conv_workspace_size(int64_t n_in, int64_t n_out, int64_t K, int64_t cin, int64_t cout,
+                                   int64_t pair_cap, int dtype, int backward, size_t* bytes);
+
+int bfb_indice_conv(const void* features_dev, int dtype, int64_t n_in, int64_t cin, const void* filters_dev,
+                    int64_t K, int64_t cout, const int32_t* indice_pairs_dev, int64_t pair_cap,
+                    const int32_t* indice_num_dev, int64_t n_out, int inverse, const void* bias_dev,
+                    void* out_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* input_grad [n_in, cin] = sum over k ascending of out_bp[out(i, k)] @
+ * filters[k]^T (0 rows for inputs in no pair); filters_grad [K, cin, cout] =
+ * sum over rule k's pairs of features[in]^T out_bp[out], in fp32, summed over
+ * fixed chunks of pairs in a fixed order (deterministic). */
+int bfb_indice_conv_backward(const void* features_dev, int dtype, int64_t n_in, int64_t cin,
+                             const void* filters_dev, int64_t K, int64_t cout, const void* out_bp_dev,
+                             int64_t n_out, const int32_t* indice_pairs_dev, int64_t pair_cap,
+                             const int32_t* indice_num_dev, int inverse, void* input_grad_dev,
+                             void* filters_grad_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* Max-pooling: out [n_out, C] = max(0, max over the output's inputs) (the
+ * reference pools into zeros with include_self).  Backward: input_grad
+ * [n_in, C] = sum over k ascending of out_bp where features == out_features
+ * (every equal maximum receives it), rounded to the dtype after each add.
+ * Workspace: one int32 per (row, k) (bfb_indice_maxpool_workspace_size). */
+int bfb_indice_maxpool_workspace_size(int64_t n_in, int64_t n_out, int64_t K, int backward, size_t* bytes);
+
+int bfb_indice_maxpool(const void* features_dev, int dtype, int64_t n_in, int64_t C,
+                       const int32_t* indice_pairs_dev, int64_t K, int64_t pair_cap,
+                       const int32_t* indice_num_dev, int64_t n_out, void* out_dev, void* workspace_dev,
+                       size_t workspace_bytes, void* stream);
+
+int bfb_indice_maxpool_backward(const void* features_dev, const void* out_features_dev, const void* out_bp_dev,
+                                int dtype, int64_t n_in, int64_t n_out, int64_t C,
+                                const int32_t* indice_pairs_dev, int64_t K, int64_t pair_cap,
+                                const int32_t* indice_num_dev, void* input_grad_dev, void* workspace_dev,
+                                size_t workspace_bytes, void* stream);
+
+/* Number of bounded waits in the tensor-core convolution that gave up (0 in
+ * a correct run); reset = 1 clears it.  No reference counterpart. */
+int bfb_spconv_timeouts(uint64_t* count, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -158,3 +158,68 @@ def indice_pairs(indices, out_shape, ksize, stride, padding, dilation, subm, tra
     outids = np.zeros((max(n * K, 1), nd + 1), dtype=np.int32)
     m = lib().oracle_indice_pairs(idx, n, nd, *a, int(bool(subm)), int(bool(transpose)), pairs, num, outids)
     return outids[:m], pairs, num
+
+
+# ----------------------------------------------------- sparse convolution
+# Restatements in numpy of ops/spconv/src/spconv_triton.py:967-1111 (the
+# reference's CPU path: index_select gather, one matmul per rule, index_add_
+# scatter, rules in ascending order).  The convolution is accumulated in
+# float64 (the checker's reference value); max-pooling in the input dtype, as
+# the reference's scatter_reduce / index_add_ on a tensor of that dtype.
+
+def _rules(pairs, num, inverse):
+    """(k, in_idx, out_idx) of every rule with pairs, spconv_triton.py:967-978."""
+    pairs = np.asarray(pairs)
+    num = np.asarray(num)
+    si, so = (1, 0) if inverse else (0, 1)
+    for k in range(pairs.shape[0]):
+        m = int(num[k])
+        if m > 0:
+            yield k, pairs[k, si, :m].astype(np.int64), pairs[k, so, :m].astype(np.int64)
+
+
+def indice_conv(features, filters, pairs, num, n_out, inverse=False, bias=None):
+    """spconv_triton.py:981-1007 (+ :1010-1032 with ``bias``), float64."""
+    x = np.asarray(features, np.float64)
+    cin = x.shape[1]
+    w = np.asarray(filters, np.float64).reshape(-1, cin, np.asarray(filters).shape[-1])
+    out = np.zeros((n_out, w.shape[2]), np.float64)
+    for k, i, o in _rules(pairs, num, inverse):
+        np.add.at(out, o, x[i] @ w[k])
+    if bias is not None:
+        out = out + np.asarray(bias, np.float64)
+    return out
+
+
+def indice_conv_backward(features, filters, out_bp, pairs, num, inverse=False):
+    """spconv_triton.py:1035-1061, float64: (input_grad, filters_grad)."""
+    x = np.asarray(features, np.float64)
+    cin = x.shape[1]
+    w = np.asarray(filters, np.float64).reshape(-1, cin, np.asarray(filters).shape[-1])
+    g = np.asarray(out_bp, np.float64)
+    gx = np.zeros_like(x)
+    gw = np.zeros_like(w)
+    for k, i, o in _rules(pairs, num, inverse):
+        gw[k] += x[i].T @ g[o]
+        np.add.at(gx, i, g[o] @ w[k].T)
+    return gx, gw.reshape(np.asarray(filters).shape)
+
+
+def indice_maxpool(features, pairs, num, n_out):
+    """spconv_triton.py:1064-1082: max into zeros (include_self), exact."""
+    x = np.asarray(features)
+    out = np.zeros((n_out, x.shape[1]), x.dtype)
+    for _, i, o in _rules(pairs, num, False):
+        np.maximum.at(out, o, x[i])
+    return out
+
+
+def indice_maxpool_backward(features, out_features, out_bp, pairs, num):
+    """spconv_triton.py:1085-1111: index_add_ in the dtype, rules ascending."""
+    x = np.asarray(features)
+    y = np.asarray(out_features)
+    g = np.asarray(out_bp)
+    gx = np.zeros_like(x)
+    for _, i, o in _rules(pairs, num, False):
+        np.add.at(gx, i, np.where(x[i] == y[o], g[o], np.zeros_like(g[o])))
+    return gx

@@ -13,12 +13,16 @@ package modules:
 * ops/voxel/src/voxelization_triton.py           ``dynamic_voxelize``, ``hard_voxelize``
 * ops/voxel/src/scatter_points_triton.py         ``dynamic_point_to_voxel_forward/backward``
 * ops/spconv/src/spconv_triton.py                ``_get_indice_pairs_impl`` (rulebooks, with the
-                                                 GPU path's output order: cuda_ordering=True)
+                                                 GPU path's output order: cuda_ordering=True);
+                                                 ``indice_conv``, ``fused_indice_conv``,
+                                                 ``indice_conv_backward``, ``indice_maxpool(_backward)``
+                                                 on CPU tensors (their CPU gather / index_add_ path)
 * models/vtransforms/base.py                     ``BaseTransform.get_geometry`` and the quantise +
                                                  in-grid filter of ``BaseTransform.bev_pool``
                                                  (with models/helper/amp.py ``force_fp32``)
 
-``--only spconv`` / ``--only geometry`` regenerate only that fixture.
+``--only spconv`` / ``--only spconv_conv`` / ``--only geometry`` regenerate only
+that fixture.
 
 Cases mirror the reference tests (tests/test_ops/test_bev_pool.py:24-84,
 tests/test_ops/test_voxel.py:27-79) plus seeded larger cases and full-size
@@ -177,6 +181,49 @@ def spconv_cases(sct):
     save('spconv_cases', **out)
 
 
+SPCONV_CONV_CASES = [
+    # rulebook case of SPCONV_CASES, cin, cout, inverse
+    (4, 16, 32, False),   # submanifold 3x3x3
+    (2, 16, 16, False),   # strided 3x3x3
+    (8, 5, 16, False),    # strided, odd input channels (the encoder's first layer width)
+    (5, 32, 16, False),   # transposed
+    (2, 16, 16, True),    # strided rulebook used inverse (SparseInverseConv3d)
+]
+
+
+def spconv_conv_cases(sct):
+    """Sparse convolution, its backward and sparse max-pooling run by the
+    reference on CPU tensors over the rulebooks of ``spconv_cases`` (read back
+    from spconv_cases.npz), seeded fp32 features / filters / gradients."""
+    rb = np.load(HERE / 'spconv_cases.npz')
+    g = torch.Generator().manual_seed(23)
+    out = {}
+    for j, (c, cin, cout, inverse) in enumerate(SPCONV_CONV_CASES):
+        pairs = torch.from_numpy(rb[f'c{c}_pairs'])
+        num = torch.from_numpy(rb[f'c{c}_num'])
+        n_idx = rb[f'c{c}_indices'].shape[0]
+        n_out_ids = rb[f'c{c}_outids'].shape[0]
+        n_in, n_out = (n_out_ids, n_idx) if inverse else (n_idx, n_out_ids)
+        K = pairs.shape[0]
+        x = torch.randn(n_in, cin, generator=g)
+        w = torch.randn(K, cin, cout, generator=g) * 0.2
+        bias = torch.randn(cout, generator=g)
+        gy = torch.randn(n_out, cout, generator=g)
+        y = sct.indice_conv(x, w, pairs, num, n_out, inverse=inverse)
+        yb = sct.fused_indice_conv(x, w, bias, pairs, num, n_out, inverse, False)
+        gx, gw = sct.indice_conv_backward(x, w, gy, pairs, num, inverse=inverse)
+        out.update({f'v{j}_case': np.array([c, cin, cout, int(inverse), n_in, n_out]), f'v{j}_x': x, f'v{j}_w': w,
+                    f'v{j}_bias': bias, f'v{j}_gy': gy, f'v{j}_y': y, f'v{j}_yb': yb, f'v{j}_gx': gx, f'v{j}_gw': gw})
+        if not inverse:
+            xp = torch.randn(n_in, cin, generator=g)
+            xp[:, 0] = -xp[:, 0].abs()  # an all-negative channel: pooled into zeros
+            yp = sct.indice_maxpool(xp, pairs, num, n_out)
+            gyp = torch.randn(n_out, cin, generator=g)
+            gxp = sct.indice_maxpool_backward(xp, yp, gyp, pairs, num)
+            out.update({f'v{j}_xp': xp, f'v{j}_yp': yp, f'v{j}_gyp': gyp, f'v{j}_gxp': gxp})
+    save('spconv_conv_cases', **out)
+
+
 def sha(a) -> str:
     a = np.ascontiguousarray(np.asarray(a))
     return hashlib.sha256(a.tobytes()).hexdigest()
@@ -327,6 +374,9 @@ def main():
     if only == 'spconv':
         spconv_cases(import_spconv())
         return
+    if only == 'spconv_conv':
+        spconv_conv_cases(import_spconv())
+        return
     if only == 'geometry':
         digests = json.loads((HERE / 'digests.json').read_text())
         digests.update(geometry_cases(import_base_transform(ref)))
@@ -338,6 +388,7 @@ def main():
     digests.update(voxel_cases(vt))
     scatter_cases(spt)
     spconv_cases(import_spconv())
+    spconv_conv_cases(import_spconv())
     digests.update(geometry_cases(import_base_transform(ref)))
     (HERE / 'digests.json').write_text(json.dumps(digests, indent=1, sort_keys=True) + '\n')
     print(json.dumps(digests, indent=1))

@@ -125,3 +125,31 @@ def test_indice_pairs_match_reference(golden, i):
     np.testing.assert_array_equal(o, w_out)
     np.testing.assert_array_equal(pr, w_pairs)
     np.testing.assert_array_equal(nm, w_num)
+
+
+def spconv_conv_case(g, j):
+    c, cin, cout, inverse, n_in, n_out = (int(v) for v in g[f'v{j}_case'])
+    return c, cin, cout, bool(inverse), n_in, n_out
+
+
+@pytest.mark.parametrize('j', range(5))
+def test_spconv_conv_oracle_vs_reference(golden, j):
+    """The numpy restatement of indice_conv / fused / backward (float64)
+    against the reference's own fp32 CPU results, and of max-pooling (exact)."""
+    g = golden('spconv_conv_cases')
+    rb = golden('spconv_cases')
+    c, cin, cout, inverse, n_in, n_out = spconv_conv_case(g, j)
+    pairs, num = rb[f'c{c}_pairs'], rb[f'c{c}_num']
+    x, w, bias, gy = g[f'v{j}_x'], g[f'v{j}_w'], g[f'v{j}_bias'], g[f'v{j}_gy']
+    tol = dict(rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(oracle.indice_conv(x, w, pairs, num, n_out, inverse), g[f'v{j}_y'], **tol)
+    np.testing.assert_allclose(oracle.indice_conv(x, w, pairs, num, n_out, inverse, bias), g[f'v{j}_yb'], **tol)
+    gx, gw = oracle.indice_conv_backward(x, w, gy, pairs, num, inverse)
+    np.testing.assert_allclose(gx, g[f'v{j}_gx'], **tol)
+    np.testing.assert_allclose(gw, g[f'v{j}_gw'], **tol)
+    if not inverse:
+        xp = g[f'v{j}_xp']
+        yp = oracle.indice_maxpool(xp, pairs, num, n_out)
+        np.testing.assert_array_equal(yp, g[f'v{j}_yp'])
+        np.testing.assert_array_equal(oracle.indice_maxpool_backward(xp, yp, g[f'v{j}_gyp'], pairs, num),
+                                      g[f'v{j}_gxp'])
