@@ -35,15 +35,17 @@
 //   spc_conv_simt_kernel   every other case (fp32, odd channel counts): 64-row
 //                          tiles, fp32 FMA in a 4x4 register tile per thread
 //   spc_dw_plan_kernel +   filters_grad: every rule's pairs cut into chunks of
-//   spc_dw_kernel +        one common length (planned on the device from the
-//   spc_dw_reduce_kernel   rule counts), a fp32 partial per chunk, summed per
-//                          rule in chunk order
+//   spc_dw_tc_kernel /     one common length (planned on the device from the
+//   spc_dw_kernel +        rule counts), a fp32 partial per chunk (tcgen05 for
+//   spc_dw_reduce_kernel   fp16 / bf16, reduction over pairs; else fp32 FMA),
+//                          summed per rule in chunk order
 //   spc_maxpool_kernel / spc_maxpool_bwd_kernel
 //
 // Every wait on an mbarrier is bounded; a wait that gives up counts into a
 // device error word (bfb_spconv_timeouts) and the block still waits, bounded,
 // for its own tensor-core work before it frees its tensor memory and returns.
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -240,16 +242,18 @@ __device__ __forceinline__ T epilogue(float acc, const T* bias, int n) {
 
 // ---------------------------------------------------- tensor-core convolution
 // One CTA per 128 destination rows.  x [n_src][Ck], nbr [n_dst][K],
-// wp = spc_prep_tc_kernel's blocks, out [n_dst][N].
-template <class T>
+// wp = spc_prep_tc_kernel's blocks, out [n_dst][N].  S pipeline stages: the
+// rows of offsets j+1 .. j+S-1 are in flight while the tensor cores work on
+// offset j.
+template <class T, int S>
 __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __restrict__ x, int Ck,
                                                                  const int32_t* __restrict__ nbr, int K,
                                                                  int64_t n_dst, const T* __restrict__ wp, int N,
                                                                  uint32_t tmem_cols, const T* __restrict__ bias,
                                                                  T* __restrict__ out) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bar_full[2];  // filter block of a stage has landed
-  __shared__ __align__(8) uint64_t bar_mma[2];   // tensor cores are done with a stage
+  __shared__ __align__(8) uint64_t bar_full[S];  // filter block of a stage has landed
+  __shared__ __align__(8) uint64_t bar_mma[S];   // tensor cores are done with a stage
   __shared__ uint32_t s_tmem;
   __shared__ int s_act[kMaxK];
   __shared__ int s_nact;
@@ -258,16 +262,18 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row0 = (int64_t)blockIdx.x * kTcRows;
   const uint32_t a_bytes = (uint32_t)kTcRows * Ck * 2u, b_bytes = (uint32_t)N * Ck * 2u;
-  unsigned char* st_a[2] = {smem, smem + a_bytes + b_bytes};
-  unsigned char* st_b[2] = {smem + a_bytes, smem + 2 * a_bytes + b_bytes};
-  int32_t* s_nbr = reinterpret_cast<int32_t*>(smem + 2 * (a_bytes + b_bytes));  // [128][K]
+  // stage s: A rows at smem + s * (a + b), its filter block right after;
+  // the tile's rows of the neighbour table after the stages
+  auto st_a = [&](int s) { return smem + (size_t)s * (a_bytes + b_bytes); };
+  auto st_b = [&](int s) { return smem + (size_t)s * (a_bytes + b_bytes) + a_bytes; };
+  int32_t* s_nbr = reinterpret_cast<int32_t*>(smem + (size_t)S * (a_bytes + b_bytes));  // [128][K]
 
   if (tid < (kMaxK + 31) / 32) s_mask[tid] = 0u;
   if (tid == 0) {
-    mbar_init(&bar_full[0], 1);
-    mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_mma[0], 1);
-    mbar_init(&bar_mma[1], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_mma[i], 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -277,13 +283,36 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   __syncthreads();
-  // the tile's neighbour rows and the offsets any of them uses
-  for (int e = tid; e < kTcRows * K; e += kTcThreads) {
-    const int r = e / K;
-    const int64_t row = row0 + r;
-    const int32_t v = row < n_dst ? __ldg(nbr + row0 * K + e) : -1;
-    s_nbr[e] = v;
-    if (v >= 0) atomicOr(&s_mask[(e - r * K) >> 5], 1u << ((e - r * K) & 31));
+  // the tile's neighbour rows: one contiguous slice of the table, read with
+  // 16-byte loads (the slice starts on a 512-byte boundary); rows past n_dst
+  // read as -1
+  {
+    const int64_t rows = min((int64_t)kTcRows, n_dst - row0);
+    const int valid = (int)(rows * K), total = kTcRows * K;
+    const int4* src4 = reinterpret_cast<const int4*>(nbr + row0 * K);
+    int4* dst4 = reinterpret_cast<int4*>(s_nbr);
+    for (int e4 = tid; e4 < total / 4; e4 += kTcThreads) {
+      int4 v;
+      if (e4 * 4 + 3 < valid) {
+        v = __ldg(src4 + e4);
+      } else {
+        int t[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t[i] = e4 * 4 + i < valid ? __ldg(nbr + row0 * K + e4 * 4 + i) : -1;
+        v = make_int4(t[0], t[1], t[2], t[3]);
+      }
+      dst4[e4] = v;
+    }
+  }
+  __syncthreads();
+  {
+    // the offsets any row of the tile uses: thread = row
+    uint32_t m[(kMaxK + 31) / 32] = {};
+    for (int k = 0; k < K; ++k)
+      if (s_nbr[tid * K + k] >= 0) m[k >> 5] |= 1u << (k & 31);
+#pragma unroll
+    for (int w = 0; w < (kMaxK + 31) / 32; ++w)
+      if (m[w]) atomicOr(&s_mask[w], m[w]);
   }
   tc_fence_before();
   __syncthreads();
@@ -302,49 +331,72 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
   const uint32_t idesc = idesc_f16(std::is_same<T, __nv_bfloat16>::value ? 1 : 0, N);
   bool ok = true;
 
-  auto load_stage = [&](int j, int s) {
+  // Thread t stages all chunks of tile row t: in the core-matrix layout, row
+  // r's chunk kc is the 16 bytes at (kc * 128 + r) * 16.  A row without a neighbour for the
+  // offset must read as zeros; `dirty[s]` records whether this row of stage
+  // s may hold data, so a row that is already zero is not rewritten (most
+  // rows of a sparse tile have no neighbour for most offsets).
+  bool dirty[S];
+#pragma unroll
+  for (int i = 0; i < S; ++i) dirty[i] = true;
+  // Stage s = j % S holds offset j; its n-th use (n = j / S) completes
+  // phase n of bar_full[s] and of bar_mma[s].  Iteration j loads offset
+  // j + P into the stage last read by the MMAs of offset j + P - S: with
+  // S >= 3, P = S - 2, so that stage was issued two iterations ago and its
+  // MMAs have usually finished (S = 2: P = 1, the previous offset's).  Every
+  // iteration commits one cp.async group (empty when nothing is left), so
+  // "all but the newest P groups" is always offset j's rows.
+  constexpr int P = S >= 3 ? S - 2 : 1;
+  auto load_stage = [&](int j) {
+    const int s = j % S;
     const int k = s_act[j];
     if (tid == 0) {
       mbar_expect_tx(&bar_full[s], b_bytes);
-      bulk_g2s(st_b[s], wp + (size_t)k * N * Ck, b_bytes, &bar_full[s]);
+      bulk_g2s(st_b(s), wp + (size_t)k * N * Ck, b_bytes, &bar_full[s]);
     }
-    // q -> (8-row group g, chunk kc, row r8): smem offset q * 16
-    const int nq = kTcRows * chunks;
-    for (int q = tid; q < nq; q += kTcThreads) {
-      const int r8 = q & 7, rest = q >> 3;
-      const int g = rest & (kTcRows / 8 - 1), kc = rest / (kTcRows / 8);
-      const int r = g * 8 + r8;
-      const int32_t src = s_nbr[r * K + k];
-      const T* p = x + (src >= 0 ? (int64_t)src * Ck + kc * 8 : 0);
-      cp_async16(st_a[s] + (size_t)q * 16, p, src >= 0);
+    const int32_t src = s_nbr[tid * K + k];
+    bool d = false;
+#pragma unroll
+    for (int i = 0; i < S; ++i)
+      if (i == s) d = dirty[i];
+    if (src >= 0 || d) {
+      const T* p = x + (src >= 0 ? (int64_t)src * Ck : 0);
+      for (int kc = 0; kc < chunks; ++kc)
+        cp_async16(st_a(s) + (size_t)(tid + kc * kTcThreads) * 16, p + (src >= 0 ? kc * 8 : 0), src >= 0);
+#pragma unroll
+      for (int i = 0; i < S; ++i)
+        if (i == s) dirty[i] = src >= 0;
     }
-    cp_async_commit();
   };
 
-  if (na > 0) load_stage(0, 0);
+  for (int j = 0; j < P; ++j) {
+    if (j < na) load_stage(j);
+    cp_async_commit();
+  }
   for (int j = 0; j < na; ++j) {
-    const int s = j & 1;
-    if (j + 1 < na) {
-      // stage s^1 was read by the MMAs of offset j-1
-      if (j >= 1 && !mbar_wait(&bar_mma[s ^ 1], (uint32_t)(((j - 1) >> 1) & 1))) ok = false;
-      load_stage(j + 1, s ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    const int s = j % S;
+    const int jn = j + P;  // the offset loaded in this iteration
+    if (jn < na) {
+      const int prev = jn - S;  // the stage's previous offset
+      if (prev >= 0 && !mbar_wait(&bar_mma[jn % S], (uint32_t)((prev / S) & 1))) ok = false;
+      load_stage(jn);
     }
+    cp_async_commit();
+    cp_async_wait<P>();
     fence_async_smem();  // the cp.async rows become visible to the tensor cores
     __syncthreads();
     if (tid == 0) {
-      if (!mbar_wait(&bar_full[s], (uint32_t)((j >> 1) & 1))) ok = false;
+      if (!mbar_wait(&bar_full[s], (uint32_t)((j / S) & 1))) ok = false;
       tc_fence_after();
-      const uint32_t a0 = smem_u32(st_a[s]), b0 = smem_u32(st_b[s]);
+      const uint32_t a0 = smem_u32(st_a(s)), b0 = smem_u32(st_b(s));
       for (int t = 0; t < (Ck >> 4); ++t)
         umma_f16(tmem, smem_desc(a0 + t * 2 * lbo_a, lbo_a, 128u), smem_desc(b0 + t * 2 * lbo_b, lbo_b, 128u), idesc,
                  (j > 0 || t > 0) ? 1u : 0u);
       umma_commit(&bar_mma[s]);
     }
   }
-  if (na > 0 && !mbar_wait(&bar_mma[(na - 1) & 1], (uint32_t)(((na - 1) >> 1) & 1))) ok = false;
+  if (na > 0 && !mbar_wait(&bar_mma[(na - 1) % S], (uint32_t)(((na - 1) / S) & 1))) ok = false;
+  cp_async_wait<0>();
   tc_fence_after();
 
   // epilogue: warp w owns tensor-memory lanes (tile rows) 32w .. 32w+31
@@ -408,6 +460,12 @@ __global__ __launch_bounds__(kSimtThreads) void spc_conv_simt_kernel(const T* __
     }
     __syncthreads();
     if (!s_any) continue;  // uniform: no row of the tile uses offset k
+    // a warp (rows 4ty .. 4ty+7 of two ty values) whose rows have no input
+    // for this offset adds only zeros: it skips the FMAs (warp-uniform)
+    bool mine = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mine |= s_src[ty * 4 + i] >= 0;
+    const bool warp_busy = __any_sync(0xffffffffu, mine);
     for (int c0 = 0; c0 < Ck; c0 += kSimtChunk) {
       const int cw = min(kSimtChunk, Ck - c0);
       for (int e = tid; e < kSimtChunk * kSimtRows; e += kSimtThreads) {
@@ -421,7 +479,7 @@ __global__ __launch_bounds__(kSimtThreads) void spc_conv_simt_kernel(const T* __
         s_w[c][n] = (c < cw && n < Npad) ? wp[((int64_t)k * Ck + c0 + c) * Npad + n] : 0.f;
       }
       __syncthreads();
-      for (int c = 0; c < cw; ++c) {
+      for (int c = 0; warp_busy && c < cw; ++c) {
         const float4 a = *reinterpret_cast<const float4*>(&s_a[c][ty * 4]);
         const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
@@ -550,6 +608,134 @@ __global__ __launch_bounds__(kSimtThreads) void spc_dw_kernel(const T* __restric
       if (co < Cout) dst[(int64_t)ci * Cout + co] = acc[i][q];
     }
   }
+}
+
+// Tensor-core form of spc_dw_kernel (fp16 / bf16, Cin <= 128 and a multiple
+// of 8, Cout a multiple of 16 up to 256): the partial of a chunk is
+// D[ci][co] = sum_p x[in_p][ci] * g[out_p][co], one tcgen05 GEMM chain with
+// M = 128 (input channels, zero past Cin), N = Cout and the pairs as the
+// reduction dimension, 128 pairs per stage.  Both operands are MN-major: a
+// core matrix is 8 pairs x 16 bytes of one row chunk, so every gathered
+// 16-byte chunk of an input or gradient row is copied (cp.async) straight to
+// its place.
+__device__ __forceinline__ uint32_t mn_off(int p, int c8, int groups) {
+  return (uint32_t)((((p >> 3) * groups + c8) * 8 + (p & 7)) * 16);
+}
+
+template <class T>
+__global__ __launch_bounds__(kTcThreads) void spc_dw_tc_kernel(const T* __restrict__ x, int Cin,
+                                                               const T* __restrict__ g, int Cout,
+                                                               const int32_t* __restrict__ pairs, int64_t cap,
+                                                               const int32_t* __restrict__ num, int K, int in_slot,
+                                                               int64_t n_in, int64_t n_out,
+                                                               const DwPlan* __restrict__ plan, uint32_t tmem_cols,
+                                                               float* __restrict__ part) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bar_mma[2];
+  __shared__ uint32_t s_tmem;
+  const int slot = blockIdx.x;
+  if (slot >= plan->cpre[K]) return;  // uniform, before any allocation
+  int k = 0;
+  while (k + 1 < K && plan->cpre[k + 1] <= slot) ++k;
+  const int64_t L = plan->L;
+  const int64_t cnt = min((int64_t)max(__ldg(num + k), 0), cap);
+  const int64_t p0 = (int64_t)(slot - plan->cpre[k]) * L, p1 = min(cnt, p0 + L);
+  const int nst = p1 > p0 ? (int)((p1 - p0 + kTcRows - 1) / kTcRows) : 0;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t a_bytes = (uint32_t)kTcRows * kTcRows * 2u, b_bytes = (uint32_t)Cout * kTcRows * 2u;
+  auto st_a = [&](int s) { return smem + (size_t)s * (a_bytes + b_bytes); };
+  auto st_b = [&](int s) { return smem + (size_t)s * (a_bytes + b_bytes) + a_bytes; };
+  // channel rows past Cin are never loaded: zero both A stages once
+  for (int e = tid; e < (int)(2 * (a_bytes + b_bytes) / 16); e += kTcThreads)
+    reinterpret_cast<uint4*>(smem)[e] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    mbar_init(&bar_mma[0], 1);
+    mbar_init(&bar_mma[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int ci8 = Cin >> 3, co8 = Cout >> 3;
+  const uint32_t lbo_a = (uint32_t)(kTcRows / 8) * 128u, lbo_b = (uint32_t)co8 * 128u;
+  const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 16) |
+                         ((uint32_t)(Cout >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+  bool ok = true;
+
+  // thread t gathers pair t of the step: its input row's chunks into A,
+  // its output-gradient row's chunks into B (zeros past the chunk's end)
+  auto load_step = [&](int j) {
+    const int s = j & 1;
+    const int64_t p = p0 + (int64_t)j * kTcRows + tid;
+    int32_t a = -1, b = -1;
+    if (p < p1) {
+      a = __ldg(pairs + ((int64_t)k * 2 + in_slot) * cap + p);
+      b = __ldg(pairs + ((int64_t)k * 2 + (1 - in_slot)) * cap + p);
+      if (BFB_BAD(a >= 0 && a < n_in && b >= 0 && b < n_out)) a = b = -1;
+      if (a < 0 || a >= n_in || b < 0 || b >= n_out) a = b = -1;
+    }
+    const T* xa = x + (a >= 0 ? (int64_t)a * Cin : 0);
+    const T* gb = g + (b >= 0 ? (int64_t)b * Cout : 0);
+    for (int c = 0; c < ci8; ++c) cp_async16(st_a(s) + mn_off(tid, c, kTcRows / 8), xa + (a >= 0 ? c * 8 : 0), a >= 0);
+    for (int c = 0; c < co8; ++c) cp_async16(st_b(s) + mn_off(tid, c, co8), gb + (b >= 0 ? c * 8 : 0), b >= 0);
+  };
+
+  if (nst > 0) load_step(0);
+  cp_async_commit();
+  for (int j = 0; j < nst; ++j) {
+    const int s = j & 1;
+    if (j + 1 < nst) {
+      if (j >= 1 && !mbar_wait(&bar_mma[s ^ 1], (uint32_t)(((j - 1) >> 1) & 1))) ok = false;
+      load_step(j + 1);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(st_a(s)), b0 = smem_u32(st_b(s));
+      for (int t = 0; t < kTcRows / 16; ++t)
+        umma_f16(tmem, smem_desc(a0 + t * 2 * lbo_a, lbo_a, 128u), smem_desc(b0 + t * 2 * lbo_b, lbo_b, 128u), idesc,
+                 (j > 0 || t > 0) ? 1u : 0u);
+      umma_commit(&bar_mma[s]);
+    }
+  }
+  if (nst > 0 && !mbar_wait(&bar_mma[(nst - 1) & 1], (uint32_t)(((nst - 1) >> 1) & 1))) ok = false;
+  cp_async_wait<0>();
+  tc_fence_after();
+
+  // epilogue: lane = input channel, columns = output channels
+  const int ci = warp * 32 + lane;
+  float* dst = part + (int64_t)slot * Cin * Cout + (int64_t)ci * Cout;
+  for (int c0 = 0; c0 < Cout; c0 += 16) {
+    float v[16];
+    if (nst > 0) {
+      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    }
+    if (ci < Cin) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<float4*>(dst + c0 + i) =
+            make_float4(ok ? v[i] : 0.f, ok ? v[i + 1] : 0.f, ok ? v[i + 2] : 0.f, ok ? v[i + 3] : 0.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
 }
 
 // dw[k] = sum of rule k's chunk partials in chunk order (0 for a rule
@@ -681,13 +867,16 @@ int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n
     BFB_CHECK_LAUNCH();
     uint32_t cols = 32;
     while (cols < (uint32_t)N) cols <<= 1;
-    size_t smem = 2 * ((size_t)kTcRows * Ck * 2 + (size_t)N * Ck * 2) + (size_t)kTcRows * K * 4;
+    const size_t stage = (size_t)kTcRows * Ck * 2 + (size_t)N * Ck * 2;
+    // two stages: measured faster than three or four here, because more
+    // blocks fit on an SM (the tile's latency is hidden across blocks)
+    size_t smem = 2 * stage + (size_t)kTcRows * K * 4;
     // at most 512 / cols blocks per SM, so that every resident block's
     // tensor-memory allocation succeeds at once
     const size_t per_sm = 227 * 1024, min_smem = per_sm / (512 / cols + 1) + 1;
     smem = std::max(smem, min_smem);
-    BFB_CUDA(cudaFuncSetAttribute(spc_conv_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    spc_conv_tc_kernel<T><<<(unsigned)ceil_div(n_dst, kTcRows), kTcThreads, smem, st>>>(
+    BFB_CUDA(cudaFuncSetAttribute(spc_conv_tc_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    spc_conv_tc_kernel<T, 2><<<(unsigned)ceil_div(n_dst, kTcRows), kTcThreads, smem, st>>>(
         x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, cols, bias, out);
     BFB_CHECK_LAUNCH();
     return BFB_OK;
@@ -741,11 +930,30 @@ int conv_backward(const void* features, int64_t n_in, int64_t cin, const void* f
   const int slots = dw_slots(K, cin, cout);
   spc_dw_plan_kernel<<<1, 32, 0, st>>>(num, (int)K, cap, slots, w.dwplan);
   BFB_CHECK_LAUNCH();
+  bool tc = false;
+  if constexpr (!std::is_same<T, float>::value)
+    tc = cin <= kTcRows && cin % 8 == 0 && cout % 16 == 0 && cout >= 16 && cout <= 256 && aligned16(features) &&
+         aligned16(out_bp);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (tc) {
+      uint32_t cols = 32;
+      while (cols < (uint32_t)cout) cols <<= 1;
+      const size_t per_sm = 227 * 1024, min_smem = per_sm / (512 / cols + 1) + 1;
+      const size_t smem = std::max((size_t)2 * ((size_t)kTcRows * kTcRows * 2 + (size_t)cout * kTcRows * 2), min_smem);
+      BFB_CUDA(cudaFuncSetAttribute(spc_dw_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      spc_dw_tc_kernel<T><<<(unsigned)slots, kTcThreads, smem, st>>>(
+          static_cast<const T*>(features), (int)cin, static_cast<const T*>(out_bp), (int)cout, pairs, cap, num, (int)K,
+          in_slot, n_in, n_out, w.dwplan, cols, w.part);
+      BFB_CHECK_LAUNCH();
+    }
+  }
   const int tiles_ci = (int)ceil_div(cin, 64), tiles_co = (int)ceil_div(cout, 64);
-  spc_dw_kernel<T><<<dim3((unsigned)slots, (unsigned)(tiles_ci * tiles_co)), kSimtThreads, 0, st>>>(
-      static_cast<const T*>(features), (int)cin, static_cast<const T*>(out_bp), (int)cout, pairs, cap, num, (int)K,
-      in_slot, n_in, n_out, w.dwplan, tiles_co, w.part);
-  BFB_CHECK_LAUNCH();
+  if (!tc) {
+    spc_dw_kernel<T><<<dim3((unsigned)slots, (unsigned)(tiles_ci * tiles_co)), kSimtThreads, 0, st>>>(
+        static_cast<const T*>(features), (int)cin, static_cast<const T*>(out_bp), (int)cout, pairs, cap, num, (int)K,
+        in_slot, n_in, n_out, w.dwplan, tiles_co, w.part);
+    BFB_CHECK_LAUNCH();
+  }
   spc_dw_reduce_kernel<T><<<grid_for(K * cin * cout, 256), 256, 0, st>>>(w.part, (int)K, w.dwplan, cin * cout,
                                                                          static_cast<T*>(filters_grad));
   BFB_CHECK_LAUNCH();
