@@ -32,8 +32,9 @@
 //                          by one cp.async.bulk copy completing on an mbarrier.
 //                          Two stages: the next offset's rows load while the
 //                          tensor cores work on the current one.
-//   spc_conv_simt_kernel   every other case (fp32, odd channel counts): 64-row
-//                          tiles, fp32 FMA in a 4x4 register tile per thread
+//   spc_conv_simt_kernel   every other case (fp32, odd channel counts): thread
+//                          = (row, 4 channels), per real pair a fp32 FMA dot
+//                          product from L1-resident filter rows
 //   spc_dw_plan_kernel +   filters_grad: every rule's pairs cut into chunks of
 //   spc_dw_tc_kernel /     one common length (planned on the device from the
 //   spc_dw_kernel +        rule counts), a fp32 partial per chunk (tcgen05 for
@@ -61,7 +62,6 @@ __device__ unsigned long long g_spc_timeouts = 0ull;
 
 constexpr int kTcRows = 128;          // output rows per tensor-core tile (UMMA M)
 constexpr int kTcThreads = 128;       // one thread per tile row in the epilogue
-constexpr int kSimtRows = 64;         // output rows per SIMT tile
 constexpr int kSimtThreads = 256;     // 16 x 16 threads, 4 x 4 outputs each
 constexpr int kSimtChunk = 32;        // input channels staged per step
 constexpr int kMaxK = 125;            // kernel volume up to 5x5x5
@@ -426,86 +426,61 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
 }
 
 // ------------------------------------------------------------ SIMT convolution
-// One block per 64 destination rows; thread (ty, tx) accumulates rows
-// 4ty..4ty+3 x columns 4tx..4tx+3 of each 64-column pass.  Sums in ascending
-// offset, then ascending input channel, with fp32 FMA.
-template <class T, int NP>
+// Thread = (destination row, 4 output channels).  For every offset k in
+// ascending order whose neighbour exists, the dot product of the input row
+// with filters[k] (fp32 FMA, ascending input channel; the filter rows stay
+// in L1, the input row is one broadcast per row) is added to the output: an
+// output is a sum over k of per-offset dot products, as the reference's
+// matmul-then-index_add_ forms it.  Only real pairs cost arithmetic.
+template <class T>
 __global__ __launch_bounds__(kSimtThreads) void spc_conv_simt_kernel(const T* __restrict__ x, int Ck,
                                                                      const int32_t* __restrict__ nbr, int K,
                                                                      int64_t n_dst, const float* __restrict__ wp,
                                                                      int N, int Npad, const T* __restrict__ bias,
                                                                      T* __restrict__ out) {
-  __shared__ __align__(16) float s_a[kSimtChunk][kSimtRows + 4];  // padded: fewer bank conflicts on the transposing store
-  __shared__ __align__(16) float s_w[kSimtChunk][NP * 64];
-  __shared__ int32_t s_src[kSimtRows];
-  __shared__ int s_any;
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int64_t row0 = (int64_t)blockIdx.x * kSimtRows;
-  float acc[NP][4][4];
-#pragma unroll
-  for (int p = 0; p < NP; ++p)
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[p][i][c] = 0.f;
-
+  const int nq = Npad >> 2;
+  const int64_t idx = (int64_t)blockIdx.x * kSimtThreads + threadIdx.x;
+  const int64_t row = idx / nq;
+  if (row >= n_dst) return;
+  const int q = (int)(idx - row * nq);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool vec = std::is_same<T, float>::value && (Ck & 3) == 0;
   for (int k = 0; k < K; ++k) {
-    if (tid == 0) s_any = 0;
-    __syncthreads();
-    if (tid < kSimtRows) {
-      const int64_t row = row0 + tid;
-      const int32_t v = row < n_dst ? __ldg(nbr + row * K + k) : -1;
-      s_src[tid] = v;
-      if (v >= 0) s_any = 1;
-    }
-    __syncthreads();
-    if (!s_any) continue;  // uniform: no row of the tile uses offset k
-    // a warp (rows 4ty .. 4ty+7 of two ty values) whose rows have no input
-    // for this offset adds only zeros: it skips the FMAs (warp-uniform)
-    bool mine = false;
+    const int32_t src = __ldg(nbr + row * K + k);
+    if (src < 0) continue;
+    const T* xr = x + (int64_t)src * Ck;
+    const float4* wr = reinterpret_cast<const float4*>(wp + (int64_t)k * Ck * Npad) + q;
+    float p[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec) {
+      for (int c = 0; c < Ck; c += 4) {
+        const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + c));
+        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mine |= s_src[ty * 4 + i] >= 0;
-    const bool warp_busy = __any_sync(0xffffffffu, mine);
-    for (int c0 = 0; c0 < Ck; c0 += kSimtChunk) {
-      const int cw = min(kSimtChunk, Ck - c0);
-      for (int e = tid; e < kSimtChunk * kSimtRows; e += kSimtThreads) {
-        const int r = e / kSimtChunk, c = e - r * kSimtChunk;
-        const int32_t src = s_src[r];
-        s_a[c][r] = (c < cw && src >= 0) ? to_f32(x[(int64_t)src * Ck + c0 + c]) : 0.f;
-      }
-      const int wn = NP * 64;
-      for (int e = tid; e < kSimtChunk * wn; e += kSimtThreads) {
-        const int c = e / wn, n = e - c * wn;
-        s_w[c][n] = (c < cw && n < Npad) ? wp[((int64_t)k * Ck + c0 + c) * Npad + n] : 0.f;
-      }
-      __syncthreads();
-      for (int c = 0; warp_busy && c < cw; ++c) {
-        const float4 a = *reinterpret_cast<const float4*>(&s_a[c][ty * 4]);
-        const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const float4 w = *reinterpret_cast<const float4*>(&s_w[c][p * 64 + tx * 4]);
-          const float wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[p][i][q] = fmaf(av[i], wv[q], acc[p][i][q]);
+        for (int u = 0; u < 4; ++u) {
+          const float4 w = __ldg(wr + (int64_t)(c + u) * nq);
+          p[0] = fmaf(xs[u], w.x, p[0]);
+          p[1] = fmaf(xs[u], w.y, p[1]);
+          p[2] = fmaf(xs[u], w.z, p[2]);
+          p[3] = fmaf(xs[u], w.w, p[3]);
         }
       }
-      __syncthreads();
+    } else {
+      for (int c = 0; c < Ck; ++c) {
+        const float xv = to_f32(xr[c]);
+        const float4 w = __ldg(wr + (int64_t)c * nq);
+        p[0] = fmaf(xv, w.x, p[0]);
+        p[1] = fmaf(xv, w.y, p[1]);
+        p[2] = fmaf(xv, w.z, p[2]);
+        p[3] = fmaf(xv, w.w, p[3]);
+      }
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[u] += p[u];
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = row0 + ty * 4 + i;
-    if (row >= n_dst) continue;
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int n = p * 64 + tx * 4 + q;
-        if (n < N) out[row * N + n] = epilogue<T>(acc[p][i][q], bias, n);
-      }
+  for (int u = 0; u < 4; ++u) {
+    const int n = q * 4 + u;
+    if (n < N) out[row * N + n] = epilogue<T>(acc[u], bias, n);
   }
 }
 
@@ -887,15 +862,8 @@ int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n
   spc_prep_simt_kernel<T><<<grid_for(K * Ck * Npad, 256), 256, 0, st>>>(w, (int)K, (int)N, (int)Ck, (int)Npad,
                                                                         transposed, wp);
   BFB_CHECK_LAUNCH();
-  const unsigned grid = (unsigned)ceil_div(n_dst, kSimtRows);
-  const int np = (int)ceil_div(N, 64);
-  switch (np) {
-    case 1: spc_conv_simt_kernel<T, 1><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out); break;
-    case 2: spc_conv_simt_kernel<T, 2><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out); break;
-    case 3: spc_conv_simt_kernel<T, 3><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out); break;
-    case 4: spc_conv_simt_kernel<T, 4><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out); break;
-    default: return BFB_ERR_INVALID_ARG;
-  }
+  spc_conv_simt_kernel<T><<<(unsigned)ceil_div(n_dst * (Npad / 4), kSimtThreads), kSimtThreads, 0, st>>>(
+      x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out);
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
