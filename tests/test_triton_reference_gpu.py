@@ -33,6 +33,15 @@ baseline/ref_triton.py) are the GPU-side oracle:
   map and counts exact; max exact; sum / mean (atomics) within 1e-5; the
   backward exactly (mean: within 1 ulp, the division above).
 
+* sparse convolution (ops/spconv/src/spconv_triton.py:981-1111): the
+  reference loops over the rules on the host and scatter-adds each rule's
+  matmul into the output, one rule after the other, so an output is the
+  rule-ordered sum of per-rule dot products, which ours forms the same way
+  for fp32: equal bit for bit.  fp16: the reference rounds every rule's
+  partial to fp16 while ours accumulates in fp32 and rounds once, both
+  within 1e-2.  Gradients within 1e-5 (fp32; the filter gradient's chunked
+  sum order differs).  Max-pooling exact.
+
 The reference Triton ``bev_pool`` has no bounds check (an out-of-grid
 coordinate makes it write outside its output), so only in-grid coordinates
 are given to it.
@@ -283,3 +292,51 @@ def test_dynamic_scatter_vs_triton(ref, red):
         assert torch.equal(ga, want)  # IEEE division, as the reference CPU path
     else:
         assert torch.equal(ga, gb)
+
+
+@pytest.fixture(scope='module')
+def ref_spconv(cuda):
+    why = ref_triton.available()
+    if why:
+        pytest.skip(why)
+    try:
+        return ref_triton.load_spconv()
+    except RuntimeError as e:
+        pytest.skip(str(e))
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16])
+@pytest.mark.parametrize('layer', ['subm', 'down'])
+def test_sparse_conv_vs_reference_gpu(ref_spconv, dtype, layer):
+    from bevfusion_triton_b200.ops.spconv import (get_indice_pairs, indice_conv, indice_conv_backward, indice_maxpool,
+                                                  indice_maxpool_backward)
+    from tests.test_spconv_gpu import SPARSE_SHAPE, lidar_voxel_indices
+    idx = lidar_voxel_indices(1)
+    kw = dict(ksize=3, padding=1, subm=True) if layer == 'subm' else dict(ksize=3, stride=2, padding=1)
+    outids, pairs, num = get_indice_pairs(idx, 1, SPARSE_SHAPE, **kw)
+    n_in, n_out = idx.size(0), outids.size(0)
+    g = torch.Generator(device='cuda').manual_seed(13)
+    x = torch.randn(n_in, 32, device='cuda', generator=g).to(dtype)
+    w = (torch.randn(27, 32, 64, device='cuda', generator=g) / 30).to(dtype)
+    gy = torch.randn(n_out, 64, device='cuda', generator=g).to(dtype)
+    y, yr = indice_conv(x, w, pairs, num, n_out), ref_spconv.indice_conv(x, w, pairs, num, n_out)
+    gx, gw = indice_conv_backward(x, w, gy, pairs, num)
+    gxr, gwr = ref_spconv.indice_conv_backward(x, w, gy, pairs, num)
+    if dtype == torch.float32:
+        assert torch.equal(y, yr)
+        torch.testing.assert_close(gx, gxr, **FP32_TOL)
+        scale = float(gwr.abs().max())
+        torch.testing.assert_close(gw / scale, gwr / scale, **FP32_TOL)
+    else:
+        for a, b in ((y, yr), (gx, gxr)):
+            assert float(((a.float() - b.float()).abs() / b.float().abs().clamp(min=1.0)).max()) <= 1e-2
+        scale = float(gwr.float().abs().max())
+        assert float((gw.float() - gwr.float()).abs().max()) <= 1e-2 * scale
+    p, pr = indice_maxpool(x, pairs, num, n_out), ref_spconv.indice_maxpool(x, pairs, num, n_out)
+    assert torch.equal(p, pr)
+    gp = indice_maxpool_backward(x, p, gy[:, :32].contiguous(), pairs, num)
+    gpr = ref_spconv.indice_maxpool_backward(x, pr, gy[:, :32].contiguous(), pairs, num)
+    if dtype == torch.float32:
+        torch.testing.assert_close(gp, gpr, **FP32_TOL)
+    else:
+        torch.testing.assert_close(gp, gpr, rtol=1e-2, atol=1e-2)
