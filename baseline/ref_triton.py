@@ -88,7 +88,7 @@ def _load_package(name: str, rel: str):
 def load():
     """(bev_pool_triton, voxelization_triton, scatter_points_triton) modules of
     the installed reference.  Raises RuntimeError when it is unavailable."""
-    if _mods:
+    if 'bev' in _mods:
         return _mods['bev'], _mods['vox'], _mods['scatter']
     why = available()
     if why:
