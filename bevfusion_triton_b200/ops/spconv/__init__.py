@@ -1,5 +1,19 @@
+"""Sparse convolution: rulebook, convolution and max-pooling ops
+(``ops.py``, ``functional.py``) and the module layer the sparse encoder is
+built from (``conv.py``, ``pool.py``, ``modules.py``, ``structure.py``),
+drop-ins for the reference's ``ops/spconv`` package."""
+from .conv import (SparseConv2d, SparseConv3d, SparseConv4d, SparseConvolution, SparseConvTranspose2d,
+                   SparseConvTranspose3d, SparseInverseConv2d, SparseInverseConv3d, SubMConv2d, SubMConv3d,
+                   SubMConv4d)
+from .modules import RemoveGrid, SparseModule, SparseSequential, ToDense
 from .ops import (fused_indice_conv, get_conv_output_size, get_deconv_output_size, get_indice_pairs, indice_conv,
                   indice_conv_backward, indice_maxpool, indice_maxpool_backward)
+from .pool import SparseMaxPool2d, SparseMaxPool3d
+from .structure import SparseConvTensor, scatter_nd
 
-__all__ = ['fused_indice_conv', 'get_conv_output_size', 'get_deconv_output_size', 'get_indice_pairs', 'indice_conv',
-           'indice_conv_backward', 'indice_maxpool', 'indice_maxpool_backward']
+__all__ = ['SparseConv2d', 'SparseConv3d', 'SparseConv4d', 'SparseConvolution', 'SparseConvTranspose2d',
+           'SparseConvTranspose3d', 'SparseInverseConv2d', 'SparseInverseConv3d', 'SubMConv2d', 'SubMConv3d',
+           'SubMConv4d', 'RemoveGrid', 'SparseModule', 'SparseSequential', 'ToDense', 'SparseMaxPool2d',
+           'SparseMaxPool3d', 'SparseConvTensor', 'scatter_nd', 'fused_indice_conv', 'get_conv_output_size',
+           'get_deconv_output_size', 'get_indice_pairs', 'indice_conv', 'indice_conv_backward', 'indice_maxpool',
+           'indice_maxpool_backward']
