@@ -239,7 +239,8 @@ def run_ours(args, ws, rank, local):
     wl = Workload(rank, args.samples_per_gpu, dev, ws)
     B, D, H, W = wl.shape
     stream = torch.cuda.current_stream()
-    s_lid = torch.cuda.Stream()  # the LiDAR branch, concurrent with the camera branch
+    # the LiDAR branch, concurrent with the camera branch
+    s_lid = torch.cuda.Stream(priority=-1 if args.lidar_priority else 0)
 
     def lidar(ev):
         if ev:
@@ -254,10 +255,9 @@ def run_ours(args, ws, rank, local):
         The two branches are independent: by default the voxelisation (a
         latency-bound chain) runs on its own stream beside the plan (also
         latency-bound), and the step ends when both have finished; --serial
-        runs them one after the other on one stream.  Starting it after the
-        plan instead, beside the gathers, starves it: the gather grids hold
-        every SM and the voxelisation finishes after them."""
-        if not args.serial:
+        runs them one after the other on one stream, --lidar-beside gather
+        starts it after the plan."""
+        if not args.serial and args.lidar_beside == 'plan':
             s_lid.wait_stream(stream)
             with torch.cuda.stream(s_lid):
                 lidar(ev)
@@ -266,6 +266,10 @@ def run_ours(args, ws, rank, local):
         plan = O.bev_pool_plan(wl.coords, B, D, H, W)
         if ev:
             ev[1].record(stream)
+        if not args.serial and args.lidar_beside == 'gather':
+            s_lid.wait_stream(stream)
+            with torch.cuda.stream(s_lid):
+                lidar(ev)
         out = O.bev_pool_forward_planned(wl.feats, plan, B, D, H, W)
         if ev:
             ev[2].record(stream)
@@ -938,6 +942,9 @@ def main():
     ap.add_argument('--no-spconv', action='store_true', help='skip the sparse-convolution timings')
     ap.add_argument('--no-triton', action='store_true', help='skip timing the reference Triton GPU path')
     ap.add_argument('--no-extra', action='store_true', help='skip the config-4 and fp16 bev_pool timings')
+    ap.add_argument('--lidar-beside', choices=('plan', 'gather'), default='plan',
+                    help='start the concurrent voxelisation with the plan or after it, beside the gathers')
+    ap.add_argument('--lidar-priority', action='store_true', help='run the LiDAR stream at high priority')
     ap.add_argument('--serial', action='store_true', help='run the LiDAR voxelisation after the camera branch on one stream')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
