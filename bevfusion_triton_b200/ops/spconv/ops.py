@@ -92,6 +92,16 @@ def _require_cuda(*ts) -> None:
             raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
 
 
+def _like_features(t, features):
+    """Under torch.autocast the reference's per-rule matmul accepts fp32
+    filters with fp16 / bf16 features; here the filters (and bias) are cast
+    to the features' dtype then (a differentiable cast, so fp32 parameters
+    still receive gradients).  Outside autocast the dtypes must match."""
+    if t is None or t.dtype == features.dtype or not torch.is_autocast_enabled():
+        return t
+    return t.to(features.dtype)
+
+
 def indice_conv(features: torch.Tensor, filters: torch.Tensor, indice_pairs: torch.Tensor,
                 indice_pair_num: torch.Tensor, num_activate_out: int, inverse: bool = False,
                 subm: bool = False) -> torch.Tensor:
@@ -104,8 +114,8 @@ def indice_conv(features: torch.Tensor, filters: torch.Tensor, indice_pairs: tor
     filters."""
     del subm
     _require_cuda(features, filters, indice_pairs, indice_pair_num)
-    return ops().indice_conv(features, filters, indice_pairs, indice_pair_num, int(num_activate_out),
-                             bool(inverse), None)
+    return ops().indice_conv(features, _like_features(filters, features), indice_pairs, indice_pair_num,
+                             int(num_activate_out), bool(inverse), None)
 
 
 def fused_indice_conv(features, filters, bias, indice_pairs, indice_pair_num, num_activate_out, inverse, subm):
@@ -113,8 +123,8 @@ def fused_indice_conv(features, filters, bias, indice_pairs, indice_pair_num, nu
     reference (spconv_triton.py:1010-1032) a submanifold convolution adds no
     bias here."""
     _require_cuda(features, filters, indice_pairs, indice_pair_num)
-    return ops().indice_conv(features, filters, indice_pairs, indice_pair_num, int(num_activate_out),
-                             bool(inverse), None if subm else bias)
+    return ops().indice_conv(features, _like_features(filters, features), indice_pairs, indice_pair_num,
+                             int(num_activate_out), bool(inverse), None if subm else _like_features(bias, features))
 
 
 def indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_num, inverse: bool = False,
@@ -124,8 +134,10 @@ def indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_nu
     order, so it is deterministic."""
     del subm
     _require_cuda(features, filters, out_bp, indice_pairs, indice_pair_num)
-    gin, gw = ops().indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_num, bool(inverse))
-    return gin, gw.view_as(filters)
+    gin, gw = ops().indice_conv_backward(features, _like_features(filters, features),
+                                         _like_features(out_bp, features), indice_pairs, indice_pair_num,
+                                         bool(inverse))
+    return gin, gw.view(filters.shape).to(filters.dtype)
 
 
 def indice_maxpool(features, indice_pairs, indice_pair_num, num_activate_out):

@@ -125,3 +125,21 @@ def test_maxpool_and_dense(ref):
     d = S.ToDense()(S.SparseSequential(S.SubMConv3d(8, 4, 1).cuda())(small))
     assert d.shape == (1, 4, *SPARSE_SHAPE)
     assert int((d.abs().sum(1) > 0).sum()) <= 100
+
+
+def test_autocast_fp16_features_fp32_filters(ref):
+    """Under autocast a layer takes fp16 features with its fp32 parameters
+    (the reference's matmul does); the fp32 parameters get gradients."""
+    idx = lidar_voxel_indices(1)
+    net = S.SparseSequential(S.SubMConv3d(16, 32, 3, padding=1, indice_key='a'), nn.ReLU(),
+                             S.SparseConv3d(32, 32, 3, stride=2, padding=1, indice_key='b')).cuda()
+    x = torch.randn(idx.size(0), 16, device='cuda', dtype=torch.float16)
+    with torch.autocast('cuda', dtype=torch.float16):
+        out = net(S.SparseConvTensor(x, idx, SPARSE_SHAPE, 1))
+    assert out.features.dtype == torch.float16
+    out.features.float().square().mean().backward()
+    assert all(p.grad is not None and p.grad.dtype == torch.float32 and bool(torch.isfinite(p.grad).all())
+               for p in net.parameters())
+    # outside autocast mismatched dtypes are refused, as a plain matmul is
+    with pytest.raises(TypeError):
+        net(S.SparseConvTensor(x, idx, SPARSE_SHAPE, 1))
