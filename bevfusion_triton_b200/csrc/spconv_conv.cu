@@ -64,7 +64,7 @@ constexpr int kTcRows = 128;          // output rows per tensor-core tile (UMMA 
 constexpr int kTcThreads = 128;       // one thread per tile row in the epilogue
 constexpr int kSimtThreads = 256;     // 16 x 16 threads, 4 x 4 outputs each
 constexpr int kSimtChunk = 32;        // input channels staged per step
-constexpr int kMaxK = 125;            // kernel volume up to 5x5x5
+constexpr int kMaxK = 343;            // kernel volume up to 7x7x7
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: a correct wait takes microseconds
 
 // ------------------------------------------------------------------ helpers
@@ -306,13 +306,14 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
   }
   __syncthreads();
   {
-    // the offsets any row of the tile uses: thread = row
-    uint32_t m[(kMaxK + 31) / 32] = {};
-    for (int k = 0; k < K; ++k)
-      if (s_nbr[tid * K + k] >= 0) m[k >> 5] |= 1u << (k & 31);
-#pragma unroll
-    for (int w = 0; w < (kMaxK + 31) / 32; ++w)
-      if (m[w]) atomicOr(&s_mask[w], m[w]);
+    // the offsets any row of the tile uses: thread = row, one mask word of
+    // 32 offsets at a time
+    for (int w = 0; w * 32 < K; ++w) {
+      uint32_t bits = 0u;
+      for (int k = w * 32; k < min(K, w * 32 + 32); ++k)
+        if (s_nbr[tid * K + k] >= 0) bits |= 1u << (k & 31);
+      if (bits) atomicOr(&s_mask[w], bits);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -871,7 +872,7 @@ int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n
 int check_conv_args(int dtype, int64_t n_in, int64_t cin, int64_t K, int64_t cout, int64_t cap, int64_t n_out) {
   if (!dtype_size(dtype)) return BFB_ERR_UNSUPPORTED_DTYPE;
   if (n_in < 0 || n_out < 0 || cap < 0 || cin <= 0 || cout <= 0 || K <= 0) return BFB_ERR_INVALID_ARG;
-  if (K > kMaxK || cin > 256 || cout > 256) return BFB_ERR_INVALID_ARG;
+  if (K > kMaxK) return BFB_ERR_INVALID_ARG;
   if (n_in * K >= 0x7fffffffLL || n_out * K >= 0x7fffffffLL || n_in >= 0x7fffffffLL) return BFB_ERR_TOO_LARGE;
   return BFB_OK;
 }

@@ -430,7 +430,7 @@ int bfb_indice_pairs_outids(int64_t n, int ndim, int64_t batch, const int64_t* o
  * + bias (nullable; the reference's fused form rounds the sum and the biased
  * value separately, and so does this).  fp16 / bf16 with cin and cout
  * multiples of 16 (cout <= 256) run on the tensor cores; everything else
- * (fp32 included) on fp32 FMA.  K <= 125, cin, cout <= 256.  The workspace
+ * (fp32 included) on fp32 FMA.  K <= 343 (7x7x7), any channel count.  The workspace
  * (bfb_indice_conv_workspace_size, backward = 0 or 1) holds the neighbour
  * table and the filters in the kernels' layout.
  * ---------------------------------------------------------------------- */

@@ -210,3 +210,22 @@ def test_opcheck_spconv_ops(cuda, lidar_rulebooks):
     torch.library.opcheck(O.indice_conv_backward.default, (x, w, gy, p, m, False),
                           test_utils=('test_schema', 'test_faketensor'))
     torch.library.opcheck(O.indice_maxpool.default, (x, p, m, n), test_utils=('test_schema', 'test_faketensor'))
+
+
+def test_wide_channels_and_large_kernel(cuda):
+    """Channel counts past the tensor-core shapes and a 5x5x5 kernel run on
+    the FMA path (any width; kernel volume up to 7x7x7)."""
+    idx = lidar_voxel_indices(1)[:20000].contiguous()
+    outids, pairs, num = get_indice_pairs(idx, 1, SPARSE_SHAPE, ksize=5, padding=2, subm=True)
+    n = idx.size(0)
+    pr, nm = pairs.cpu().numpy(), num.cpu().numpy()
+    for cin, cout, dtype in ((260, 300, torch.float32), (48, 272, torch.float16)):
+        x, w, gy = _inputs(n, n, 125, cin, cout, dtype, seed=cin)
+        y = indice_conv(x, w, pairs, num, n)
+        close(y, oracle.indice_conv(x.float().cpu().numpy(), w.float().cpu().numpy(), pr, nm, n), dtype)
+        gx, gw = indice_conv_backward(x, w, gy, pairs, num)
+        rgx, rgw = oracle.indice_conv_backward(x.float().cpu().numpy(), w.float().cpu().numpy(),
+                                               gy.float().cpu().numpy(), pr, nm)
+        close(gx, rgx, dtype)
+        scale = max(1.0, float(np.abs(rgw).max()))
+        close(gw.float() / scale, rgw / scale, dtype)
