@@ -97,7 +97,7 @@ def _like_features(t, features):
     filters with fp16 / bf16 features; here the filters (and bias) are cast
     to the features' dtype then (a differentiable cast, so fp32 parameters
     still receive gradients).  Outside autocast the dtypes must match."""
-    if t is None or t.dtype == features.dtype or not torch.is_autocast_enabled():
+    if t is None or t.dtype == features.dtype or not torch.is_autocast_enabled(features.device.type):
         return t
     return t.to(features.dtype)
 
