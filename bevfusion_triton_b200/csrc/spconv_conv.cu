@@ -498,18 +498,32 @@ struct DwPlan {
 
 __global__ void spc_dw_plan_kernel(const int32_t* __restrict__ num, int K, int64_t cap, int slots,
                                    DwPlan* __restrict__ plan) {
-  if (threadIdx.x != 0) return;
+  // one warp: the counts are loaded in parallel, the prefix is a warp scan
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x >= 32) return;
   int64_t total = 0;
-  for (int k = 0; k < K; ++k) total += min((int64_t)max(num[k], 0), cap);
+  for (int k = lane; k < K; k += 32) total += min((int64_t)max(__ldg(num + k), 0), cap);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
   const int64_t room = max(slots - K, 1);
   const int64_t L = max((int64_t)32, ((total + room - 1) / room + 31) / 32 * 32);
-  int32_t c = 0;
-  for (int k = 0; k < K; ++k) {
-    plan->cpre[k] = c;
-    c += (int32_t)((min((int64_t)max(num[k], 0), cap) + L - 1) / L);
+  int32_t carry = 0;
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    const int k = k0 + lane;
+    const int32_t c = k < K ? (int32_t)((min((int64_t)max(__ldg(num + k), 0), cap) + L - 1) / L) : 0;
+    int32_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (k < K) plan->cpre[k] = carry + x - c;
+    carry += __shfl_sync(0xffffffffu, x, 31);
   }
-  plan->cpre[K] = c;
-  plan->L = (int32_t)L;
+  if (lane == 0) {
+    plan->cpre[K] = carry;
+    plan->L = (int32_t)L;
+  }
 }
 
 // Block (slot, tile): the slot's chunk of one rule, a 64 x 64 tile (input
@@ -722,8 +736,17 @@ __global__ void spc_dw_reduce_kernel(const float* __restrict__ part, int K, cons
   const int64_t total = (int64_t)K * cc;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = e / cc, r = e - k * cc;
+    const int c1 = plan->cpre[k + 1];
     float s = 0.f;
-    for (int c = plan->cpre[k]; c < plan->cpre[k + 1]; ++c) s += part[(int64_t)c * cc + r];
+    int c = plan->cpre[k];
+    for (; c + 8 <= c1; c += 8) {  // eight loads in flight, added in chunk order
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(part + (int64_t)(c + u) * cc + r);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; c < c1; ++c) s += __ldg(part + (int64_t)c * cc + r);
     dw[e] = from_f32<T>(s);
   }
 }
