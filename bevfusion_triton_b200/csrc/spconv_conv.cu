@@ -39,7 +39,7 @@
 //   spc_dw_tc_kernel /     one common length (planned on the device from the
 //   spc_dw_kernel +        rule counts), a fp32 partial per chunk (tcgen05 for
 //   spc_dw_reduce_kernel   fp16 / bf16, reduction over pairs; else fp32 FMA),
-//                          summed per rule in chunk order
+//                          summed per rule in a fixed two-level order
 //   spc_maxpool_kernel / spc_maxpool_bwd_kernel
 //
 // Every wait on an mbarrier is bounded; a wait that gives up counts into a
@@ -728,26 +728,39 @@ __global__ __launch_bounds__(kTcThreads) void spc_dw_tc_kernel(const T* __restri
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
 }
 
-// dw[k] = sum of rule k's chunk partials in chunk order (0 for a rule
-// without pairs).
+// dw[k] = sum of rule k's chunk partials (0 for a rule without pairs).  A
+// block covers 32 consecutive entries of dw[k] (lanes, coalesced) and 8
+// chunk groups (warps): warp w adds chunks w, w + 8, ... in order, then the
+// 8 group sums are added in group order -- a fixed tree, so the result is
+// deterministic, and one rule's hundreds of chunks are summed 8-wide.
 template <class T>
-__global__ void spc_dw_reduce_kernel(const float* __restrict__ part, int K, const DwPlan* __restrict__ plan,
-                                     int64_t cc, T* __restrict__ dw) {
-  const int64_t total = (int64_t)K * cc;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = e / cc, r = e - k * cc;
-    const int c1 = plan->cpre[k + 1];
-    float s = 0.f;
-    int c = plan->cpre[k];
-    for (; c + 8 <= c1; c += 8) {  // eight loads in flight, added in chunk order
-      float v[8];
+__global__ __launch_bounds__(256) void spc_dw_reduce_kernel(const float* __restrict__ part, int K,
+                                                            const DwPlan* __restrict__ plan, int64_t cc,
+                                                            T* __restrict__ dw) {
+  __shared__ float s_sum[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int k = blockIdx.y;
+  const int64_t r = (int64_t)blockIdx.x * 32 + lane;
+  const int c0 = plan->cpre[k], c1 = plan->cpre[k + 1];
+  float s = 0.f;
+  if (r < cc) {
+    int c = c0 + w;
+    for (; c + 24 < c1; c += 32) {  // four loads in flight, added in order
+      float v[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(part + (int64_t)(c + u) * cc + r);
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(part + (int64_t)(c + 8 * u) * cc + r);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) s += v[u];
+      for (int u = 0; u < 4; ++u) s += v[u];
     }
-    for (; c < c1; ++c) s += __ldg(part + (int64_t)c * cc + r);
-    dw[e] = from_f32<T>(s);
+    for (; c < c1; c += 8) s += __ldg(part + (int64_t)c * cc + r);
+  }
+  s_sum[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && r < cc) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) t += s_sum[g][lane];
+    dw[(int64_t)k * cc + r] = from_f32<T>(t);
   }
 }
 
@@ -946,8 +959,8 @@ int conv_backward(const void* features, int64_t n_in, int64_t cin, const void* f
         in_slot, n_in, n_out, w.dwplan, tiles_co, w.part);
     BFB_CHECK_LAUNCH();
   }
-  spc_dw_reduce_kernel<T><<<grid_for(K * cin * cout, 256), 256, 0, st>>>(w.part, (int)K, w.dwplan, cin * cout,
-                                                                         static_cast<T*>(filters_grad));
+  spc_dw_reduce_kernel<T><<<dim3((unsigned)ceil_div(cin * cout, 32), (unsigned)K), 256, 0, st>>>(
+      w.part, (int)K, w.dwplan, cin * cout, static_cast<T*>(filters_grad));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }
