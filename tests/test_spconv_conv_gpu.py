@@ -229,3 +229,31 @@ def test_wide_channels_and_large_kernel(cuda):
         close(gx, rgx, dtype)
         scale = max(1.0, float(np.abs(rgw).max()))
         close(gw.float() / scale, rgw / scale, dtype)
+
+
+@pytest.mark.parametrize('kind', ['transposed3d', 'dilated3d', 'conv2d'])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16])
+def test_other_rulebook_kinds_vs_oracle(cuda, kind, dtype):
+    """Convolution over a transposed 3-D rulebook, a dilated submanifold one
+    and a 2-D one (the bird's-eye plane of the LiDAR sites), forward and
+    backward against the oracle."""
+    idx = lidar_voxel_indices(1)[:30000].contiguous()
+    if kind == 'transposed3d':
+        shape = [720, 720, 21]
+        idx = torch.cat([idx[:, :1], idx[:, 1:] // 2], 1).unique(dim=0).contiguous()
+        outids, pairs, num = get_indice_pairs(idx, 1, shape, ksize=3, stride=2, padding=1, transpose=True)
+    elif kind == 'dilated3d':
+        outids, pairs, num = get_indice_pairs(idx, 1, SPARSE_SHAPE, ksize=3, padding=2, dilation=2, subm=True)
+    else:
+        idx = idx[:, :3].unique(dim=0).contiguous()
+        outids, pairs, num = get_indice_pairs(idx, 1, SPARSE_SHAPE[:2], ksize=3, stride=2, padding=1)
+    n_in, n_out, K = idx.size(0), outids.size(0), pairs.size(0)
+    x, w, gy = _inputs(n_in, n_out, K, 32, 48, dtype, seed=K + n_in)
+    pr, nm = pairs.cpu().numpy(), num.cpu().numpy()
+    xr, wr, gr = x.float().cpu().numpy(), w.float().cpu().numpy(), gy.float().cpu().numpy()
+    close(indice_conv(x, w, pairs, num, n_out), oracle.indice_conv(xr, wr, pr, nm, n_out), dtype)
+    gx, gw = indice_conv_backward(x, w, gy, pairs, num)
+    rgx, rgw = oracle.indice_conv_backward(xr, wr, gr, pr, nm)
+    close(gx, rgx, dtype)
+    scale = max(1.0, float(np.abs(rgw).max()))
+    close(gw.float() / scale, rgw / scale, dtype)
