@@ -181,3 +181,24 @@ def test_status_injection_returns_before_touching_arguments(cabi):
 def test_release_build_has_no_debug_checks(cabi):
     cabi.bfb_debug_checks_enabled.restype = ctypes.c_int
     assert cabi.bfb_debug_checks_enabled() == 0
+
+
+def test_sparse_conv_argument_checks(cabi):
+    """Size queries and argument checks of the sparse-convolution entry
+    points, host side only (no launch)."""
+    sz = ctypes.c_size_t()
+    q = cabi.bfb_indice_conv_workspace_size
+    q.argtypes = [ctypes.c_int64] * 6 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_size_t)]
+    assert q(1000, 900, 27, 64, 64, 1000, 1, 0, ctypes.byref(sz)) == 0 and sz.value > 0
+    fwd = sz.value
+    assert q(1000, 900, 27, 64, 64, 1000, 1, 1, ctypes.byref(sz)) == 0 and sz.value > fwd  # + backward parts
+    assert q(1000, 900, 343, 300, 260, 1000, 0, 1, ctypes.byref(sz)) == 0  # any width, up to 7x7x7
+    assert q(1000, 900, 344, 64, 64, 1000, 0, 0, ctypes.byref(sz)) == -1  # kernel volume past 7x7x7
+    assert q(1000, 900, 0, 64, 64, 1000, 0, 0, ctypes.byref(sz)) == -1
+    assert q(-1, 900, 27, 64, 64, 1000, 0, 0, ctypes.byref(sz)) == -1
+    assert q(1000, 900, 27, 64, 64, 1000, 9, 0, ctypes.byref(sz)) == -2  # dtype code
+    assert q(1 << 30, 900, 27, 64, 64, 1000, 0, 0, ctypes.byref(sz)) == -4  # n * K past 32 bits
+    m = cabi.bfb_indice_maxpool_workspace_size
+    m.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_size_t)]
+    assert m(1000, 300, 27, 0, ctypes.byref(sz)) == 0 and sz.value >= 300 * 27 * 4
+    assert m(1000, 300, 27, 1, ctypes.byref(sz)) == 0 and sz.value >= 1000 * 27 * 4
