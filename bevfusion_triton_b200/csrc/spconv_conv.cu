@@ -438,14 +438,15 @@ __global__ __launch_bounds__(kSimtThreads) void spc_conv_simt_kernel(const T* __
                                                                      const int32_t* __restrict__ nbr, int K,
                                                                      int64_t n_dst, const float* __restrict__ wp,
                                                                      int N, int Npad, const T* __restrict__ bias,
-                                                                     T* __restrict__ out) {
+                                                                     T* __restrict__ out, bool vec) {
   const int nq = Npad >> 2;
   const int64_t idx = (int64_t)blockIdx.x * kSimtThreads + threadIdx.x;
   const int64_t row = idx / nq;
   if (row >= n_dst) return;
   const int q = (int)(idx - row * nq);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const bool vec = std::is_same<T, float>::value && (Ck & 3) == 0;
+  // vec: fp32 rows read 16 bytes at a time (the host checked Ck % 4 == 0
+  // and a 16-byte aligned x)
   for (int k = 0; k < K; ++k) {
     const int32_t src = __ldg(nbr + row * K + k);
     if (src < 0) continue;
@@ -900,7 +901,8 @@ int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n
                                                                         transposed, wp);
   BFB_CHECK_LAUNCH();
   spc_conv_simt_kernel<T><<<(unsigned)ceil_div(n_dst * (Npad / 4), kSimtThreads), kSimtThreads, 0, st>>>(
-      x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out);
+      x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out,
+      std::is_same<T, float>::value && Ck % 4 == 0 && aligned16(x));
   BFB_CHECK_LAUNCH();
   return BFB_OK;
 }

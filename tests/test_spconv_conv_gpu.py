@@ -257,3 +257,27 @@ def test_other_rulebook_kinds_vs_oracle(cuda, kind, dtype):
     close(gx, rgx, dtype)
     scale = max(1.0, float(np.abs(rgw).max()))
     close(gw.float() / scale, rgw / scale, dtype)
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16])
+def test_unaligned_feature_rows(cuda, lidar_rulebooks, dtype):
+    """A contiguous feature view starting 1 element into its storage (not
+    16-byte aligned) takes the paths without 16-byte loads: fp32 gives the
+    same bits; 16-bit features leave the tensor cores for the FMA path (other
+    summation order), within the 16-bit tolerance."""
+    n_in, _, pairs, num = lidar_rulebooks['subm3']
+    x, w, gy = _inputs(n_in, n_in, 27, 16, 32, dtype, seed=77)
+    base = torch.empty(n_in * 16 + 1, device='cuda', dtype=dtype)
+    xu = base[1:].view(n_in, 16)
+    xu.copy_(x)
+    assert xu.data_ptr() % 16 != 0 and xu.is_contiguous()
+    y, yu = indice_conv(x, w, pairs, num, n_in), indice_conv(xu, w, pairs, num, n_in)
+    gx, gw = indice_conv_backward(x, w, gy, pairs, num)
+    gxu, gwu = indice_conv_backward(xu, w, gy, pairs, num)
+    if dtype == torch.float32:
+        assert torch.equal(yu, y) and torch.equal(gxu, gx) and torch.equal(gwu, gw)
+    else:
+        close(yu, y.float().cpu().numpy(), dtype)
+        close(gxu, gx.float().cpu().numpy(), dtype)
+        scale = float(gw.float().abs().max())
+        assert float((gwu.float() - gw.float()).abs().max()) <= 1e-2 * scale
