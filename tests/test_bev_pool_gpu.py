@@ -308,3 +308,18 @@ def test_opcheck_bev_pool_ops(cuda):
     torch.library.opcheck(O.bev_pool_forward_planned, (feats, plan, 1, 1, 20, 20), test_utils=utils)
     g = torch.randn((1, 16, 1, 20, 20), device='cuda')
     torch.library.opcheck(O.bev_pool_backward, (g, plan, 3000, 1, 1, 20, 20), test_utils=utils)
+
+
+def test_legacy_import_path(cuda):
+    """ops.bev_pool.bev_pool_legacy.bev_pool (the sort + interval path's
+    import name) is the same op: equal outputs; mismatched lengths assert."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool as current
+    from bevfusion_triton_b200.ops.bev_pool.bev_pool_legacy import bev_pool as legacy
+    g = torch.Generator().manual_seed(4)
+    n, C, B, D, H, W = 5000, 16, 2, 2, 12, 10
+    feats = torch.randn(n, C, generator=g).cuda()
+    coords = torch.stack([torch.randint(0, H, (n,), generator=g), torch.randint(0, W, (n,), generator=g),
+                          torch.randint(0, D, (n,), generator=g), torch.randint(0, B, (n,), generator=g)], 1).cuda()
+    assert torch.equal(legacy(feats, coords, B, D, H, W), current(feats, coords, B, D, H, W))
+    with pytest.raises(AssertionError):
+        legacy(feats[:-1], coords, B, D, H, W)
