@@ -374,3 +374,23 @@ def test_opcheck_voxel_ops(cuda):
     c = torch.randint(0, 20, (5000, 3), dtype=torch.int32, device='cuda')
     torch.library.opcheck(O.dynamic_scatter_forward, (f, c, 'max', None),
                           test_utils=('test_schema', 'test_autograd_registration'))
+
+
+def test_legacy_import_path(cuda, golden):
+    """ops.voxel.voxel_layer_legacy (the compiled extension's import name and
+    positional signatures) runs the same ops."""
+    from bevfusion_triton_b200.ops.voxel import voxel_layer_legacy as legacy
+    g = golden('voxel_points8')
+    pts = torch.from_numpy(g['points']).cuda()
+    a = [torch.zeros((64, 5, pts.size(1)), device='cuda'), torch.zeros((64, 3), dtype=torch.int32, device='cuda'),
+         torch.zeros((64,), dtype=torch.int32, device='cuda')]
+    b = [t.clone() for t in a]
+    n1 = legacy.hard_voxelize(pts, *a, VS8, CR8, 5, 64, 3)
+    n2 = legacy.voxel_layer_ext.hard_voxelize(pts, *b, VS8, CR8, 5, 64)
+    n3 = hard_voxelize(pts, *[t.clone() for t in b], VS8, CR8, 5, 64)
+    assert n1 == n2 == n3 and all(torch.equal(x, y) for x, y in zip(a, b))
+    c1 = torch.empty((pts.size(0), 3), dtype=torch.int32, device='cuda')
+    c2 = torch.empty_like(c1)
+    legacy.dynamic_voxelize(pts, c1, VS8, CR8, 3)
+    dynamic_voxelize(pts, c2, VS8, CR8)
+    assert torch.equal(c1, c2)
