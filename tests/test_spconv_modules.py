@@ -93,3 +93,13 @@ def test_fused_folds_batch_norm_with_the_reference_formula():
     scale = bn.weight / (torch.sqrt(bn.running_var) + bn.eps)
     torch.testing.assert_close(fused[0].weight, conv.weight * scale)
     torch.testing.assert_close(fused[0].bias, -bn.running_mean * scale + bn.bias)
+
+
+def test_legacy_import_paths():
+    """The reference's legacy module names resolve to this library's ops."""
+    from bevfusion_triton_b200.ops.bev_pool import bev_pool_legacy
+    from bevfusion_triton_b200.ops.spconv import ops_legacy
+    from bevfusion_triton_b200.ops.voxel import voxel_layer_legacy
+    assert ops_legacy.indice_conv is S.indice_conv and ops_legacy.get_indice_pairs is S.get_indice_pairs
+    assert voxel_layer_legacy.voxel_layer_ext.dynamic_voxelize is voxel_layer_legacy.dynamic_voxelize
+    assert callable(bev_pool_legacy.bev_pool)
