@@ -103,3 +103,31 @@ def test_legacy_import_paths():
     assert ops_legacy.indice_conv is S.indice_conv and ops_legacy.get_indice_pairs is S.get_indice_pairs
     assert voxel_layer_legacy.voxel_layer_ext.dynamic_voxelize is voxel_layer_legacy.dynamic_voxelize
     assert callable(bev_pool_legacy.bev_pool)
+
+
+REFERENCE_SPCONV_ALL = ['SparseConv2d', 'SparseConv3d', 'SubMConv2d', 'SubMConv3d', 'SparseConvTranspose2d',
+                        'SparseConvTranspose3d', 'SparseInverseConv2d', 'SparseInverseConv3d', 'SparseModule',
+                        'SparseSequential', 'SparseMaxPool2d', 'SparseMaxPool3d', 'SparseConvTensor', 'scatter_nd']
+
+
+def test_package_exports_match_the_reference():
+    """The export lists the reference's own tests pin
+    (tests/test_ops/test_spconv/test_spconv.py:27-42, 221-227), and the
+    symbols are the module-level classes."""
+    from bevfusion_triton_b200.ops import voxel
+    from bevfusion_triton_b200.ops.spconv import conv, modules, pool, structure
+    assert S.__all__ == REFERENCE_SPCONV_ALL and all(hasattr(S, n) for n in S.__all__)
+    assert voxel.__all__ == ['Voxelization', 'voxelization', 'dynamic_scatter', 'DynamicScatter']
+    assert S.SparseConv3d is conv.SparseConv3d and S.SparseSequential is modules.SparseSequential
+    assert S.SparseMaxPool2d is pool.SparseMaxPool2d and S.SparseConvTensor is structure.SparseConvTensor
+    for m in (S.SparseConv2d(3, 4, 3, stride=1, padding=1), S.SparseConv3d(3, 4, 3, stride=1, padding=1),
+              S.SubMConv2d(3, 4, 3), S.SubMConv3d(3, 4, 3), S.SparseConvTranspose2d(3, 4, 3, stride=1, padding=1),
+              S.SparseConvTranspose3d(3, 4, 3, stride=1, padding=1), S.SparseInverseConv2d(3, 4, 3, indice_key='k'),
+              S.SparseInverseConv3d(3, 4, 3, indice_key='k'), S.SparseMaxPool2d(1), S.SparseMaxPool3d(1),
+              S.SparseSequential()):
+        assert isinstance(m, S.SparseModule)
+    dense = S.scatter_nd(torch.tensor([[0, 0], [1, 1]]), torch.tensor([1.0, 2.0]), [2, 2])
+    assert dense.tolist() == [[1.0, 0.0], [0.0, 2.0]]
+    st = S.SparseConvTensor(torch.tensor([[1.0, 2.0], [3.0, 4.0]]), torch.tensor([[0, 0, 0], [0, 0, 1]],
+                                                                                dtype=torch.int32), [1, 2], 1)
+    assert st.dense(channels_first=True).shape == (1, 2, 1, 2) and st.dense(channels_first=False).shape == (1, 1, 2, 2)
