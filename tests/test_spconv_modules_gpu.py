@@ -143,3 +143,60 @@ def test_autocast_fp16_features_fp32_filters(ref):
     # outside autocast mismatched dtypes are refused, as a plain matmul is
     with pytest.raises(TypeError):
         net(S.SparseConvTensor(x, idx, SPARSE_SHAPE, 1))
+
+
+def _sites(ndim, shape, dense, seed):
+    """(b, c0, ..) int32 rows: every cell of `shape`, or a seeded third of them."""
+    grids = torch.meshgrid(*[torch.arange(s) for s in shape], indexing='ij')
+    cells = torch.stack([g.reshape(-1) for g in grids], 1)
+    if not dense:
+        g = torch.Generator().manual_seed(seed)
+        cells = cells[torch.randperm(cells.size(0), generator=g)[:max(2, cells.size(0) // 3)]]
+    return torch.cat([torch.zeros(cells.size(0), 1, dtype=torch.long), cells], 1).int().cuda()
+
+
+MODULE_CASES = [
+    ('SparseConv', dict(kernel_size=1, bias=True)), ('SparseConv', dict(kernel_size=1, bias=False)),
+    ('SparseConv', dict(kernel_size=3, padding=1, bias=True)), ('SubMConv', dict(kernel_size=1, bias=False)),
+    ('SubMConv', dict(kernel_size=3, padding=1, bias=True)), ('SparseMaxPool', dict(kernel_size=2, stride=1, padding=1)),
+]
+
+
+@pytest.mark.parametrize('ndim', [2, 3])
+@pytest.mark.parametrize('dense', [True, False], ids=['full', 'sparse'])
+@pytest.mark.parametrize('kind,kw', MODULE_CASES, ids=[f'{k}-{i}' for i, (k, _) in enumerate(MODULE_CASES)])
+def test_small_modules_vs_reference(ref, ndim, dense, kind, kw):
+    """Forward and backward of one module on a small grid, against the
+    reference's GPU functions called as its module would (fp32: 1e-5)."""
+    shape = [3, 4] if ndim == 2 else [2, 3, 3]
+    idx = _sites(ndim, shape, dense, seed=ndim * 10 + len(kind))
+    torch.manual_seed(123)
+    pool = kind == 'SparseMaxPool'
+    ctor = getattr(S, f'{kind}{ndim}d')
+    m = (ctor(**kw) if pool else ctor(3, 4, **kw)).cuda()
+    x = torch.randn(idx.size(0), 3, device='cuda', requires_grad=True)
+    out = m(S.SparseConvTensor(x, idx, shape, 1))
+    out.features.sum().backward()
+    ks = [kw['kernel_size']] * ndim
+    st, pd = [kw.get('stride', 1)] * ndim, [kw.get('padding', 0)] * ndim
+    subm = kind == 'SubMConv'
+    xr = x.detach()
+    if not pool and m.conv1x1:
+        want = xr @ m.weight.detach().view(3, 4) + (m.bias.detach() if m.bias is not None else 0)
+        wid = idx
+    else:
+        wid, pairs, num = ref.get_indice_pairs(idx, 1, shape, ks, st, pd, [1] * ndim, [0] * ndim, subm, False)
+        if pool:
+            want = ref.indice_maxpool(xr, pairs, num, wid.shape[0])
+            gx_ref = ref.indice_maxpool_backward(xr, want, torch.ones_like(want), pairs, num)
+        else:
+            want = ref.indice_conv(xr, m.weight.detach(), pairs, num, wid.shape[0], False, subm)
+            if m.bias is not None:
+                want = want + m.bias.detach()
+            gx_ref, gw_ref = ref.indice_conv_backward(xr, m.weight.detach(), torch.ones_like(want), pairs, num)
+            torch.testing.assert_close(m.weight.grad, gw_ref.view_as(m.weight), rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(x.grad, gx_ref, rtol=1e-5, atol=1e-5)
+    assert torch.equal(out.indices, wid)
+    torch.testing.assert_close(out.features, want, rtol=1e-5, atol=1e-5)
+    if not pool and m.bias is not None:
+        torch.testing.assert_close(m.bias.grad, torch.full_like(m.bias, float(out.features.size(0))))
