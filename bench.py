@@ -362,6 +362,11 @@ def run_ours(args, ws, rank, local):
             line['sparse_conv'] = run_spconv(args, wl, ws)
         except Exception as e:  # an extra leg must not cost the benchmark line
             line['sparse_conv'] = {'error': repr(e)[:300]}
+    if not args.no_spconv:
+        try:
+            line['sparse_encoder'] = run_sparse_encoder(args, wl, ws)
+        except Exception as e:  # an extra leg must not cost the benchmark line
+            line['sparse_encoder'] = {'error': repr(e)[:300]}
     if not args.no_triton:
         try:
             line['triton_reference'] = run_triton_reference(args, wl, ws)
@@ -755,6 +760,132 @@ def run_spconv(args, wl, ws):
                       'fwd_speedup': round(rf / fwd, 2), 'bwd_speedup': round(rb / bwd, 2),
                       'max_rel_diff_vs_ref': float(((y - yr).abs() / yr.abs().clamp(min=1.0)).max())})
         res[name] = r
+    return res
+
+
+def run_sparse_encoder(args, wl, ws):
+    """A LiDAR sparse-encoder stack shaped like BEVFusion's SparseEncoder
+    default configuration (models/backbones/sparse_encoder.py: 5 -> 16 input
+    conv, stages of channels (16, 16, 32), (32, 32, 64), (64, 64, 128),
+    (128, 128) with residual submanifold blocks and strided 3x3x3 downsampling,
+    the (1, 1, 3) output conv to 128 channels, batch norm + ReLU after each
+    conv), built from this library's module layer, over the rank's voxelised
+    LiDAR samples (mean voxel features), fp32 and under fp16 autocast.  The
+    same stack composed from the reference's own GPU functions
+    (spconv_triton, installed unmodified) is timed for the forward.  ms per
+    call of all S samples, max over ranks."""
+    from torch import nn
+    from bevfusion_triton_b200.ops import spconv as S
+    sys.path.insert(0, str(ROOT / 'baseline'))
+    import ref_triton
+    try:
+        rsc = ref_triton.load_spconv()
+    except Exception:
+        rsc = None
+    # the voxelisation's packed mean features and (b, x, y, z) sites
+    vf, vc, _, total = torch.ops.bfb_b200.voxelize_mean_epilogue(wl.voxels, wl.vcoors, wl.vnum, wl.vn)
+    m = int(total.item())
+    feats, idx = vf[:m].contiguous(), vc[:m].contiguous()
+    shape = [1440, 1440, 41]
+
+    class Block(S.SparseModule):  # residual block of two submanifold convs
+        def __init__(self, c, key):
+            super().__init__()
+            self.c1, self.b1 = S.SubMConv3d(c, c, 3, padding=1, bias=False, indice_key=key), nn.BatchNorm1d(c, 1e-3)
+            self.c2, self.b2 = S.SubMConv3d(c, c, 3, padding=1, bias=False, indice_key=key), nn.BatchNorm1d(c, 1e-3)
+
+        def forward(self, x):
+            y = self.c1(x)
+            y.features = torch.relu(self.b1(y.features))
+            y = self.c2(y)
+            y.features = torch.relu(self.b2(y.features) + x.features)
+            return y
+
+    def cbr(conv, c):
+        return [conv, nn.BatchNorm1d(c, eps=1e-3), nn.ReLU()]
+
+    torch.manual_seed(0)
+    layers = cbr(S.SubMConv3d(5, 16, 3, padding=1, bias=False, indice_key='subm1'), 16)
+    chans = ((16, 16, 32), (32, 32, 64), (64, 64, 128), (128, 128))
+    pads = ((0, 0, 1), (0, 0, 1), (0, 0, (1, 1, 0)), (0, 0))
+    cin = 16
+    for i, blocks in enumerate(chans):
+        for j, c in enumerate(blocks):
+            if j == len(blocks) - 1 and i != len(chans) - 1:
+                layers += cbr(S.SparseConv3d(cin, c, 3, stride=2, padding=pads[i][j], bias=False,
+                                             indice_key=f'spconv{i + 1}'), c)
+            else:
+                layers.append(Block(c, f'subm{i + 1}'))
+            cin = c
+    layers += cbr(S.SparseConv3d(128, 128, (1, 1, 3), stride=(1, 1, 2), padding=0, bias=False,
+                                 indice_key='spconv_down2'), 128)
+    net = S.SparseSequential(*layers).cuda()
+
+    def ours(autocast, backward):
+        x = feats.detach().requires_grad_(backward)
+        with torch.autocast('cuda', dtype=torch.float16, enabled=autocast):
+            out = net(S.SparseConvTensor(x, idx, shape, wl.S))
+        if backward:
+            out.features.float().sum().backward()
+        return out
+
+    def ref_forward():
+        """The stack's calls, composed from the reference's functions."""
+        f, ind, shp, cache = feats, idx, shape, {}
+
+        def conv(m, f, ind, shp):
+            if m.indice_key in cache:
+                outids, _, pairs, num, _ = cache[m.indice_key]
+                oshp = shp
+            else:
+                outids, pairs, num = rsc.get_indice_pairs(ind, wl.S, shp, m.kernel_size, m.stride, m.padding,
+                                                          m.dilation, m.output_padding, m.subm, m.transposed)
+                cache[m.indice_key] = (outids, ind, pairs, num, shp)
+                oshp = shp if m.subm else S.get_conv_output_size(shp, m.kernel_size, m.stride, m.padding, m.dilation)
+            return rsc.indice_conv(f, m.weight, pairs, num, outids.shape[0], False, m.subm), outids, oshp
+
+        with torch.no_grad():
+            for m in net:
+                if isinstance(m, Block):
+                    y, _, _ = conv(m.c1, f, ind, shp)
+                    y = torch.relu(m.b1(y))
+                    y, _, _ = conv(m.c2, y, ind, shp)
+                    f = torch.relu(m.b2(y) + f)
+                elif isinstance(m, S.SparseConvolution):
+                    f, ind, shp = conv(m, f, ind, shp)
+                else:
+                    f = m(f)
+        return f
+
+    k = max(3, min(args.steps, 10))
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier(ws)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        return round(max_over_ranks(s0.elapsed_time(s1), ws) / k, 3)
+
+    net.eval()
+    res = {'sites': int(idx.size(0)), 'layers': sum(isinstance(m, S.SparseConvolution) for m in net.modules()),
+           'fwd_fp32_ms': timed(lambda: ours(False, False)), 'fwd_fp16_autocast_ms': timed(lambda: ours(True, False))}
+    net.train()
+    res['fwd_bwd_fp32_ms'] = timed(lambda: ours(False, True))
+    res['fwd_bwd_fp16_autocast_ms'] = timed(lambda: ours(True, True))
+    net.eval()
+    if rsc is not None:
+        res['reference_fwd_fp32_ms'] = timed(ref_forward)
+        with torch.no_grad():
+            a, b = ours(False, False).features, ref_forward()
+        res['fwd_fp32_speedup'] = round(res['reference_fwd_fp32_ms'] / res['fwd_fp32_ms'], 2)
+        res['max_abs_diff_vs_reference'] = float((a - b).abs().max())
     return res
 
 

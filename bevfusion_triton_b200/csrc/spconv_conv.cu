@@ -32,9 +32,10 @@
 //                          by one cp.async.bulk copy completing on an mbarrier.
 //                          Two stages: the next offset's rows load while the
 //                          tensor cores work on the current one.
-//   spc_conv_simt_kernel   every other case (fp32, odd channel counts): thread
-//                          = (row, 4 channels), per real pair a fp32 FMA dot
-//                          product from L1-resident filter rows
+//   spc_rule_kernel        every other case (fp32, odd channel counts): one
+//                          launch per offset in ascending order, 64 of the
+//                          rule's pairs per block, the filter in shared memory,
+//                          fp32 FMA, read-modify-write of the output rows
 //   spc_dw_plan_kernel +   filters_grad: every rule's pairs cut into chunks of
 //   spc_dw_tc_kernel /     one common length (planned on the device from the
 //   spc_dw_kernel +        rule counts), a fp32 partial per chunk (tcgen05 for
@@ -427,63 +428,103 @@ __global__ __launch_bounds__(kTcThreads) void spc_conv_tc_kernel(const T* __rest
 }
 
 // ------------------------------------------------------------ SIMT convolution
-// Thread = (destination row, 4 output channels).  For every offset k in
-// ascending order whose neighbour exists, the dot product of the input row
-// with filters[k] (fp32 FMA, ascending input channel; the filter rows stay
-// in L1, the input row is one broadcast per row) is added to the output: an
-// output is a sum over k of per-offset dot products, as the reference's
-// matmul-then-index_add_ forms it.  Only real pairs cost arithmetic.
-template <class T>
-__global__ __launch_bounds__(kSimtThreads) void spc_conv_simt_kernel(const T* __restrict__ x, int Ck,
-                                                                     const int32_t* __restrict__ nbr, int K,
-                                                                     int64_t n_dst, const float* __restrict__ wp,
-                                                                     int N, int Npad, const T* __restrict__ bias,
-                                                                     T* __restrict__ out, bool vec) {
-  const int nq = Npad >> 2;
-  const int64_t idx = (int64_t)blockIdx.x * kSimtThreads + threadIdx.x;
-  const int64_t row = idx / nq;
-  if (row >= n_dst) return;
-  const int q = (int)(idx - row * nq);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  // vec: fp32 rows read 16 bytes at a time (the host checked Ck % 4 == 0
-  // and a 16-byte aligned x)
-  for (int k = 0; k < K; ++k) {
-    const int32_t src = __ldg(nbr + row * K + k);
-    if (src < 0) continue;
-    const T* xr = x + (int64_t)src * Ck;
-    const float4* wr = reinterpret_cast<const float4*>(wp + (int64_t)k * Ck * Npad) + q;
-    float p[4] = {0.f, 0.f, 0.f, 0.f};
-    if (vec) {
-      for (int c = 0; c < Ck; c += 4) {
-        const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + c));
-        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+// Rule-major: one launch per kernel offset k, in ascending order.  A block
+// takes 64 of rule k's pairs at a time (every row useful), stages their
+// source rows and filter k in shared memory (32 reduced channels per step),
+// and each thread forms 4 pairs x 4 output channels per 64-column pass of
+// the dot products x[src] @ filters[k] (fp32 FMA, ascending reduced
+// channel), then adds them to the fp32 accumulator rows acc[dst] (read,
+// add, write: a rule names every destination row at most once and the rules
+// run one after another, so no atomics; an output is the rule-ordered sum of
+// per-rule dot products, as the reference's matmul-then-index_add_ forms
+// it).  NP 64-column passes per block; blockIdx.y picks the column group.
+template <class T, int NP>
+__global__ __launch_bounds__(kSimtThreads) void spc_rule_kernel(const T* __restrict__ x, int Ck,
+                                                                const int32_t* __restrict__ pairs, int64_t cap,
+                                                                const int32_t* __restrict__ num, int k, int src_slot,
+                                                                int64_t n_src, int64_t n_dst,
+                                                                const float* __restrict__ wp, int N, int Npad,
+                                                                float* __restrict__ acc) {
+  __shared__ __align__(16) float s_a[kSimtChunk][64 + 4];  // [channel][pair], padded
+  __shared__ __align__(16) float s_w[kSimtChunk][NP * 64];
+  __shared__ int32_t s_src[64], s_dst[64];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int n0 = blockIdx.y * NP * 64;
+  const int64_t cnt = min((int64_t)max(__ldg(num + k), 0), cap);
+  const int32_t* ps = pairs + ((int64_t)k * 2 + src_slot) * cap;
+  const int32_t* pd = pairs + ((int64_t)k * 2 + (1 - src_slot)) * cap;
+  for (int64_t t0 = (int64_t)blockIdx.x * 64; t0 < cnt; t0 += (int64_t)gridDim.x * 64) {
+    if (tid < 64) {
+      const int64_t p = t0 + tid;
+      int32_t a = -1, b = -1;
+      if (p < cnt) {
+        a = __ldg(ps + p);
+        b = __ldg(pd + p);
+        if (BFB_BAD(a >= 0 && a < n_src && b >= 0 && b < n_dst)) a = b = -1;
+        if (a < 0 || a >= n_src || b < 0 || b >= n_dst) a = b = -1;
+      }
+      s_src[tid] = a;
+      s_dst[tid] = b;
+    }
+    __syncthreads();
+    float r[NP][4][4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 w = __ldg(wr + (int64_t)(c + u) * nq);
-          p[0] = fmaf(xs[u], w.x, p[0]);
-          p[1] = fmaf(xs[u], w.y, p[1]);
-          p[2] = fmaf(xs[u], w.z, p[2]);
-          p[3] = fmaf(xs[u], w.w, p[3]);
+    for (int q = 0; q < NP; ++q)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[q][i][c] = 0.f;
+    for (int c0 = 0; c0 < Ck; c0 += kSimtChunk) {
+      const int cw = min(kSimtChunk, Ck - c0);
+      for (int e = tid; e < 64 * kSimtChunk; e += kSimtThreads) {
+        const int pp = e / kSimtChunk, c = e - pp * kSimtChunk;
+        const int32_t a = s_src[pp];
+        s_a[c][pp] = (a >= 0 && c < cw) ? to_f32(x[(int64_t)a * Ck + c0 + c]) : 0.f;
+      }
+      for (int e = tid; e < kSimtChunk * NP * 64; e += kSimtThreads) {
+        const int c = e / (NP * 64), n = e - c * (NP * 64);
+        s_w[c][n] = (c < cw && n0 + n < Npad) ? wp[((int64_t)k * Ck + c0 + c) * Npad + n0 + n] : 0.f;
+      }
+      __syncthreads();
+      for (int c = 0; c < cw; ++c) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&s_a[c][ty * 4]);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+          const float4 w4 = *reinterpret_cast<const float4*>(&s_w[c][q * 64 + tx * 4]);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) r[q][i][u] = fmaf(av[i], wv[u], r[q][i][u]);
         }
       }
-    } else {
-      for (int c = 0; c < Ck; ++c) {
-        const float xv = to_f32(xr[c]);
-        const float4 w = __ldg(wr + (int64_t)c * nq);
-        p[0] = fmaf(xv, w.x, p[0]);
-        p[1] = fmaf(xv, w.y, p[1]);
-        p[2] = fmaf(xv, w.z, p[2]);
-        p[3] = fmaf(xv, w.w, p[3]);
-      }
+      __syncthreads();
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) acc[u] += p[u];
-  }
+    for (int i = 0; i < 4; ++i) {
+      const int32_t d = s_dst[ty * 4 + i];
+      if (d < 0) continue;
+      float* arow = acc + (int64_t)d * N;
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int n = q * 4 + u;
-    if (n < N) out[row * N + n] = epilogue<T>(acc[u], bias, n);
+      for (int q = 0; q < NP; ++q)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int n = n0 + q * 64 + tx * 4 + u;
+          if (n < N) arow[n] += r[q][i][u];
+        }
+    }
+    __syncthreads();  // s_src / s_dst are rewritten next
   }
+}
+
+// out = epilogue(acc) over [rows][N] (the fp32 sums rounded once, + bias).
+template <class T>
+__global__ void spc_finish_kernel(const float* __restrict__ acc, int64_t rows, int N, const T* __restrict__ bias,
+                                  T* __restrict__ out) {
+  const int64_t total = rows * N;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x)
+    out[e] = epilogue<T>(acc[e], bias, (int)(e % N));
 }
 
 // ------------------------------------------------------------ filter gradient
@@ -815,6 +856,7 @@ struct ConvWork {
   void* wprep_t = nullptr;     // transposed filter operand (backward)
   float* part = nullptr;       // filter-gradient partials
   DwPlan* dwplan = nullptr;
+  float* acc = nullptr;        // fp32 sums of the rule-major path (16-bit features)
 };
 
 bool tc_ok(int dtype, int64_t Ck, int64_t N, int64_t K) {
@@ -843,6 +885,7 @@ size_t carve_conv(void* base, int dtype, int64_t n_in, int64_t n_out, int64_t K,
   Carver c(base);
   w->nbr_out = c.take<int32_t>((size_t)(n_out * K));
   w->wprep = c.take<char>(prep_bytes(K, cin, cout));
+  if (dtype != BFB_F32) w->acc = c.take<float>((size_t)std::max(n_out * cout, backward ? n_in * cin : 0));
   if (backward) {
     w->nbr_in = c.take<int32_t>((size_t)(n_in * K));
     w->wprep_t = c.take<char>(prep_bytes(K, cout, cin));
@@ -869,12 +912,20 @@ int build_tables(const int32_t* pairs, int64_t K, int64_t cap, const int32_t* nu
 }
 
 template <class T>
-int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n_dst, const T* w, int64_t N,
-                int transposed, const T* bias, void* wprep, T* out, cudaStream_t st) {
-  if (n_dst == 0) return BFB_OK;
-  const int dtype = std::is_same<T, float>::value ? BFB_F32 : std::is_same<T, __half>::value ? BFB_F16 : BFB_BF16;
+bool use_tc(int64_t Ck, int64_t N, int64_t K, const void* x, const void* out, const void* wprep) {
+  if constexpr (std::is_same<T, float>::value) {
+    return false;
+  } else {
+    const int dtype = std::is_same<T, __half>::value ? BFB_F16 : BFB_BF16;
+    return tc_ok(dtype, Ck, N, K) && aligned16(x) && aligned16(out) && aligned16(wprep);
+  }
+}
+
+// Tensor-core path over the neighbour table nbr [n_dst][K].
+template <class T>
+int launch_conv_tc(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n_dst, const T* w, int64_t N,
+                   int transposed, const T* bias, void* wprep, T* out, cudaStream_t st) {
   if constexpr (!std::is_same<T, float>::value) {
-  if (tc_ok(dtype, Ck, N, K) && aligned16(x) && aligned16(out) && aligned16(wprep)) {
     T* wp = static_cast<T*>(wprep);
     spc_prep_tc_kernel<T><<<grid_for(K * N * Ck, 256), 256, 0, st>>>(w, (int)K, (int)N, (int)Ck, transposed, wp);
     BFB_CHECK_LAUNCH();
@@ -893,17 +944,45 @@ int launch_conv(const T* x, int64_t Ck, const int32_t* nbr, int64_t K, int64_t n
         x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, cols, bias, out);
     BFB_CHECK_LAUNCH();
     return BFB_OK;
+  } else {
+    return BFB_ERR_UNSUPPORTED_DTYPE;
   }
-  }
+}
+
+// Rule-major FMA path straight over the rulebook: pair slot src_slot names
+// the source row (of x, n_src rows), the other slot the destination row.
+template <class T>
+int launch_conv_rules(const T* x, int64_t Ck, const int32_t* pairs, int64_t cap, const int32_t* num, int64_t K,
+                      int src_slot, int64_t n_src, int64_t n_dst, const T* w, int64_t N, int transposed,
+                      const T* bias, void* wprep, float* acc_ws, T* out, cudaStream_t st) {
   const int64_t Npad = ceil_div(N, 4) * 4;
   float* wp = static_cast<float*>(wprep);
   spc_prep_simt_kernel<T><<<grid_for(K * Ck * Npad, 256), 256, 0, st>>>(w, (int)K, (int)N, (int)Ck, (int)Npad,
                                                                         transposed, wp);
   BFB_CHECK_LAUNCH();
-  spc_conv_simt_kernel<T><<<(unsigned)ceil_div(n_dst * (Npad / 4), kSimtThreads), kSimtThreads, 0, st>>>(
-      x, (int)Ck, nbr, (int)K, n_dst, wp, (int)N, (int)Npad, bias, out,
-      std::is_same<T, float>::value && Ck % 4 == 0 && aligned16(x));
-  BFB_CHECK_LAUNCH();
+  constexpr bool f32 = std::is_same<T, float>::value;
+  float* acc = f32 ? reinterpret_cast<float*>(out) : acc_ws;
+  BFB_CUDA(cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)(n_dst * N), st));
+  if (cap > 0) {
+    const int np = Npad <= 64 ? 1 : Npad <= 128 ? 2 : 4;
+    const dim3 grid((unsigned)std::min<int64_t>(ceil_div(cap, 64), 148 * 4), (unsigned)ceil_div(Npad, np * 64));
+    for (int64_t k = 0; k < K; ++k) {
+      if (np == 1)
+        spc_rule_kernel<T, 1><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, pairs, cap, num, (int)k, src_slot, n_src,
+                                                             n_dst, wp, (int)N, (int)Npad, acc);
+      else if (np == 2)
+        spc_rule_kernel<T, 2><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, pairs, cap, num, (int)k, src_slot, n_src,
+                                                             n_dst, wp, (int)N, (int)Npad, acc);
+      else
+        spc_rule_kernel<T, 4><<<grid, kSimtThreads, 0, st>>>(x, (int)Ck, pairs, cap, num, (int)k, src_slot, n_src,
+                                                             n_dst, wp, (int)N, (int)Npad, acc);
+      BFB_CHECK_LAUNCH();
+    }
+  }
+  if (!f32 || bias) {
+    spc_finish_kernel<T><<<grid_for(n_dst * N, 256), 256, 0, st>>>(acc, n_dst, (int)N, bias, out);
+    BFB_CHECK_LAUNCH();
+  }
   return BFB_OK;
 }
 
@@ -919,9 +998,16 @@ template <class T>
 int conv_forward(const void* features, int64_t n_in, int64_t cin, const void* filters, int64_t K, int64_t cout,
                  const int32_t* pairs, int64_t cap, const int32_t* num, int64_t n_out, int inverse, const void* bias,
                  void* out, const ConvWork& w, cudaStream_t st) {
-  BFB_TRY(build_tables(pairs, K, cap, num, inverse ? 1 : 0, n_in, n_out, w.nbr_out, nullptr, st));
-  return launch_conv<T>(static_cast<const T*>(features), cin, w.nbr_out, K, n_out, static_cast<const T*>(filters),
-                        cout, 0, static_cast<const T*>(bias), w.wprep, static_cast<T*>(out), st);
+  if (n_out == 0) return BFB_OK;
+  const int in_slot = inverse ? 1 : 0;
+  const T* x = static_cast<const T*>(features);
+  if (use_tc<T>(cin, cout, K, features, out, w.wprep)) {
+    BFB_TRY(build_tables(pairs, K, cap, num, in_slot, n_in, n_out, w.nbr_out, nullptr, st));
+    return launch_conv_tc<T>(x, cin, w.nbr_out, K, n_out, static_cast<const T*>(filters), cout, 0,
+                             static_cast<const T*>(bias), w.wprep, static_cast<T*>(out), st);
+  }
+  return launch_conv_rules<T>(x, cin, pairs, cap, num, K, in_slot, n_in, n_out, static_cast<const T*>(filters), cout,
+                              0, static_cast<const T*>(bias), w.wprep, w.acc, static_cast<T*>(out), st);
 }
 
 template <class T>
@@ -929,11 +1015,20 @@ int conv_backward(const void* features, int64_t n_in, int64_t cin, const void* f
                   const void* out_bp, int64_t n_out, const int32_t* pairs, int64_t cap, const int32_t* num,
                   int inverse, void* input_grad, void* filters_grad, const ConvWork& w, cudaStream_t st) {
   const int in_slot = inverse ? 1 : 0;
-  BFB_TRY(build_tables(pairs, K, cap, num, in_slot, n_in, n_out, nullptr, w.nbr_in, st));
   // input gradient: destination = inputs, source = output gradients,
   // reduced channel = cout, filters transposed
-  BFB_TRY(launch_conv<T>(static_cast<const T*>(out_bp), cout, w.nbr_in, K, n_in, static_cast<const T*>(filters), cin,
-                         1, nullptr, w.wprep_t, static_cast<T*>(input_grad), st));
+  const T* g = static_cast<const T*>(out_bp);
+  if (n_in > 0) {
+    if (use_tc<T>(cout, cin, K, out_bp, input_grad, w.wprep_t)) {
+      BFB_TRY(build_tables(pairs, K, cap, num, in_slot, n_in, n_out, nullptr, w.nbr_in, st));
+      BFB_TRY(launch_conv_tc<T>(g, cout, w.nbr_in, K, n_in, static_cast<const T*>(filters), cin, 1, nullptr,
+                                w.wprep_t, static_cast<T*>(input_grad), st));
+    } else {
+      BFB_TRY(launch_conv_rules<T>(g, cout, pairs, cap, num, K, 1 - in_slot, n_out, n_in,
+                                   static_cast<const T*>(filters), cin, 1, nullptr, w.wprep_t, w.acc,
+                                   static_cast<T*>(input_grad), st));
+    }
+  }
   const int slots = dw_slots(K, cin, cout);
   spc_dw_plan_kernel<<<1, 32, 0, st>>>(num, (int)K, cap, slots, w.dwplan);
   BFB_CHECK_LAUNCH();

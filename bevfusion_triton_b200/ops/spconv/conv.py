@@ -115,9 +115,12 @@ class SparseConvolution(SparseModule):
                 input.indice_dict[self.indice_key] = (outids, indices, pairs, num, spatial_shape)
             # the fused (folded batch-norm) form of a submanifold layer adds no
             # bias, as the reference's fused_indice_conv
-            bias = None if (self.fused_bn and self.subm) else spops._like_features(self.bias, feats)
-            out = _native().indice_conv(feats, spops._like_features(self.weight, feats), pairs.to(feats.device),
-                                        num.to(feats.device), int(outids.shape[0]), bool(self.inverse), bias)
+            f, (w, b), back = spops._amp(feats, self.weight,
+                                         None if (self.fused_bn and self.subm) else self.bias)
+            out = _native().indice_conv(f, w, pairs.to(feats.device), num.to(feats.device), int(outids.shape[0]),
+                                        bool(self.inverse), b)
+            if back is not None:
+                out = out.to(back)
             res = SparseConvTensor(out, outids, out_shape, batch)
         res.indice_dict = input.indice_dict
         res.grid = input.grid

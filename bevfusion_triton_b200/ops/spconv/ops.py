@@ -92,14 +92,23 @@ def _require_cuda(*ts) -> None:
             raise RuntimeError('bevfusion_triton_b200 ops run on CUDA tensors only (no CPU fallback)')
 
 
-def _like_features(t, features):
-    """Under torch.autocast the reference's per-rule matmul accepts fp32
-    filters with fp16 / bf16 features; here the filters (and bias) are cast
-    to the features' dtype then (a differentiable cast, so fp32 parameters
-    still receive gradients).  Outside autocast the dtypes must match."""
-    if t is None or t.dtype == features.dtype or not torch.is_autocast_enabled(features.device.type):
-        return t
-    return t.to(features.dtype)
+def _amp(features, *ts):
+    """Operands as the convolution computes them.  Under torch.autocast the
+    reference's per-rule matmul runs in the autocast dtype (fp16 / bf16, on
+    the tensor cores) whatever the features' and filters' dtypes, and its
+    result lands in a buffer of the features' dtype; here the features and
+    the other operands are cast to the autocast dtype (a differentiable cast,
+    so fp32 parameters still receive gradients) and the result is returned
+    in the features' dtype.  Outside autocast the dtypes must match.
+    Returns (features, operands, dtype to return the result in, or None)."""
+    dev = features.device.type
+    if not torch.is_autocast_enabled(dev):
+        return features, ts, None
+    dt = torch.get_autocast_dtype(dev)
+    cast = (lambda t: None if t is None or t.dtype == dt else t.to(dt))  # noqa: E731
+    keep = (lambda t, c: t if c is None else c)  # noqa: E731
+    return keep(features, cast(features)), tuple(keep(t, cast(t)) for t in ts), (
+        None if features.dtype == dt else features.dtype)
 
 
 def indice_conv(features: torch.Tensor, filters: torch.Tensor, indice_pairs: torch.Tensor,
@@ -114,8 +123,9 @@ def indice_conv(features: torch.Tensor, filters: torch.Tensor, indice_pairs: tor
     filters."""
     del subm
     _require_cuda(features, filters, indice_pairs, indice_pair_num)
-    return ops().indice_conv(features, _like_features(filters, features), indice_pairs, indice_pair_num,
-                             int(num_activate_out), bool(inverse), None)
+    f, (w,), back = _amp(features, filters)
+    out = ops().indice_conv(f, w, indice_pairs, indice_pair_num, int(num_activate_out), bool(inverse), None)
+    return out if back is None else out.to(back)
 
 
 def fused_indice_conv(features, filters, bias, indice_pairs, indice_pair_num, num_activate_out, inverse, subm):
@@ -123,8 +133,9 @@ def fused_indice_conv(features, filters, bias, indice_pairs, indice_pair_num, nu
     reference (spconv_triton.py:1010-1032) a submanifold convolution adds no
     bias here."""
     _require_cuda(features, filters, indice_pairs, indice_pair_num)
-    return ops().indice_conv(features, _like_features(filters, features), indice_pairs, indice_pair_num,
-                             int(num_activate_out), bool(inverse), None if subm else _like_features(bias, features))
+    f, (w, b), back = _amp(features, filters, None if subm else bias)
+    out = ops().indice_conv(f, w, indice_pairs, indice_pair_num, int(num_activate_out), bool(inverse), b)
+    return out if back is None else out.to(back)
 
 
 def indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_num, inverse: bool = False,
@@ -134,10 +145,9 @@ def indice_conv_backward(features, filters, out_bp, indice_pairs, indice_pair_nu
     order, so it is deterministic."""
     del subm
     _require_cuda(features, filters, out_bp, indice_pairs, indice_pair_num)
-    gin, gw = ops().indice_conv_backward(features, _like_features(filters, features),
-                                         _like_features(out_bp, features), indice_pairs, indice_pair_num,
-                                         bool(inverse))
-    return gin, gw.view(filters.shape).to(filters.dtype)
+    f, (w, g), back = _amp(features, filters, out_bp)
+    gin, gw = ops().indice_conv_backward(f, w, g, indice_pairs, indice_pair_num, bool(inverse))
+    return (gin if back is None else gin.to(back)), gw.view(filters.shape).to(filters.dtype)
 
 
 def indice_maxpool(features, indice_pairs, indice_pair_num, num_activate_out):

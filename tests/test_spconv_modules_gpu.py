@@ -128,21 +128,25 @@ def test_maxpool_and_dense(ref):
 
 
 def test_autocast_fp16_features_fp32_filters(ref):
-    """Under autocast a layer takes fp16 features with its fp32 parameters
-    (the reference's matmul does); the fp32 parameters get gradients."""
+    """Under autocast a layer computes in fp16 whatever its inputs' dtypes
+    (the reference's matmul does) and returns the features' dtype; fp32
+    parameters get gradients.  Outside autocast mismatched dtypes are
+    refused, as a plain matmul refuses them."""
     idx = lidar_voxel_indices(1)
     net = S.SparseSequential(S.SubMConv3d(16, 32, 3, padding=1, indice_key='a'), nn.ReLU(),
                              S.SparseConv3d(32, 32, 3, stride=2, padding=1, indice_key='b')).cuda()
-    x = torch.randn(idx.size(0), 16, device='cuda', dtype=torch.float16)
+    x16 = torch.randn(idx.size(0), 16, device='cuda', dtype=torch.float16)
     with torch.autocast('cuda', dtype=torch.float16):
-        out = net(S.SparseConvTensor(x, idx, SPARSE_SHAPE, 1))
-    assert out.features.dtype == torch.float16
+        out = net(S.SparseConvTensor(x16, idx, SPARSE_SHAPE, 1))
+        out32 = net(S.SparseConvTensor(x16.float(), idx, SPARSE_SHAPE, 1))
+    assert out.features.dtype == torch.float16 and out32.features.dtype == torch.float32
+    # fp32 features under autocast: the same fp16 computation, returned in fp32
+    torch.testing.assert_close(out32.features, out.features.float(), rtol=1e-2, atol=1e-2)
     out.features.float().square().mean().backward()
     assert all(p.grad is not None and p.grad.dtype == torch.float32 and bool(torch.isfinite(p.grad).all())
                for p in net.parameters())
-    # outside autocast mismatched dtypes are refused, as a plain matmul is
     with pytest.raises(TypeError):
-        net(S.SparseConvTensor(x, idx, SPARSE_SHAPE, 1))
+        net(S.SparseConvTensor(x16, idx, SPARSE_SHAPE, 1))
 
 
 def _sites(ndim, shape, dense, seed):
