@@ -12,13 +12,15 @@
 //   :1085-1111 indice_maxpool_backward: input_grad[in_idx] += out_bp[out_idx]
 //              where features[in_idx] == out_features[out_idx]
 //
-// Design: output-stationary.  The rulebook (rule-major pairs) is turned into a
-// neighbour table nbr[row][k] (the input feeding output `row` through offset
-// k, or -1) by one scatter kernel.  Every output row is then produced by ONE
-// thread block as a sum over k in ascending order, written once: no atomics,
-// no zero-fill pass, deterministic.  The backward's input gradient is the
-// same operation on the inverse table (input -> output per offset) with the
-// filters transposed, so it runs through the same kernels.
+// Design.  The tensor-core path is output-stationary: the rulebook
+// (rule-major pairs) is turned into a neighbour table nbr[row][k] (the input
+// feeding output `row` through offset k, or -1) by one scatter kernel, and
+// every output row is produced by ONE thread block as a sum over k, written
+// once.  The FMA path (fp32 and other widths) is rule-major: the offsets run
+// in ascending order, each reusing its filter over 64 pairs at a time, and
+// add into the output rows.  Neither uses atomics; both are deterministic.
+// The backward's input gradient is the same operation with the pair slots
+// swapped and the filters transposed, so it runs through the same kernels.
 //
 //   spc_nbr_kernel         rulebook -> nbr_out[n_out][K] (+ nbr_in[n_in][K])
 //   spc_conv_tc_kernel     fp16 / bf16, channels multiples of 16: a tile of
